@@ -1,0 +1,375 @@
+"""CPU restatement of REAX's quantized MLP gate/up path.
+
+TEST INFRASTRUCTURE ONLY.  Nothing in the product imports this module: only
+``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+``bench.py`` use it, and only as the checker (or, for the CPU baseline, as the
+timed port of the reference's arithmetic).
+
+Every function restates one piece of the reference and cites the file:line it
+follows (paths relative to the reference project root).  Arithmetic is numpy
+float32 (IEEE-754 single, round-to-nearest-even, no fused multiply-add), int8
+GEMMs are computed exactly in float64 (every partial sum is an integer below
+2**53), and bfloat16 values travel as their uint16 bit patterns.
+
+Pinning:
+  * ``prepare_rows``/``prepare_groups``/``reduce_partials``/``fold`` are checked
+    against golden vectors produced by running the reference's own Triton
+    kernels (``reaxv2/quantize.py``, ``runtime/mixed_origin_bf16.py``) under
+    Triton's CPU interpreter (``tests/golden/gen_golden.py``).
+  * The SiLU formula is checked against the reference's all-65536-input domain
+    check idea (``model-addressed-bulk-activation-table-r1/wide_warp_hybrid.py:41-49``)
+    on the GPU, where the reference's own CUDA ``silu_f32`` runs.
+  * The INT8 GEMM + dequant + SwiGLU chain is checked on the GPU against the
+    reference's own kernel (``kernel-source/legacy-v2/src/native_hybrid8.cu``)
+    compiled from source for sm_100a (``oracle/build_ref.py``).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+
+# ----------------------------------------------------------------------------------------------- bfloat16 bit helpers
+
+
+def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
+    """bfloat16 bit patterns (uint16) -> float32 values (exact)."""
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(values: np.ndarray) -> np.ndarray:
+    """float32 -> bfloat16 bit patterns, round-to-nearest-even (``__float2bfloat16_rn``).
+
+    NaN inputs map to a quiet NaN with the input's sign and upper payload bits.
+    """
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    u = v.view(np.uint32).astype(np.uint64)
+    rounded = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(v)
+    if nan.any():
+        rounded[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return rounded
+
+
+def round_bf16(values: np.ndarray) -> np.ndarray:
+    """float32 -> nearest bfloat16 value, returned as float32."""
+    return bf16_to_f32(f32_to_bf16(values))
+
+
+# ------------------------------------------------------------------------------------ a1: per-token INT8 quantization
+
+
+def quant_scale(amax: np.ndarray) -> np.ndarray:
+    """``scale = max(absmax, 1e-12) / 127.`` (reaxv2/quantize.py:19), IEEE float32 division."""
+    return (np.maximum(np.asarray(amax, dtype=F32), F32(1.0e-12)) / F32(127.0)).astype(F32)
+
+
+def quant_codes(values: np.ndarray, scale: np.ndarray, clamp: bool = True) -> np.ndarray:
+    """``nearbyint(div_rn(value, scale))`` then clamp to [-127, 127] (reaxv2/quantize.py:20-21).
+
+    ``values`` is [M, C] float32, ``scale`` is [M] float32; division is IEEE round-to-nearest
+    and ``np.rint`` rounds half to even, as libdevice ``nearbyint`` does.
+    """
+    q = np.rint(np.asarray(values, dtype=F32) / np.asarray(scale, dtype=F32)[:, None])
+    if clamp:
+        q = np.clip(q, -127.0, 127.0)
+    return q.astype(np.int8)
+
+
+def prepare_rows(x_bits, low_columns, high_columns, smoothing, centers, center):
+    """Restates ``reaxv2.quantize._prepare`` (reaxv2/quantize.py:5-29), one row per program.
+
+    x_bits [M, K] uint16 (bf16), low_columns [KL] int, high_columns [KH] int,
+    smoothing/centers [KL] float32, center: bool.
+    Returns (low int8 [M, KL], high uint16 [M, KH], scales float32 [M]).
+    """
+    x_bits = np.asarray(x_bits, dtype=np.uint16)
+    M = x_bits.shape[0]
+    low_columns = np.asarray(low_columns, dtype=np.int64)
+    high_columns = np.asarray(high_columns, dtype=np.int64)
+    KL, KH = len(low_columns), len(high_columns)
+    if KL:
+        value = bf16_to_f32(x_bits[:, low_columns])                      # :12-13
+        if center:
+            value = value - np.asarray(centers, dtype=F32)[None, :]       # :14-16
+        value = value / np.asarray(smoothing, dtype=F32)[None, :]        # :17-18
+        scales = quant_scale(np.abs(value).max(axis=1))                  # :19
+        low = quant_codes(value, scales)                                  # :20-22
+    else:
+        scales = np.ones(M, dtype=F32)                                    # :24-25
+        low = np.zeros((M, 0), dtype=np.int8)
+    high = x_bits[:, high_columns] if KH else np.zeros((M, 0), dtype=np.uint16)   # :26-29
+    return low, np.ascontiguousarray(high), scales.astype(F32)
+
+
+# ---------------------------------------------------------------------------------- a2: grouped (sliced) quantization
+
+
+def prepare_groups(x_bits, low_columns, high_columns, centers, smoothing, G, HP, P):
+    """Restates ``reaxv2.quantize.prepare_kernel`` (reaxv2/quantize.py:31-52), grid (M, P).
+
+    low_columns [P*G] (``-1`` pads a group), high_columns [P*HP] (``-1`` pads), centers and
+    smoothing [P*G].  The centre is always subtracted, padded columns quantize as 0, and codes
+    are not clamped (:44-45).
+    Returns (low int8 [M, P*G], high uint16 [M, P*HP], scales float32 [P, M]).
+    """
+    x_bits = np.asarray(x_bits, dtype=np.uint16)
+    M = x_bits.shape[0]
+    src = np.asarray(low_columns, dtype=np.int64).reshape(P, G)
+    mean = np.asarray(centers, dtype=F32).reshape(P, G)
+    smooth = np.asarray(smoothing, dtype=F32).reshape(P, G)
+    low = np.zeros((M, P * G), dtype=np.int8)
+    scales = np.zeros((P, M), dtype=F32)
+    for part in range(P):
+        valid = src[part] >= 0
+        raw = bf16_to_f32(x_bits[:, np.maximum(src[part], 0)])            # :38-39
+        value = np.where(valid[None, :], (raw - mean[part][None, :]) / smooth[part][None, :], F32(0.0)).astype(F32)  # :40-42
+        scale = quant_scale(np.abs(value).max(axis=1))                    # :43
+        low[:, part * G:(part + 1) * G] = quant_codes(value, scale, clamp=False)   # :44-45
+        scales[part] = scale                                              # :46
+    if HP:
+        hsrc = np.asarray(high_columns, dtype=np.int64)
+        high = np.where(hsrc[None, :] >= 0, x_bits[:, np.maximum(hsrc, 0)], np.uint16(0)).astype(np.uint16)  # :47-52
+    else:
+        high = np.zeros((M, 0), dtype=np.uint16)
+    return low, high, scales
+
+
+def reduce_partials(partial_bits):
+    """Restates ``reaxv2.quantize.reduce_kernel`` (reaxv2/quantize.py:55-61): ordered fp32 sum of bf16 partials."""
+    parts = np.asarray(partial_bits, dtype=np.uint16)
+    value = bf16_to_f32(parts[0])
+    for p in range(1, parts.shape[0]):
+        value = (value + bf16_to_f32(parts[p])).astype(F32)
+    return f32_to_bf16(value)
+
+
+# ------------------------------------------------------------------------------------------------ integer GEMM + dequant
+
+
+def int_gemm(a: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """int32 ``acc[m, n] = sum_k a[m, k] * w[n, k]`` (the s8 x s8 -> s32 MMA of hybrid8_tiles.cuh:35-44).
+
+    Computed in float64, which is exact here: |acc| <= K * 127 * 128 < 2**53 for any K below 2**38.
+    """
+    if a.shape[1] == 0:
+        return np.zeros((a.shape[0], w.shape[0]), dtype=np.int32)
+    return (np.asarray(a, dtype=np.float64) @ np.asarray(w, dtype=np.float64).T).astype(np.int64).astype(np.int32)
+
+
+def dequant(acc: np.ndarray, sa: np.ndarray, sw: np.ndarray, bias: np.ndarray) -> np.ndarray:
+    """``__fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(acc), sa[row]), sw[col]), bias[col])``
+    (kernel-source/legacy-v2/src/native_hybrid8.cu:23-24): three separately rounded float32 ops."""
+    raw = np.asarray(acc, dtype=np.int32).astype(F32)
+    v = (raw * np.asarray(sa, dtype=F32)[:, None]).astype(F32)
+    v = (v * np.asarray(sw, dtype=F32)[None, :]).astype(F32)
+    return (v + np.asarray(bias, dtype=F32)[None, :]).astype(F32)
+
+
+def bf16_gemm_f32(a_bits: np.ndarray, w_bits: np.ndarray) -> np.ndarray:
+    """float32 ``sum_k a[m,k] * w[n,k]`` of bf16 operands: computed in float64 then rounded once.
+
+    The reference accumulates in float32 through ``mma.sync.m16n8k16`` in ascending k
+    (hybrid8_tiles.cuh:392-397); that hardware order is not restated, so BF16 results are compared
+    with a tolerance.
+    """
+    if a_bits.shape[1] == 0:
+        return np.zeros((a_bits.shape[0], w_bits.shape[0]), dtype=F32)
+    a = bf16_to_f32(a_bits).astype(np.float64)
+    w = bf16_to_f32(w_bits).astype(np.float64)
+    return (a @ w.T).astype(F32)
+
+
+# ------------------------------------------------------------------------------------------------------- SiLU / SwiGLU
+
+
+def silu_f32(g: np.ndarray) -> np.ndarray:
+    """``silu_f32(x) = __fdiv_rn(x, 1.0f + expf(-x))`` (hybrid8_tiles.cuh:675), every step in float32.
+
+    ``exp`` here is the correctly rounded float32 exponential (float64 ``exp`` rounded once), not
+    CUDA's ``expf``; the two can differ by a few float32 ulps, which can move a bfloat16 rounding
+    in rare cases.  GPU parity tests therefore also run the oracle with the GPU's own SiLU table.
+    """
+    g = np.asarray(g, dtype=F32)
+    with np.errstate(over="ignore"):
+        e = np.exp(-g.astype(np.float64)).astype(F32)          # overflows to +inf below about -88.7
+    t = (F32(1.0) + e).astype(F32)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        return (g / t).astype(F32)
+
+
+_SILU_TABLE = None
+
+
+def silu_table() -> np.ndarray:
+    """``bf16(silu_f32(x))`` for every bfloat16 bit pattern x (uint16[65536] -> uint16[65536]).
+
+    The reference builds the same table on the device (model-addressed-bulk-activation-table-r1/
+    addressed_gate_up.cu:115-127) and checks it against the direct formula over the whole domain
+    (model-addressed-bulk-activation-table-r1/wide_warp_hybrid.py:41-49).
+    """
+    global _SILU_TABLE
+    if _SILU_TABLE is None:
+        allbits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+        _SILU_TABLE = f32_to_bf16(silu_f32(bf16_to_f32(allbits)))
+    return _SILU_TABLE
+
+
+def swiglu_bits(g_bits: np.ndarray, u_bits: np.ndarray, table: np.ndarray | None = None) -> np.ndarray:
+    """``swiglu1``: s = bf16(silu_f32(g)); out = bf16(float(s) * float(u)) (hybrid8_tiles.cuh:676-679).
+
+    The same contract as the engine's ``silu_mul`` (vendor/s1eng/s1eng/fused.py:131-164).
+    ``table`` (uint16[65536]) replaces the SiLU step when given, e.g. a table read back from the GPU.
+    """
+    table = silu_table() if table is None else np.asarray(table, dtype=np.uint16)
+    s = bf16_to_f32(table[np.asarray(g_bits, dtype=np.uint16)])
+    return f32_to_bf16((s * bf16_to_f32(u_bits)).astype(F32))
+
+
+# ------------------------------------------------------------------------------------------- a4-a9: INT8 gate/up + SwiGLU
+
+
+def gate_up_values(a, w, ah_bits, wh_bits, sa, sw, bias):
+    """float32 [M, N2] gate|up values before bf16 rounding (native_hybrid8.cu:9-26).
+
+    INT8 part exact (dequant as :23-24).  The BF16 outlier part (:26, accumulated by mma.sync into
+    the dequantized registers) is restated as one float32 add of the float32-rounded dot product.
+    """
+    v = dequant(int_gemm(a, w), sa, sw, bias)
+    if ah_bits is not None and np.asarray(ah_bits).shape[1] > 0:
+        v = (v + bf16_gemm_f32(np.asarray(ah_bits), np.asarray(wh_bits))).astype(F32)
+    return v
+
+
+def gate_up_product(a, w, ah_bits, wh_bits, sa, sw, bias, table=None):
+    """Restates ``reaxv2.gate_up.Native.product`` (reaxv2/gate_up.py:11-27) and its kernel
+    ``hybrid_tile`` (native_hybrid8.cu:4-28) with ``store_tile_swiglu`` (hybrid8_tiles.cuh:681-713).
+
+    a int8 [M, KL]; w int8 [N2, KL] = [Wg; Wu] (gate rows first, hybrid8_tiles.cuh:93-94);
+    ah_bits uint16 [M, KH]; wh_bits uint16 [N2, KH]; sa [M]; sw, bias [N2].
+    Returns uint16 (bf16) [M, N2 // 2].
+    """
+    v = gate_up_values(a, w, ah_bits, wh_bits, sa, sw, bias)
+    H = v.shape[1] // 2
+    g = f32_to_bf16(v[:, :H])
+    u = f32_to_bf16(v[:, H:])
+    return swiglu_bits(g, u, table)
+
+
+def gate_up_project(x_bits, bank, table=None):
+    """Restates ``reaxv2.gate_up.Native.project`` (reaxv2/gate_up.py:29-37): quantize then product.
+
+    ``bank`` has the fields of the reference's bank namespace (earlier_gate_up_screen.py:30-33):
+    width, centered, low_columns, high_columns, low_weight, high_weight, smoothing, centers,
+    scales, bias (numpy arrays; high_weight as uint16 bf16 bits).
+    """
+    low, high, scales = prepare_rows(x_bits, bank.low_columns, bank.high_columns, bank.smoothing,
+                                     bank.centers, bank.centered)
+    return gate_up_product(low, bank.low_weight, high, bank.high_weight, scales, bank.scales, bank.bias, table)
+
+
+# ------------------------------------------------------------------------------------------ a11: grouped (sliced) INT8
+
+
+def sliced_partials(low, w, high_bits, wh_bits, scales, sw, bias, group, hp, parts):
+    """Restates ``sliced_tile`` (kernel-source/legacy-v2/src/sliced_linear8.cu:4-32): one bf16 partial per K group.
+
+    low int8 [M, P*G]; w int8 [N, P*G]; high_bits [M, P*HP]; wh_bits [N, P*HP]; scales [P, M];
+    sw, bias [P, N].  Returns uint16 [P, M, N].
+    """
+    M, N = low.shape[0], w.shape[0]
+    out = np.zeros((parts, M, N), dtype=np.uint16)
+    for z in range(parts):
+        k0, k1 = z * group, (z + 1) * group
+        v = dequant(int_gemm(low[:, k0:k1], w[:, k0:k1]), scales[z], sw[z], bias[z])      # :11-27
+        if hp > 0:
+            h0, h1 = z * hp, (z + 1) * hp
+            v = (v + bf16_gemm_f32(high_bits[:, h0:h1], wh_bits[:, h0:h1])).astype(F32)  # :28-30
+        out[z] = f32_to_bf16(v)                                                          # :31
+    return out
+
+
+def sliced_project(x_bits, bank):
+    """Restates ``reaxv2.sliced.Native.project`` (reaxv2/sliced.py:20-47): grouped quant, partials, ordered fold."""
+    low, high, scales = prepare_groups(x_bits, bank.low_columns, bank.high_columns, bank.centers, bank.smoothing,
+                                       bank.group, bank.hp, bank.parts)
+    partials = sliced_partials(low, bank.low_weight, high, bank.high_weight, scales, bank.scales, bank.bias,
+                               bank.group, bank.hp, bank.parts)
+    if bank.parts == 1:
+        return partials[0]
+    return reduce_partials(partials)
+
+
+# ------------------------------------------------------------------------------------------- a12: BF16 mixed-origin path
+
+
+def slice_bounds(K: int, parts: int, chunk: int):
+    """K ranges of the split plan: slice s covers [s*chunk, min(K, (s+1)*chunk)) (hybrid8_tiles.cuh:5-7 comment).
+
+    With ``parts == 1`` the single slice is the whole of K (runtime/mixed_origin_bf16.py:28).
+    """
+    if parts <= 1:
+        return [(0, K)]
+    return [(min(K, s * chunk), min(K, (s + 1) * chunk)) for s in range(parts)]
+
+
+def bf16_partials(x_bits, w_bits, split, left, right):
+    """Restates ``mixed_origin_bf16.Native.partials`` (runtime/mixed_origin_bf16.py:34-44).
+
+    Rows ``< split`` follow the ``left`` plan, the rest the ``right`` plan (each ``{parts, chunk}``).
+    Slice s of a row is bf16(float32 sum over the slice); slices past a row's plan, and empty slices,
+    are written as zeros (as the reference's slice kernel does for empty slices, n64_parts.cu:11-16).
+    Returns uint16 [max(P0, P1), M, N].
+    """
+    x_bits = np.asarray(x_bits, dtype=np.uint16)
+    w_bits = np.asarray(w_bits, dtype=np.uint16)
+    M, K = x_bits.shape
+    N = w_bits.shape[0]
+    P = max(left["parts"], right["parts"])
+    out = np.zeros((P, M, N), dtype=np.uint16)
+    for rows, plan in ((slice(0, min(split, M)), left), (slice(min(split, M), M), right)):
+        if rows.start >= rows.stop:
+            continue
+        for s, (k0, k1) in enumerate(slice_bounds(K, plan["parts"], plan["chunk"])):
+            if k1 > k0:
+                out[s, rows] = f32_to_bf16(bf16_gemm_f32(x_bits[rows, k0:k1], w_bits[:, k0:k1]))
+    return out
+
+
+def fold(parts_bits, split, P0, P1):
+    """Restates the ``fold`` kernel (runtime/mixed_origin_bf16.py:8-17): rows < split sum P0 partials,
+    the rest P1, in slice order, in float32; one bf16 rounding."""
+    parts = np.asarray(parts_bits, dtype=np.uint16)
+    M = parts.shape[1]
+    count = np.where(np.arange(M) < split, P0, P1)
+    value = bf16_to_f32(parts[0])
+    for p in range(1, max(P0, P1)):
+        active = (p < count)[:, None]
+        value = np.where(active, (value + bf16_to_f32(parts[p])).astype(F32), value).astype(F32)
+    return f32_to_bf16(value)
+
+
+def bf16_project(x_bits, w_bits, split, left, right):
+    """``mixed_origin_bf16.Native.project`` (runtime/mixed_origin_bf16.py:45-48): partials then fold -> [M, N2] bf16."""
+    parts = bf16_partials(x_bits, w_bits, split, left, right)
+    return fold(parts, split, left["parts"], right["parts"])
+
+
+def gate_up_bf16(x_bits, w_bits, split, left, right, table=None):
+    """BF16-weight gate/up + SwiGLU: the mixed-origin projection of [Wg; Wu] followed by ``silu_mul``
+    (vendor/s1eng/s1eng/fused.py:145-164).  Returns uint16 [M, N2 // 2]."""
+    gu = bf16_project(x_bits, w_bits, split, left, right)
+    H = gu.shape[1] // 2
+    return swiglu_bits(gu[:, :H], gu[:, H:], table)
+
+
+# --------------------------------------------------------------------------------------------------------- comparison
+
+
+def ulp_distance_bf16(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
+    """Distance in bfloat16 ulps between two arrays of finite bf16 bit patterns (signed-magnitude ordering)."""
+    def key(bits):
+        b = np.asarray(bits, dtype=np.uint16).astype(np.int32)
+        mag = b & 0x7FFF
+        return np.where(b & 0x8000, -mag, mag)
+    return np.abs(key(a_bits) - key(b_bits))

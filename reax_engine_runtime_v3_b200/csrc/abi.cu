@@ -1,0 +1,609 @@
+// C ABI of the B200 gate/up path (declarations and contracts: include/reax_b200.h).
+//
+// Host side of every entry point: argument validation (the preconditions the reference asserts in
+// reaxv2/gate_up.py:14 and reaxv2/sliced.py:26, plus the alignment the kernels need), TMA tensor-map
+// encoding, the tile / stream-K plan of the tcgen05 kernels, and the launches.  Nothing here
+// allocates device memory or synchronizes, so every entry point is usable inside graph capture.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <utility>
+
+#include <cudaTypedefs.h>
+
+#include "gate_up_tc.cuh"
+#include "reax_b200.h"
+#include "rowwise.cuh"
+
+namespace {
+
+constexpr int kVersion = 10000;           // 1.0.0
+constexpr int kEpiWarps = 4;
+constexpr int kStages = 4;
+constexpr int kMaxDevices = 64;
+constexpr size_t kStatusBytes = 256;
+constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;   // 2 s
+
+// Quantizer division for the plain '/' of reaxv2/quantize.py:18-19,42 (see rowwise.cuh).
+constexpr int kQuantDivision = reax::kDivFull;
+
+thread_local std::string g_last_error;
+unsigned long long g_timeout_ns = kDefaultTimeoutNs;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(REAX_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+struct DeviceInfo {
+    bool ready = false;
+    int sms = 0;
+    int major = 0, minor = 0;
+    bool smem_set = false;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mutex;
+
+template <int EPI>
+void* tc_kernel_ptr() {
+    return reinterpret_cast<void*>(&reax::tc_gemm_kernel<kEpiWarps, kStages, EPI>);
+}
+
+constexpr size_t tc_smem_bytes() { return static_cast<size_t>(kStages) * reax::kStageBytes + 1024 + 256; }
+
+// Current device, its SM count, and a check that it is sm_100; sets kernel attributes once.
+int current_device(int* dev_out, DeviceInfo** info_out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail(REAX_ERR_DEVICE, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    DeviceInfo& d = g_dev[dev];
+    if (!d.ready) {
+        if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+        if ((e = cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute(major)");
+        if ((e = cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+            return cuda_fail(e, "cudaDeviceGetAttribute(minor)");
+        d.ready = true;
+    }
+    if (d.major != 10 || d.minor != 0)
+        return fail(REAX_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a (B200)", dev, d.major,
+                    d.minor);
+    if (!d.smem_set) {
+        const int bytes = static_cast<int>(tc_smem_bytes());
+        if ((e = cudaFuncSetAttribute(tc_kernel_ptr<reax::kEpiSwiglu>(), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      bytes)) != cudaSuccess)
+            return cuda_fail(e, "cudaFuncSetAttribute(swiglu kernel smem)");
+        if ((e = cudaFuncSetAttribute(tc_kernel_ptr<reax::kEpiPlain>(), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      bytes)) != cudaSuccess)
+            return cuda_fail(e, "cudaFuncSetAttribute(plain kernel smem)");
+        d.smem_set = true;
+    }
+    *dev_out = dev;
+    *info_out = &d;
+    return REAX_OK;
+}
+
+// ------------------------------------------------------------------------------------------------ tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_status = cudaSuccess;
+
+int get_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+    std::call_once(g_encode_once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        g_encode_status = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q);
+        if (g_encode_status == cudaSuccess && q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (g_encode == nullptr) {
+        if (g_encode_status != cudaSuccess) return cuda_fail(g_encode_status, "cudaGetDriverEntryPointByVersion");
+        return fail(REAX_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+    }
+    *fn = g_encode;
+    return REAX_OK;
+}
+
+// 2-D map of a row-major [rows, inner] tensor, box = 128 bytes of the inner dimension x 128 rows,
+// 128-byte swizzle, zero fill out of bounds.
+int make_map(CUtensorMap* map, CUtensorMapDataType dt, size_t elem, const void* base, uint64_t inner, uint64_t rows,
+             uint64_t row_stride_elems) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int rc = get_encoder(&enc);
+    if (rc != REAX_OK) return rc;
+    cuuint64_t dims[2] = {inner, rows};
+    cuuint64_t strides[1] = {row_stride_elems * elem};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(reax::kRowBytes / elem), 128};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(REAX_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for a [%llu, %llu] tensor", static_cast<int>(r),
+                    static_cast<unsigned long long>(rows), static_cast<unsigned long long>(inner));
+    return REAX_OK;
+}
+
+// ------------------------------------------------------------------------------------------------- workspace
+struct Workspace {
+    unsigned* status;
+    int* counters;
+    int* partials;
+};
+
+size_t workspace_bytes_for(int sms) {
+    const size_t counters = ((static_cast<size_t>(2 * sms) * sizeof(int)) + 255) / 256 * 256;
+    return kStatusBytes + counters + static_cast<size_t>(sms) * 2 * reax::kSlotInts * sizeof(int);
+}
+
+int carve_workspace(void* ws, size_t bytes, int sms, Workspace* w) {
+    if (ws == nullptr) return fail(REAX_ERR_WORKSPACE, "workspace is NULL");
+    if (!aligned(ws, 256)) return fail(REAX_ERR_ALIGN, "workspace must be 256-byte aligned");
+    const size_t need = workspace_bytes_for(sms);
+    if (bytes < need) return fail(REAX_ERR_WORKSPACE, "workspace has %zu bytes, %zu needed", bytes, need);
+    uint8_t* b = static_cast<uint8_t*>(ws);
+    w->status = reinterpret_cast<unsigned*>(b);
+    w->counters = reinterpret_cast<int*>(b + kStatusBytes);
+    const size_t counters = ((static_cast<size_t>(2 * sms) * sizeof(int)) + 255) / 256 * 256;
+    w->partials = reinterpret_cast<int*>(b + kStatusBytes + counters);
+    return REAX_OK;
+}
+
+// ----------------------------------------------------------------------------------------------- tcgen05 plan
+// Tiles are dealt whole while at least one full wave remains beyond them; the rest (between one and
+// two waves of tiles, or every tile when there are fewer tiles than SMs) is split by K blocks.
+void plan_schedule(reax::TcParams& p, int sms, bool allow_split, int* grid) {
+    const int KB = p.kb_int + p.kb_f16;
+    const int T = p.tiles;
+    if (!allow_split || T % sms == 0 || KB < 2) {
+        p.dp_tiles = T;
+        p.sk_iters = 0;
+        *grid = T < sms ? T : sms;
+        return;
+    }
+    p.dp_tiles = T > sms ? (T / sms - 1) * sms : 0;
+    p.sk_iters = static_cast<long long>(T - p.dp_tiles) * KB;
+    long long g = sms;
+    if (p.dp_tiles == 0) {
+        // at least two K blocks per CTA
+        const long long cap = p.sk_iters / 2;
+        if (cap < g) g = cap < 1 ? 1 : cap;
+    }
+    *grid = static_cast<int>(g);
+}
+
+int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(64 + 32 * kEpiWarps, 1, 1);
+    cfg.dynamicSmemBytes = tc_smem_bytes();
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    if (epi == reax::kEpiSwiglu)
+        e = cudaLaunchKernelEx(&cfg, reax::tc_gemm_kernel<kEpiWarps, kStages, reax::kEpiSwiglu>, p);
+    else
+        e = cudaLaunchKernelEx(&cfg, reax::tc_gemm_kernel<kEpiWarps, kStages, reax::kEpiPlain>, p);
+    if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
+    return REAX_OK;
+}
+
+void init_params(reax::TcParams& p) {
+    std::memset(&p, 0, sizeof(p));
+    p.group_m = 16;
+    p.acc_bufs = 2;
+    p.timeout_ns = g_timeout_ns;
+    p.parts = 1;
+}
+
+// Plain launch (no attributes) whose error comes from the launch call itself, so no sticky error
+// state of unrelated work is read or reset.
+template <typename... KArgs, typename... Args>
+int launch_plain(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
+                 Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cfg.attrs = nullptr;
+    cfg.numAttrs = 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return REAX_OK;
+}
+
+int elementwise_grid(long long work, int sms) {
+    long long g = (work + 255) / 256;
+    const long long cap = static_cast<long long>(sms) * 16;
+    if (g > cap) g = cap;
+    if (g < 1) g = 1;
+    return static_cast<int>(g);
+}
+
+}  // namespace
+
+extern "C" {
+
+int reax_version(void) { return kVersion; }
+
+const char* reax_last_error(void) { return g_last_error.c_str(); }
+
+void reax_set_wait_timeout_ns(unsigned long long ns) { g_timeout_ns = ns == 0 ? kDefaultTimeoutNs : ns; }
+
+size_t reax_workspace_bytes(int device) {
+    int dev = device;
+    if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) return 0;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    return workspace_bytes_for(sms);
+}
+
+int reax_quant_rows(const void* x, const int32_t* low_columns, const int32_t* high_columns, const float* smoothing,
+                    const float* centers, int8_t* low, void* high, float* scales, int M, int K, int KL, int KH,
+                    int center, void* stream) {
+    if (M < 0 || K < 0 || KL < 0 || KH < 0 || KL + KH > K)
+        return fail(REAX_ERR_INVALID, "quant_rows: bad sizes M=%d K=%d KL=%d KH=%d", M, K, KL, KH);
+    if (M == 0) return REAX_OK;
+    if (!x || !scales || (KL && (!low_columns || !smoothing || !low || (center && !centers))) ||
+        (KH && (!high_columns || !high)))
+        return fail(REAX_ERR_INVALID, "quant_rows: NULL pointer argument");
+    if (!aligned(low_columns, 16) || !aligned(smoothing, 16) || (center && !aligned(centers, 16)))
+        return fail(REAX_ERR_ALIGN, "quant_rows: low_columns, smoothing and centers must be 16-byte aligned");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    const int aligned_x = (aligned(x, 16) && K % 8 == 0) ? 1 : 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return launch_plain("quant_rows launch", reax::quant_rows_kernel<kQuantDivision>, dim3(M), dim3(256), s,
+                        static_cast<const __nv_bfloat16*>(x), static_cast<const int*>(low_columns),
+                        static_cast<const int*>(high_columns), smoothing, centers, low,
+                        static_cast<__nv_bfloat16*>(high), scales, K, KL, KH, center ? 1 : 0, aligned_x);
+}
+
+int reax_quant_groups(const void* x, const int32_t* low_columns, const int32_t* high_columns, const float* centers,
+                      const float* smoothing, int8_t* low, void* high, float* scales, int M, int K, int G, int HP,
+                      int P, void* stream) {
+    if (M < 0 || K <= 0 || G < 0 || HP < 0 || P < 1)
+        return fail(REAX_ERR_INVALID, "quant_groups: bad sizes M=%d K=%d G=%d HP=%d P=%d", M, K, G, HP, P);
+    if (M == 0) return REAX_OK;
+    if (!x || !scales || !low_columns || !centers || !smoothing || (G && !low) || (HP && (!high_columns || !high)))
+        return fail(REAX_ERR_INVALID, "quant_groups: NULL pointer argument");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    return launch_plain("quant_groups launch", reax::quant_groups_kernel<kQuantDivision>, dim3(M, P), dim3(256),
+                        static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
+                        static_cast<const int*>(low_columns), static_cast<const int*>(high_columns), centers,
+                        smoothing, low, static_cast<__nv_bfloat16*>(high), scales, M, K, G, HP, P);
+}
+
+int reax_reduce_partials(const void* partials, void* out, long long total, int P, void* stream) {
+    if (total < 0 || P < 1) return fail(REAX_ERR_INVALID, "reduce_partials: bad sizes total=%lld P=%d", total, P);
+    if (total == 0) return REAX_OK;
+    if (!partials || !out) return fail(REAX_ERR_INVALID, "reduce_partials: NULL pointer argument");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    const int vec = (aligned(partials, 16) && aligned(out, 16) && total % 8 == 0) ? 1 : 0;
+    return launch_plain("reduce_partials launch", reax::fold_partials_kernel,
+                        dim3(elementwise_grid((total + 7) / 8, info->sms)), dim3(256), static_cast<cudaStream_t>(stream),
+                        static_cast<const __nv_bfloat16*>(partials), static_cast<const int*>(nullptr),
+                        static_cast<__nv_bfloat16*>(out), total, 1, P, P, vec);
+}
+
+int reax_fold_partials(const void* parts, const int32_t* split, void* out, int M, int N, int P0, int P1,
+                       void* stream) {
+    if (M < 0 || N <= 0 || P0 < 1 || P1 < 1)
+        return fail(REAX_ERR_INVALID, "fold_partials: bad sizes M=%d N=%d P0=%d P1=%d", M, N, P0, P1);
+    if (M == 0) return REAX_OK;
+    if (!parts || !split || !out) return fail(REAX_ERR_INVALID, "fold_partials: NULL pointer argument");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    const long long total = static_cast<long long>(M) * N;
+    return launch_plain("fold_partials launch", reax::fold_partials_kernel,
+                        dim3(elementwise_grid((total + 7) / 8, info->sms)), dim3(256), static_cast<cudaStream_t>(stream),
+                        static_cast<const __nv_bfloat16*>(parts), static_cast<const int*>(split),
+                        static_cast<__nv_bfloat16*>(out), total, N, P0, P1,
+                        (aligned(parts, 16) && aligned(out, 16) && N % 8 == 0) ? 1 : 0);
+}
+
+int reax_silu_mul(const void* g, const void* u, void* out, int rows, int cols, long long g_stride, long long u_stride,
+                  void* stream) {
+    if (rows < 0 || cols < 0 || g_stride < cols || u_stride < cols)
+        return fail(REAX_ERR_INVALID, "silu_mul: bad sizes rows=%d cols=%d", rows, cols);
+    if (rows == 0 || cols == 0) return REAX_OK;
+    if (!g || !u || !out) return fail(REAX_ERR_INVALID, "silu_mul: NULL pointer argument");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    return launch_plain("silu_mul launch", reax::silu_mul_kernel,
+                        dim3(elementwise_grid(static_cast<long long>(rows) * cols, info->sms)), dim3(256),
+                        static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(g),
+                        static_cast<const __nv_bfloat16*>(u), static_cast<__nv_bfloat16*>(out), rows, cols, g_stride,
+                        u_stride);
+}
+
+int reax_silu_table(void* table, void* stream) {
+    if (!table) return fail(REAX_ERR_INVALID, "silu_table: NULL table");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    return launch_plain("silu_table launch", reax::silu_table_kernel, dim3(256), dim3(256),
+                        static_cast<cudaStream_t>(stream), static_cast<__nv_bfloat16*>(table));
+}
+
+int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa, const float* sw,
+                    const float* bias, void* out, int M, int N2, int KL, int KH, int ldo, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+    if (M < 0 || N2 <= 0 || KL < 0 || KH < 0 || KL + KH == 0)
+        return fail(REAX_ERR_INVALID, "gate_up_i8: bad sizes M=%d N2=%d KL=%d KH=%d", M, N2, KL, KH);
+    if (KL % 128 != 0 || KH % 64 != 0 || N2 % 256 != 0)
+        return fail(REAX_ERR_INVALID, "gate_up_i8: needs KL %% 128 == 0, KH %% 64 == 0, N2 %% 256 == 0 (KL=%d KH=%d N2=%d)",
+                    KL, KH, N2);
+    if (ldo < N2 / 2 || ldo % 8 != 0) return fail(REAX_ERR_INVALID, "gate_up_i8: ldo=%d (needs >= N2/2, %% 8 == 0)", ldo);
+    if (KL == 0) return fail(REAX_ERR_INVALID, "gate_up_i8: KL must be > 0 (the INT8 part of the bank is empty)");
+    if (M == 0) return REAX_OK;
+    if (!out || !sw || !bias || (KL && (!A || !W || !sa)) || (KH && (!AH || !WH)))
+        return fail(REAX_ERR_INVALID, "gate_up_i8: NULL pointer argument");
+    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(AH, 16) || !aligned(WH, 16) || !aligned(sw, 16) ||
+        !aligned(bias, 16) || !aligned(out, 16))
+        return fail(REAX_ERR_ALIGN, "gate_up_i8: operands, sw, bias and out must be 16-byte aligned");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    Workspace ws;
+    if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
+
+    reax::TcParams p;
+    init_params(p);
+    if (KL) {
+        if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL)) != REAX_OK) return rc;
+    }
+    if (KH) {
+        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH)) != REAX_OK) return rc;
+    }
+    if (!KL) {
+        p.tm_a = p.tm_ah;
+        p.tm_b = p.tm_bh;
+    }
+    if (!KH) {
+        p.tm_ah = p.tm_a;
+        p.tm_bh = p.tm_b;
+    }
+    p.sa = sa;
+    p.sw = sw;
+    p.bias = bias;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.M = M;
+    p.H = N2 / 2;
+    p.ldo = ldo;
+    p.kb_int = KL / 128;
+    p.kb_f16 = KH / 64;
+    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
+    p.n_tiles = (N2 / 2) / (reax::kBN / 2);
+    p.tiles = p.m_tiles * p.n_tiles;
+    p.mode = 0;
+    p.acc_bufs = KH ? 1 : 2;
+    p.ws_partials = ws.partials;
+    p.ws_counters = ws.counters;
+    p.status = ws.status;
+    p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
+    int grid = 0;
+    plan_schedule(p, info->sms, KH == 0, &grid);
+    return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
+}
+
+int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, int K, int ldo, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+    if (M < 0 || N2 <= 0 || K <= 0) return fail(REAX_ERR_INVALID, "gate_up_bf16: bad sizes M=%d N2=%d K=%d", M, N2, K);
+    if (K % 64 != 0 || N2 % 256 != 0)
+        return fail(REAX_ERR_INVALID, "gate_up_bf16: needs K %% 64 == 0 and N2 %% 256 == 0 (K=%d N2=%d)", K, N2);
+    if (ldo < N2 / 2 || ldo % 8 != 0) return fail(REAX_ERR_INVALID, "gate_up_bf16: ldo=%d (needs >= N2/2, %% 8 == 0)", ldo);
+    if (M == 0) return REAX_OK;
+    if (!x || !w || !out) return fail(REAX_ERR_INVALID, "gate_up_bf16: NULL pointer argument");
+    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16))
+        return fail(REAX_ERR_ALIGN, "gate_up_bf16: x, w and out must be 16-byte aligned");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    Workspace ws;
+    if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
+    reax::TcParams p;
+    init_params(p);
+    if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K)) != REAX_OK) return rc;
+    if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K)) != REAX_OK) return rc;
+    p.tm_a = p.tm_ah;
+    p.tm_b = p.tm_bh;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.M = M;
+    p.H = N2 / 2;
+    p.ldo = ldo;
+    p.kb_int = 0;
+    p.kb_f16 = K / 64;
+    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
+    p.n_tiles = (N2 / 2) / (reax::kBN / 2);
+    p.tiles = p.m_tiles * p.n_tiles;
+    p.mode = 1;
+    p.acc_bufs = 2;
+    p.ws_partials = ws.partials;
+    p.ws_counters = ws.counters;
+    p.status = ws.status;
+    p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
+    int grid = 0;
+    // float32 partial sums of one tile would round differently from one unsplit accumulation, which
+    // would make a row's result depend on the batch it came in: BF16 tiles are never split.
+    plan_schedule(p, info->sms, false, &grid);
+    return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
+}
+
+int reax_bf16_partials(const void* x, const void* w, const int32_t* split, void* parts, int M, int N, int K, int chunk0,
+                       int chunk1, int P0, int P1, void* workspace, size_t workspace_bytes, void* stream) {
+    if (M < 0 || N <= 0 || K <= 0 || P0 < 1 || P1 < 1)
+        return fail(REAX_ERR_INVALID, "bf16_partials: bad sizes M=%d N=%d K=%d P0=%d P1=%d", M, N, K, P0, P1);
+    if (K % 64 != 0 || N % 256 != 0 || (P0 > 1 && (chunk0 <= 0 || chunk0 % 64 != 0)) ||
+        (P1 > 1 && (chunk1 <= 0 || chunk1 % 64 != 0)))
+        return fail(REAX_ERR_INVALID, "bf16_partials: needs K %% 64 == 0, N %% 256 == 0, chunks multiples of 64");
+    if (M == 0) return REAX_OK;
+    if (!x || !w || !split || !parts) return fail(REAX_ERR_INVALID, "bf16_partials: NULL pointer argument");
+    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(parts, 16))
+        return fail(REAX_ERR_ALIGN, "bf16_partials: x, w and parts must be 16-byte aligned");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    Workspace ws;
+    if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int KB = K / 64;
+    const int ck0 = P0 > 1 ? chunk0 / 64 : KB;
+    const int ck1 = P1 > 1 ? chunk1 / 64 : KB;
+    const size_t plane = static_cast<size_t>(M) * N * 2;
+    // slices whose K range is empty for a plan are zero planes (the kernel skips them)
+    for (int sidx = 0; sidx < (P0 > P1 ? P0 : P1); ++sidx) {
+        const bool empty0 = sidx < P0 && sidx * ck0 >= KB;
+        const bool empty1 = sidx < P1 && sidx * ck1 >= KB;
+        if (empty0 || empty1) {
+            cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(parts) + sidx * plane, 0, plane, s);
+            if (e != cudaSuccess) return cuda_fail(e, "bf16_partials zero fill");
+        }
+    }
+    reax::TcParams p;
+    init_params(p);
+    if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K)) != REAX_OK) return rc;
+    if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N, K)) != REAX_OK) return rc;
+    p.tm_a = p.tm_ah;
+    p.tm_b = p.tm_bh;
+    p.out = static_cast<__nv_bfloat16*>(parts);
+    p.out_part_stride = static_cast<long long>(M) * N;
+    p.M = M;
+    p.ldo = N;
+    p.kb_int = 0;
+    p.kb_f16 = KB;
+    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
+    p.n_tiles = N / reax::kBN;
+    p.parts = P0 + P1;
+    p.tiles = p.parts * p.m_tiles * p.n_tiles;
+    p.mode = 1;
+    p.acc_bufs = 2;
+    p.slice_mode = 1;
+    p.plan_parts0 = P0;
+    p.plan_chunk_kb0 = ck0;
+    p.plan_chunk_kb1 = ck1;
+    p.split = split;
+    p.ws_partials = ws.partials;
+    p.ws_counters = ws.counters;
+    p.status = ws.status;
+    int grid = 0;
+    plan_schedule(p, info->sms, false, &grid);
+    return launch_tc(reax::kEpiPlain, p, grid, s);
+}
+
+int reax_sliced_i8(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa, const float* sw,
+                   const float* bias, void* partials, int M, int N, int G, int HP, int P, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+    if (M < 0 || N <= 0 || G <= 0 || HP < 0 || P < 1)
+        return fail(REAX_ERR_INVALID, "sliced_i8: bad sizes M=%d N=%d G=%d HP=%d P=%d", M, N, G, HP, P);
+    if (G % 128 != 0 || HP % 64 != 0 || N % 256 != 0)
+        return fail(REAX_ERR_INVALID, "sliced_i8: needs G %% 128 == 0, HP %% 64 == 0, N %% 256 == 0 (G=%d HP=%d N=%d)", G,
+                    HP, N);
+    if (M == 0) return REAX_OK;
+    if (!A || !W || !sa || !sw || !bias || !partials || (HP && (!AH || !WH)))
+        return fail(REAX_ERR_INVALID, "sliced_i8: NULL pointer argument");
+    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(AH, 16) || !aligned(WH, 16) || !aligned(sw, 16) ||
+        !aligned(bias, 16) || !aligned(partials, 16))
+        return fail(REAX_ERR_ALIGN, "sliced_i8: operands, sw, bias and partials must be 16-byte aligned");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    Workspace ws;
+    if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
+    reax::TcParams p;
+    init_params(p);
+    if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, static_cast<uint64_t>(P) * G, M,
+                       static_cast<uint64_t>(P) * G)) != REAX_OK)
+        return rc;
+    if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, static_cast<uint64_t>(P) * G, N,
+                       static_cast<uint64_t>(P) * G)) != REAX_OK)
+        return rc;
+    if (HP) {
+        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, static_cast<uint64_t>(P) * HP, M,
+                           static_cast<uint64_t>(P) * HP)) != REAX_OK)
+            return rc;
+        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, static_cast<uint64_t>(P) * HP, N,
+                           static_cast<uint64_t>(P) * HP)) != REAX_OK)
+            return rc;
+    } else {
+        p.tm_ah = p.tm_a;
+        p.tm_bh = p.tm_b;
+    }
+    p.sa = sa;
+    p.sw = sw;
+    p.bias = bias;
+    p.out = static_cast<__nv_bfloat16*>(partials);
+    p.out_part_stride = static_cast<long long>(M) * N;
+    p.M = M;
+    p.ldo = N;
+    p.kb_int = G / 128;
+    p.kb_f16 = HP / 64;
+    p.kb_int_part = G / 128;
+    p.kb_f16_part = HP / 64;
+    p.sa_part_stride = M;
+    p.n_part_stride = N;
+    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
+    p.n_tiles = N / reax::kBN;
+    p.parts = P;
+    p.tiles = P * p.m_tiles * p.n_tiles;
+    p.mode = 0;
+    p.acc_bufs = HP ? 1 : 2;
+    p.ws_partials = ws.partials;
+    p.ws_counters = ws.counters;
+    p.status = ws.status;
+    int grid = 0;
+    plan_schedule(p, info->sms, false, &grid);
+    return launch_tc(reax::kEpiPlain, p, grid, static_cast<cudaStream_t>(stream));
+}
+
+int reax_selftest_wait(void* workspace, unsigned long long timeout_ns, void* stream) {
+    if (!workspace || !aligned(workspace, 256)) return fail(REAX_ERR_WORKSPACE, "selftest_wait: bad workspace");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    return launch_plain("selftest_wait launch", reax::selftest_wait_kernel, dim3(1), dim3(32),
+                        static_cast<cudaStream_t>(stream), static_cast<unsigned*>(workspace), timeout_ns);
+}
+
+}  // extern "C"

@@ -1,0 +1,579 @@
+// tcgen05 GEMM kernels of the gate/up path (sm_100a).
+//
+// One warp-specialised persistent kernel computes C = A[M, K] x B[N, K]^T tile by tile with the
+// 5th-generation tensor cores and hands each accumulator tile to an epilogue:
+//   warp 0        TMA producer: 128x128-byte boxes of A and B into a STAGES-deep smem ring (128B swizzle)
+//   warp 1        TMEM allocator + MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=32 bytes)
+//   warps 2..     epilogue: tcgen05.ld of its 32 TMEM lanes, dequant / SwiGLU / bf16 store
+//
+// Tile = 128 rows of A (tokens) x 256 rows of B.  For the gate/up SwiGLU epilogue the 256 B rows
+// are 128 gate rows W[n0 .. n0+127] followed by the matching up rows W[H+n0 ..] (the interleave of
+// the reference's loader, hybrid8_tiles.cuh:93-94), so TMEM columns j and 128+j of one lane hold
+// the gate and up accumulators of the same output element and the SwiGLU needs no data exchange.
+//
+// Work distribution ("stream-K hybrid"): the tile list (grouped GROUP_M x n_tiles order, for L2
+// reuse) is cut into data-parallel tiles, dealt round-robin to the CTAs, and a remainder (< 2 waves)
+// whose K-blocks are split evenly between all CTAs.  A CTA that computes only part of a tile writes
+// its int32 partial to its own workspace slot and adds its K-block count to the tile's counter; the
+// CTA that completes the count sums every partial (integer addition: exact, order-free) with its own
+// TMEM accumulator and runs the epilogue, then clears the counter.  No CTA ever waits for another.
+//
+// Every mbarrier wait is bounded (timeout_ns of global time); on expiry the kernel ORs a bit into
+// the caller's status word, raises a shared abort flag so the other roles stop, drains its own
+// in-flight TMA copies and MMAs (again bounded), frees its TMEM and returns.
+#pragma once
+
+#include "common.cuh"
+
+namespace reax {
+
+constexpr int kBM = 128;                        // A rows per tile (MMA M)
+constexpr int kBN = 256;                        // B rows per tile (MMA N)
+constexpr int kRowBytes = 128;                  // K bytes per stage row: one 128-byte swizzle row
+constexpr int kAStage = kBM * kRowBytes;        // 16 KiB
+constexpr int kBStage = kBN * kRowBytes;        // 32 KiB
+constexpr int kStageBytes = kAStage + kBStage;  // 48 KiB
+constexpr int kTmemCols = 512;
+constexpr int kSlotInts = kBM * kBN;            // one split-tile partial: 128 x 256 int32 (128 KiB)
+
+enum EpilogueKind : int { kEpiSwiglu = 0, kEpiPlain = 1 };
+
+struct TcParams {
+    CUtensorMap tm_a;    // INT8 A [M, KL] (K blocks [0, kb_int))
+    CUtensorMap tm_b;    // INT8 B [rows, KL]
+    CUtensorMap tm_ah;   // BF16 A [M, KH or K] (K blocks [kb_int, kb_int + kb_f16))
+    CUtensorMap tm_bh;   // BF16 B [rows, KH or K]
+    const float* sa;     // per-row scale of A (INT8 path), indexed part * sa_part_stride + row
+    const float* sw;     // per-column scale of B (INT8 path), indexed part * n_part_stride + column
+    const float* bias;   // per-column bias (INT8 path)
+    __nv_bfloat16* out;  // bf16 output: SwiGLU [M, ldo] or plain [parts][M, ldo]
+    long long out_part_stride;  // elements between output parts (plain epilogue)
+    int M;               // valid A rows
+    int H;               // SwiGLU: row offset of the up half inside B; plain: unused
+    int ldo;             // output row stride (elements)
+    int kb_int;          // K blocks through kind::i8 (128 int8 each)
+    int kb_f16;          // K blocks through kind::f16 (64 bf16 each)
+    int kb_int_part;     // K-block offset between consecutive parts (INT8 part of a grouped projection)
+    int kb_f16_part;     // same for the BF16 columns
+    int sa_part_stride;  // = M for grouped projections, 0 otherwise
+    int n_part_stride;   // = N for grouped projections, 0 otherwise
+    int m_tiles, n_tiles, parts, group_m;
+    int tiles;           // parts * m_tiles * n_tiles
+    int dp_tiles;        // tiles dealt whole; tiles [dp_tiles, tiles) are split by K blocks
+    long long sk_iters;  // (tiles - dp_tiles) * (kb_int + kb_f16)
+    int acc_bufs;        // 2 = double-buffered accumulators; 1 = INT8 region + float32 region of one tile
+    int mode;            // 0 = INT8 dequant (+ BF16 columns added), 1 = BF16 only (float32 accumulators)
+    int* ws_partials;    // [gridDim.x][2][kSlotInts] int32
+    int* ws_counters;    // [2 * gridDim.x] int32, zero between launches
+    unsigned* status;    // OR-ed error bits (kStatus*)
+    unsigned long long timeout_ns;
+    int evict_first_b;   // stream B with an evict-first L2 policy (weights read once)
+    // Mixed-origin slicing (BF16 partials): parts = P0 + P1 and part z < P0 is slice z of plan 0 (rows
+    // < *split), part z >= P0 is slice z - P0 of plan 1 (rows >= *split).  Slice s of a plan covers K
+    // blocks [s * chunk_kb, (s + 1) * chunk_kb) clipped to the K extent; its output part is s.
+    int slice_mode;
+    int plan_parts0;
+    int plan_chunk_kb0, plan_chunk_kb1;
+    const int* split;
+};
+
+struct Segment {
+    int tile;    // linear tile index (grouped order)
+    int k0;      // first K block
+    int k1;      // one past the last K block
+    bool whole;  // this CTA computes every K block of the tile
+};
+
+struct Cursor {
+    int dp_i;
+    long long sk;
+    long long sk_end;
+};
+
+REAX_DEVI long long sk_begin(const TcParams& p, int c) { return p.sk_iters * c / gridDim.x; }
+
+REAX_DEVI Cursor cursor_init(const TcParams& p) {
+    Cursor c;
+    c.dp_i = 0;
+    c.sk = sk_begin(p, blockIdx.x);
+    c.sk_end = sk_begin(p, blockIdx.x + 1);
+    return c;
+}
+
+// linear tile -> (part, m tile, n tile); inside a part, groups of group_m m-tiles sweep all n-tiles
+REAX_DEVI void tile_coords(const TcParams& p, int t, int& part, int& mt, int& nt) {
+    const int per_part = p.m_tiles * p.n_tiles;
+    part = t / per_part;
+    const int r0 = t % per_part;
+    const int per_group = p.group_m * p.n_tiles;
+    const int g = r0 / per_group, r = r0 % per_group;
+    const int first_m = g * p.group_m;
+    const int gm = min(p.group_m, p.m_tiles - first_m);
+    mt = first_m + r % gm;
+    nt = r / gm;
+}
+
+// Row range and output part of a tile's plan (slice mode); the whole of [0, M) and `part` otherwise.
+REAX_DEVI void tile_plan(const TcParams& p, int part, int split, int& row_lo, int& row_hi, int& out_part) {
+    if (!p.slice_mode) {
+        row_lo = 0;
+        row_hi = p.M;
+        out_part = part;
+        return;
+    }
+    const bool second = part >= p.plan_parts0;
+    row_lo = second ? split : 0;
+    row_hi = second ? p.M : split;
+    out_part = second ? part - p.plan_parts0 : part;
+}
+
+// K-block range of a data-parallel tile; false when the tile has nothing to compute (slice mode:
+// an empty slice, or a tile without rows of its plan).
+REAX_DEVI bool tile_active(const TcParams& p, int t, int split, int& k0, int& k1) {
+    const int KB = p.kb_int + p.kb_f16;
+    if (!p.slice_mode) {
+        k0 = 0;
+        k1 = KB;
+        return true;
+    }
+    int part, mt, nt;
+    tile_coords(p, t, part, mt, nt);
+    int row_lo, row_hi, s;
+    tile_plan(p, part, split, row_lo, row_hi, s);
+    const int chunk = part >= p.plan_parts0 ? p.plan_chunk_kb1 : p.plan_chunk_kb0;
+    k0 = min(KB, s * chunk);
+    k1 = min(KB, (s + 1) * chunk);
+    if (k1 <= k0) return false;
+    const int r0 = mt * kBM, r1 = min(p.M, r0 + kBM);
+    return max(r0, row_lo) < min(r1, row_hi);
+}
+
+REAX_DEVI bool cursor_next(const TcParams& p, int split, Cursor& c, Segment& s) {
+    const int KB = p.kb_int + p.kb_f16;
+    while (true) {
+        const int t = blockIdx.x + c.dp_i * gridDim.x;
+        if (t >= p.dp_tiles) break;
+        ++c.dp_i;
+        if (tile_active(p, t, split, s.k0, s.k1)) {
+            s.tile = t;
+            s.whole = true;
+            return true;
+        }
+    }
+    if (c.sk < c.sk_end) {
+        const long long it = c.sk;
+        const int st = static_cast<int>(it / KB);
+        const int k0 = static_cast<int>(it % KB);
+        const long long left = c.sk_end - it;
+        const int k1 = static_cast<int>(left < KB - k0 ? k0 + left : KB);
+        s.tile = p.dp_tiles + st;
+        s.k0 = k0;
+        s.k1 = k1;
+        s.whole = (k0 == 0 && k1 == KB);
+        c.sk += k1 - k0;
+        return true;
+    }
+    return false;
+}
+
+// CTA whose stream-K range holds iteration i (ranges are floor(c * S / G) .. floor((c+1) * S / G)).
+REAX_DEVI int sk_owner(const TcParams& p, long long i) {
+    return static_cast<int>(((i + 1) * gridDim.x - 1) / p.sk_iters);
+}
+
+REAX_DEVI int sk_slot(const TcParams& p, int c, int st) {
+    const int KB = p.kb_int + p.kb_f16;
+    return static_cast<int>(sk_begin(p, c) / KB) == st ? 0 : 1;
+}
+
+REAX_DEVI void raise_error(const TcParams& p, int* abort_flag, unsigned bit) {
+    atomicOr(p.status, bit);
+    *reinterpret_cast<volatile int*>(abort_flag) = 1;
+}
+
+// ------------------------------------------------------------------------------------------------ epilogue math
+
+// INT8 dequant of one accumulator element (native_hybrid8.cu:23-24): three separately rounded ops.
+REAX_DEVI float dequant1(uint32_t acc_bits, float sa_row, float sw_col, float bias_col) {
+    return __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(acc_bits)), sa_row), sw_col), bias_col);
+}
+
+template <int EPI_WARPS, int STAGES, int EPI>
+__global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* stage_a = smem;
+    uint8_t* stage_b = smem + STAGES * kAStage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(stage_b + STAGES * kBStage);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    int* last_flag = abort_flag + 1;
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int KB = p.kb_int + p.kb_f16;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], EPI_WARPS);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        *last_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&p.tm_a);
+        tma_prefetch_desc(&p.tm_b);
+        tma_prefetch_desc(&p.tm_ah);
+        tma_prefetch_desc(&p.tm_bh);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    volatile int* vabort = abort_flag;
+
+    // Inputs of this kernel may be written by the kernel launched just before it on the stream
+    // (programmatic dependent launch): everything above overlapped that kernel's tail.
+    grid_dependency_wait();
+    const int split = p.slice_mode ? min(max(__ldg(p.split), 0), p.M) : 0;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            const uint64_t pol_a = l2_policy_evict_last();
+            const uint64_t pol_b = p.evict_first_b ? l2_policy_evict_first() : l2_policy_evict_normal();
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0;        // bit s: stage s has been armed at least once
+            uint32_t armed_parity = 0; // bit s: parity of the last arming of stage s
+            Cursor cur = cursor_init(p);
+            Segment seg;
+            bool ok = true;
+            while (ok && cursor_next(p, split, cur, seg)) {
+                int part, mt, nt;
+                tile_coords(p, seg.tile, part, mt, nt);
+                const int m0 = mt * kBM;
+                const int b0 = (EPI == kEpiSwiglu) ? nt * (kBN / 2) : nt * kBN;
+                const int b1 = (EPI == kEpiSwiglu) ? p.H + nt * (kBN / 2) : nt * kBN + kBN / 2;
+                for (int kb = seg.k0; kb < seg.k1; ++kb) {
+                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns, vabort)) {
+                        if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutEmpty);
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                    uint8_t* sa_ = stage_a + stage * kAStage;
+                    uint8_t* sb_ = stage_b + stage * kBStage;
+                    if (kb < p.kb_int) {
+                        const int x = (part * p.kb_int_part + kb) * kRowBytes;
+                        tma_load_2d(sa_, &p.tm_a, &full[stage], x, m0, pol_a);
+                        tma_load_2d(sb_, &p.tm_b, &full[stage], x, b0, pol_b);
+                        tma_load_2d(sb_ + kBStage / 2, &p.tm_b, &full[stage], x, b1, pol_b);
+                    } else {
+                        const int x = (part * p.kb_f16_part + kb - p.kb_int) * (kRowBytes / 2);
+                        tma_load_2d(sa_, &p.tm_ah, &full[stage], x, m0, pol_a);
+                        tma_load_2d(sb_, &p.tm_bh, &full[stage], x, b0, pol_b);
+                        tma_load_2d(sb_ + kBStage / 2, &p.tm_bh, &full[stage], x, b1, pol_b);
+                    }
+                    armed |= 1u << stage;
+                    armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Drain: every copy this thread started must have landed before the CTA can exit.
+            for (int s = 0; s < STAGES; ++s) {
+                if (armed & (1u << s)) {
+                    if (!mbar_wait_bounded(&full[s], (armed_parity >> s) & 1, p.timeout_ns, nullptr)) {
+                        atomicOr(p.status, kStatusTimeoutDrain);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc_i8 = idesc_i8_s32(kBM, kBN);
+            const uint32_t idesc_f16 = idesc_bf16_f32(kBM, kBN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int buf = 0;
+            uint32_t acc_phase = 0;
+            Cursor cur = cursor_init(p);
+            Segment seg;
+            bool ok = true;
+            while (ok && cursor_next(p, split, cur, seg)) {
+                if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1, p.timeout_ns, vabort)) {
+                    if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutAccEmpty);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_int = tmem_base + buf * kBN;
+                const uint32_t d_f32 = (p.mode == 1) ? tmem_base + buf * kBN : tmem_base + kBN;
+                const int first_f = max(seg.k0, p.kb_int);
+                for (int kb = seg.k0; kb < seg.k1; ++kb) {
+                    if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns, vabort)) {
+                        if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutFull);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = sw128_kmajor_desc(smem_u32(stage_a + stage * kAStage));
+                    const uint64_t bd = sw128_kmajor_desc(smem_u32(stage_b + stage * kBStage));
+                    if (kb < p.kb_int) {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            umma_i8(d_int, ad + 2 * k, bd + 2 * k, idesc_i8, (kb > seg.k0 || k > 0) ? 1u : 0u);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            umma_f16(d_f32, ad + 2 * k, bd + 2 * k, idesc_f16, (kb > first_f || k > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[buf]);
+                if (p.acc_bufs == 2) {
+                    buf ^= 1;
+                    if (buf == 0) acc_phase ^= 1;
+                } else {
+                    acc_phase ^= 1;
+                }
+            }
+            // Drain: all MMAs issued by this thread complete before TMEM is freed.
+            umma_commit(drain);
+            if (!mbar_wait_bounded(drain, 0, p.timeout_ns, nullptr)) atomicOr(p.status, kStatusTimeoutDrain);
+        }
+        __syncwarp();
+    } else {
+        // --------------------------------------------------------------------------------- epilogue
+        // Epilogue warps only ever stop at the accumulator wait, and only on its own timeout (no abort
+        // flag), so either all of them pass a segment or none does: the named barriers below stay matched.
+        const int e = warp - 2;
+        const int q = warp & 3;                      // TMEM lane quarter this warp may access
+        const int r_tile = q * 32 + lane;            // accumulator row (= TMEM lane) of this thread
+        constexpr int kCols = (EPI == kEpiSwiglu) ? kBN / 2 : kBN;   // output columns of a tile
+        constexpr int kSplit = EPI_WARPS / 4;        // warps sharing one lane quarter split the columns
+        const int c_lo = (e / 4) * (kCols / kSplit);
+        const int c_hi = c_lo + kCols / kSplit;
+        const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+        int buf = 0;
+        uint32_t acc_phase = 0;
+        Cursor cur = cursor_init(p);
+        Segment seg;
+        while (cursor_next(p, split, cur, seg)) {
+            int part, mt, nt;
+            tile_coords(p, seg.tile, part, mt, nt);
+            const int m0 = mt * kBM;
+            if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
+                raise_error(p, abort_flag, kStatusTimeoutAccFull);
+                break;
+            }
+            tc_fence_after();
+            int row_lo, row_hi, out_part;
+            tile_plan(p, part, split, row_lo, row_hi, out_part);
+            const int grow = m0 + r_tile;
+            const bool row_ok = grow >= row_lo && grow < row_hi;
+            const uint32_t t_int = tmem_base + buf * kBN + lane_off;
+            const uint32_t t_f32 = ((p.mode == 1) ? tmem_base + buf * kBN : tmem_base + kBN) + lane_off;
+            const bool whole = seg.whole;
+
+            // Split tile: publish this CTA's int32 partial, then find out whether it completes the tile.
+            bool finish = whole;
+            const int st = seg.tile - p.dp_tiles;
+            if (!whole) {
+                int4* slot = reinterpret_cast<int4*>(
+                    p.ws_partials + (static_cast<size_t>(blockIdx.x) * 2 + sk_slot(p, blockIdx.x, st)) * kSlotInts);
+                for (int cc = c_lo; cc < c_hi; cc += 32) {
+                    uint32_t a[32];
+                    tmem_ld_x32_sync(t_int + cc, a);
+                    if (row_ok) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            __stcg(slot + ((cc + i) / 4) * kBM + r_tile, make_int4(a[i], a[i + 1], a[i + 2], a[i + 3]));
+                    }
+                    if (EPI == kEpiSwiglu) {
+                        tmem_ld_x32_sync(t_int + kBN / 2 + cc, a);
+                        if (row_ok) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4)
+                                __stcg(slot + ((kBN / 2 + cc + i) / 4) * kBM + r_tile,
+                                       make_int4(a[i], a[i + 1], a[i + 2], a[i + 3]));
+                        }
+                    }
+                }
+                __threadfence();
+                named_bar_sync(1, EPI_WARPS * 32);
+                if (threadIdx.x == 64) {
+                    const int n = seg.k1 - seg.k0;
+                    const int old = atomicAdd(p.ws_counters + st, n);
+                    *last_flag = (old + n == KB) ? 1 : 0;
+                }
+                named_bar_sync(1, EPI_WARPS * 32);
+                finish = *reinterpret_cast<volatile int*>(last_flag) != 0;
+                if (finish) __threadfence();
+            }
+
+            if (finish) {
+                // Contributors of a split tile other than this CTA, in CTA order.
+                int c_first = 0, c_last = -1;
+                if (!whole) {
+                    c_first = sk_owner(p, static_cast<long long>(st) * KB);
+                    c_last = sk_owner(p, static_cast<long long>(st + 1) * KB - 1);
+                }
+                const float sa_row = (p.mode == 0 && row_ok) ? p.sa[part * p.sa_part_stride + grow] : 0.f;
+                const bool add_f = (p.mode == 0 && p.kb_f16 > 0);
+                const uint32_t t_acc = (p.mode == 0) ? t_int : t_f32;
+                for (int cc = c_lo; cc < c_hi; cc += 32) {
+                    uint32_t g[32];
+                    uint32_t u[32];
+                    uint32_t fg[32];
+                    uint32_t fu[32];
+                    if (EPI == kEpiSwiglu) {
+                        tmem_ld2_x32_sync(t_acc + cc, t_acc + kBN / 2 + cc, g, u);
+                        if (add_f) tmem_ld2_x32_sync(t_f32 + cc, t_f32 + kBN / 2 + cc, fg, fu);
+                    } else {
+                        tmem_ld_x32_sync(t_acc + cc, g);
+                        if (add_f) tmem_ld_x32_sync(t_f32 + cc, fg);
+                    }
+                    if (!row_ok) continue;
+                    if (!whole) {
+                        for (int c = c_first; c <= c_last; ++c) {
+                            if (c == static_cast<int>(blockIdx.x)) continue;
+                            if (sk_begin(p, c + 1) <= sk_begin(p, c)) continue;
+                            const int4* slot = reinterpret_cast<const int4*>(
+                                p.ws_partials + (static_cast<size_t>(c) * 2 + sk_slot(p, c, st)) * kSlotInts);
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4) {
+                                const int4 v = __ldcg(slot + ((cc + i) / 4) * kBM + r_tile);
+                                g[i] += v.x; g[i + 1] += v.y; g[i + 2] += v.z; g[i + 3] += v.w;
+                            }
+                            if (EPI == kEpiSwiglu) {
+#pragma unroll
+                                for (int i = 0; i < 32; i += 4) {
+                                    const int4 v = __ldcg(slot + ((kBN / 2 + cc + i) / 4) * kBM + r_tile);
+                                    u[i] += v.x; u[i + 1] += v.y; u[i + 2] += v.z; u[i + 3] += v.w;
+                                }
+                            }
+                        }
+                    }
+                    uint32_t packed[16];
+                    __nv_bfloat16* dst;
+                    if (EPI == kEpiSwiglu) {
+                        const int n0 = nt * (kBN / 2);
+                        const int colg = part * p.n_part_stride + n0 + cc;
+                        const int colu = colg + p.H;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            float vg[4], vu[4];
+                            if (p.mode == 0) {
+                                const float4 swg = __ldg(reinterpret_cast<const float4*>(p.sw + colg + i));
+                                const float4 swu = __ldg(reinterpret_cast<const float4*>(p.sw + colu + i));
+                                const float4 bg = __ldg(reinterpret_cast<const float4*>(p.bias + colg + i));
+                                const float4 bu = __ldg(reinterpret_cast<const float4*>(p.bias + colu + i));
+                                vg[0] = dequant1(g[i], sa_row, swg.x, bg.x);
+                                vg[1] = dequant1(g[i + 1], sa_row, swg.y, bg.y);
+                                vg[2] = dequant1(g[i + 2], sa_row, swg.z, bg.z);
+                                vg[3] = dequant1(g[i + 3], sa_row, swg.w, bg.w);
+                                vu[0] = dequant1(u[i], sa_row, swu.x, bu.x);
+                                vu[1] = dequant1(u[i + 1], sa_row, swu.y, bu.y);
+                                vu[2] = dequant1(u[i + 2], sa_row, swu.z, bu.z);
+                                vu[3] = dequant1(u[i + 3], sa_row, swu.w, bu.w);
+                                if (add_f) {
+#pragma unroll
+                                    for (int j = 0; j < 4; ++j) {
+                                        vg[j] = __fadd_rn(vg[j], __uint_as_float(fg[i + j]));
+                                        vu[j] = __fadd_rn(vu[j], __uint_as_float(fu[i + j]));
+                                    }
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    vg[j] = __uint_as_float(g[i + j]);
+                                    vu[j] = __uint_as_float(u[i + j]);
+                                }
+                            }
+                            __nv_bfloat16 o[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) o[j] = swiglu_bf16(bf16_round(vg[j]), bf16_round(vu[j]));
+                            packed[i / 2] = pack_bf16x2(o[0], o[1]);
+                            packed[i / 2 + 1] = pack_bf16x2(o[2], o[3]);
+                        }
+                        dst = p.out + static_cast<size_t>(grow) * p.ldo + n0 + cc;
+                    } else {
+                        const int n0 = nt * kBN;
+                        const int col = part * p.n_part_stride + n0 + cc;
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            float v[4];
+                            if (p.mode == 0) {
+                                const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sw + col + i));
+                                const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + col + i));
+                                v[0] = dequant1(g[i], sa_row, s4.x, b4.x);
+                                v[1] = dequant1(g[i + 1], sa_row, s4.y, b4.y);
+                                v[2] = dequant1(g[i + 2], sa_row, s4.z, b4.z);
+                                v[3] = dequant1(g[i + 3], sa_row, s4.w, b4.w);
+                                if (add_f) {
+#pragma unroll
+                                    for (int j = 0; j < 4; ++j) v[j] = __fadd_rn(v[j], __uint_as_float(fg[i + j]));
+                                }
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) v[j] = __uint_as_float(g[i + j]);
+                            }
+                            packed[i / 2] = pack_bf16x2(__float2bfloat16_rn(v[0]), __float2bfloat16_rn(v[1]));
+                            packed[i / 2 + 1] = pack_bf16x2(__float2bfloat16_rn(v[2]), __float2bfloat16_rn(v[3]));
+                        }
+                        dst = p.out + out_part * p.out_part_stride + static_cast<size_t>(grow) * p.ldo + n0 + cc;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        reinterpret_cast<uint4*>(dst)[i] =
+                            make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                }
+                if (!whole) {
+                    named_bar_sync(1, EPI_WARPS * 32);
+                    if (threadIdx.x == 64) p.ws_counters[st] = 0;
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            if (p.acc_bufs == 2) {
+                buf ^= 1;
+                if (buf == 0) acc_phase ^= 1;
+            } else {
+                acc_phase ^= 1;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+}  // namespace reax

@@ -1,0 +1,295 @@
+// HBM-bound kernels of the gate/up path: per-token INT8 quantization (row and grouped variants),
+// the ordered bf16 partial reductions, the SwiGLU of a computed gate|up pair, the SiLU domain table
+// and the bounded-wait self test.
+#pragma once
+
+#include "common.cuh"
+
+namespace reax {
+
+// Division used by the quantizer where the reference writes a plain '/' in Triton
+// (reaxv2/quantize.py:18-19,42): kDivIeee = IEEE round-to-nearest, kDivFull = PTX div.full.f32.
+enum QuantDivision : int { kDivIeee = 0, kDivFull = 1 };
+
+template <int DIV>
+REAX_DEVI float quant_div(float a, float b) {
+    if constexpr (DIV == kDivIeee) {
+        return __fdiv_rn(a, b);
+    } else {
+        float r;
+        asm("div.full.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+        return r;
+    }
+}
+
+// Block-wide max of non-negative floats (warp shuffles, then one value per warp in shared memory).
+REAX_DEVI float block_max_nonneg(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x / 32;
+        v = lane < nw ? red[lane] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) red[32] = v;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+// Eight consecutive quantizer inputs of one row: x[row, src[c]] for c in [c0, c0 + 8), as float.
+// One 16-byte load when the eight sources are consecutive and 16-byte aligned, gathers otherwise.
+REAX_DEVI void load8_columns(const __nv_bfloat16* xr, const int* src, bool aligned_x, float (&v)[8], int (&idx)[8]) {
+    const int4 i0 = __ldg(reinterpret_cast<const int4*>(src));
+    const int4 i1 = __ldg(reinterpret_cast<const int4*>(src) + 1);
+    idx[0] = i0.x; idx[1] = i0.y; idx[2] = i0.z; idx[3] = i0.w;
+    idx[4] = i1.x; idx[5] = i1.y; idx[6] = i1.z; idx[7] = i1.w;
+    bool run = aligned_x && (idx[0] & 7) == 0;
+#pragma unroll
+    for (int i = 1; i < 8; ++i) run = run && idx[i] == idx[0] + i;
+    if (run) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr + idx[0]));
+        const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(b[i]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(xr[idx[i]]);
+    }
+}
+
+// ------------------------------------------------------------------------------ a1: per-token quantization
+// One CTA per row (reaxv2/quantize.py:5-29).  Pass 1: v = (x - centre) / smoothing, absmax over the
+// row; scale = max(absmax, 1e-12) / 127.  Pass 2 recomputes v (same float ops, same result) and
+// stores nearbyint(div_rn(v, scale)) clamped to [-127, 127].  The row is re-read from L1/L2.
+template <int DIV>
+__global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                                         const int* __restrict__ low_columns,
+                                                         const int* __restrict__ high_columns,
+                                                         const float* __restrict__ smoothing,
+                                                         const float* __restrict__ centers, int8_t* __restrict__ low,
+                                                         __nv_bfloat16* __restrict__ high, float* __restrict__ scales,
+                                                         int K, int KL, int KH, int center, int aligned_x) {
+    __shared__ float red[33];
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const int row = blockIdx.x;
+    const __nv_bfloat16* xr = x + static_cast<size_t>(row) * K;
+    const int KL8 = KL & ~7;
+    if (KL > 0) {
+        float amax = 0.f;
+        for (int c0 = threadIdx.x * 8; c0 < KL8; c0 += blockDim.x * 8) {
+            float v[8];
+            int idx[8];
+            load8_columns(xr, low_columns + c0, aligned_x != 0, v, idx);
+            const float4 s0 = __ldg(reinterpret_cast<const float4*>(smoothing + c0));
+            const float4 s1 = __ldg(reinterpret_cast<const float4*>(smoothing + c0) + 1);
+            const float sm[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            float ce[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (center) {
+                const float4 c0v = __ldg(reinterpret_cast<const float4*>(centers + c0));
+                const float4 c1v = __ldg(reinterpret_cast<const float4*>(centers + c0) + 1);
+                ce[0] = c0v.x; ce[1] = c0v.y; ce[2] = c0v.z; ce[3] = c0v.w;
+                ce[4] = c1v.x; ce[5] = c1v.y; ce[6] = c1v.z; ce[7] = c1v.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float t = center ? __fsub_rn(v[i], ce[i]) : v[i];
+                t = quant_div<DIV>(t, sm[i]);
+                amax = fmaxf(amax, fabsf(t));
+            }
+        }
+        for (int c = KL8 + threadIdx.x; c < KL; c += blockDim.x) {
+            float t = __bfloat162float(xr[__ldg(low_columns + c)]);
+            if (center) t = __fsub_rn(t, __ldg(centers + c));
+            t = quant_div<DIV>(t, __ldg(smoothing + c));
+            amax = fmaxf(amax, fabsf(t));
+        }
+        amax = block_max_nonneg(amax, red);
+        const float scale = quant_div<DIV>(fmaxf(amax, 1.0e-12f), 127.0f);
+        if (threadIdx.x == 0) scales[row] = scale;
+        int8_t* lr = low + static_cast<size_t>(row) * KL;
+        const bool vec_store = (KL & 7) == 0;
+        for (int c0 = threadIdx.x * 8; c0 < KL8; c0 += blockDim.x * 8) {
+            float v[8];
+            int idx[8];
+            load8_columns(xr, low_columns + c0, aligned_x != 0, v, idx);
+            const float4 s0 = __ldg(reinterpret_cast<const float4*>(smoothing + c0));
+            const float4 s1 = __ldg(reinterpret_cast<const float4*>(smoothing + c0) + 1);
+            const float sm[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+            float ce[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (center) {
+                const float4 c0v = __ldg(reinterpret_cast<const float4*>(centers + c0));
+                const float4 c1v = __ldg(reinterpret_cast<const float4*>(centers + c0) + 1);
+                ce[0] = c0v.x; ce[1] = c0v.y; ce[2] = c0v.z; ce[3] = c0v.w;
+                ce[4] = c1v.x; ce[5] = c1v.y; ce[6] = c1v.z; ce[7] = c1v.w;
+            }
+            uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                float t = center ? __fsub_rn(v[i], ce[i]) : v[i];
+                t = quant_div<DIV>(t, sm[i]);
+                const float r = fminf(fmaxf(rintf(__fdiv_rn(t, scale)), -127.f), 127.f);
+                packed[i / 4] |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * (i % 4));
+            }
+            if (vec_store) {
+                *reinterpret_cast<uint2*>(lr + c0) = make_uint2(packed[0], packed[1]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) lr[c0 + i] = static_cast<int8_t>((packed[i / 4] >> (8 * (i % 4))) & 0xFFu);
+            }
+        }
+        for (int c = KL8 + threadIdx.x; c < KL; c += blockDim.x) {
+            float t = __bfloat162float(xr[__ldg(low_columns + c)]);
+            if (center) t = __fsub_rn(t, __ldg(centers + c));
+            t = quant_div<DIV>(t, __ldg(smoothing + c));
+            const float r = fminf(fmaxf(rintf(__fdiv_rn(t, scale)), -127.f), 127.f);
+            lr[c] = static_cast<int8_t>(static_cast<int>(r));
+        }
+    } else if (threadIdx.x == 0) {
+        scales[row] = 1.0f;
+    }
+    __nv_bfloat16* hr = high + static_cast<size_t>(row) * KH;
+    for (int c = threadIdx.x; c < KH; c += blockDim.x) hr[c] = xr[__ldg(high_columns + c)];
+}
+
+// ---------------------------------------------------------------------------- a2: grouped quantization
+// grid (M, P): row `blockIdx.x`, group `blockIdx.y` (reaxv2/quantize.py:31-52).  Sources of -1 pad a
+// group and quantize as 0; the centre is always subtracted; the codes are not clamped.
+template <int DIV>
+__global__ void __launch_bounds__(256) quant_groups_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           const int* __restrict__ low_columns,
+                                                           const int* __restrict__ high_columns,
+                                                           const float* __restrict__ centers,
+                                                           const float* __restrict__ smoothing,
+                                                           int8_t* __restrict__ low, __nv_bfloat16* __restrict__ high,
+                                                           float* __restrict__ scales, int M, int K, int G, int HP,
+                                                           int P) {
+    __shared__ float red[33];
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const int row = blockIdx.x, part = blockIdx.y;
+    const __nv_bfloat16* xr = x + static_cast<size_t>(row) * K;
+    float amax = 0.f;
+    for (int o = threadIdx.x; o < G; o += blockDim.x) {
+        const int pos = part * G + o;
+        const int src = __ldg(low_columns + pos);
+        float t = 0.f;
+        if (src >= 0) t = quant_div<DIV>(__fsub_rn(__bfloat162float(xr[src]), __ldg(centers + pos)), __ldg(smoothing + pos));
+        amax = fmaxf(amax, fabsf(t));
+    }
+    amax = block_max_nonneg(amax, red);
+    const float scale = quant_div<DIV>(fmaxf(amax, 1.0e-12f), 127.0f);
+    if (threadIdx.x == 0) scales[static_cast<size_t>(part) * M + row] = scale;
+    int8_t* lr = low + static_cast<size_t>(row) * P * G;
+    for (int o = threadIdx.x; o < G; o += blockDim.x) {
+        const int pos = part * G + o;
+        const int src = __ldg(low_columns + pos);
+        float t = 0.f;
+        if (src >= 0) t = quant_div<DIV>(__fsub_rn(__bfloat162float(xr[src]), __ldg(centers + pos)), __ldg(smoothing + pos));
+        lr[pos] = static_cast<int8_t>(__float2int_rn(rintf(__fdiv_rn(t, scale))));
+    }
+    __nv_bfloat16* hr = high + static_cast<size_t>(row) * P * HP;
+    for (int o = threadIdx.x; o < HP; o += blockDim.x) {
+        const int idx = part * HP + o;
+        const int src = __ldg(high_columns + idx);
+        hr[idx] = src >= 0 ? xr[src] : __float2bfloat16_rn(0.f);
+    }
+}
+
+// ------------------------------------------------------------------ a3 / a12: ordered partial reductions
+// out[i] = bf16(((float(p0[i]) + float(p1[i])) + ...) over `count(row)` partials, float32 adds in
+// partial order (reaxv2/quantize.py:55-61; runtime/mixed_origin_bf16.py:8-17).  With `split` null
+// every row sums P0 partials; otherwise rows < split[0] sum P0 and the others P1.  With `vec` set
+// (16-byte aligned planes of a multiple of 8 elements, and N % 8 == 0 when split is given) eight
+// elements move per 16-byte access.
+__global__ void __launch_bounds__(256) fold_partials_kernel(const __nv_bfloat16* __restrict__ parts,
+                                                            const int* __restrict__ split,
+                                                            __nv_bfloat16* __restrict__ out, long long total,
+                                                            int N, int P0, int P1, int vec) {
+    grid_dependency_wait();
+    const int border = split ? __ldg(split) : 0x7fffffff;
+    const int Pm = max(P0, P1);
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; v * 8 < total; v += stride) {
+        const long long i0 = v * 8;
+        // vec: 16-byte aligned planes and, with a split, rows of a multiple of 8 elements
+        if (vec && i0 + 8 <= total) {
+            const int row = static_cast<int>(i0 / N);
+            const int count = row < border ? P0 : P1;
+            uint4 raw = __ldg(reinterpret_cast<const uint4*>(parts + i0));
+            float acc[8];
+            const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = __bfloat162float(b[j]);
+            for (int p = 1; p < Pm; ++p) {
+                if (p >= count) break;
+                raw = __ldg(reinterpret_cast<const uint4*>(parts + p * total + i0));
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], __bfloat162float(b[j]));
+            }
+            uint4 o;
+            uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) ow[j] = pack_bf16x2(__float2bfloat16_rn(acc[2 * j]), __float2bfloat16_rn(acc[2 * j + 1]));
+            *reinterpret_cast<uint4*>(out + i0) = o;
+        } else {
+            for (long long i = i0; i < total && i < i0 + 8; ++i) {
+                const int row = static_cast<int>(i / N);
+                const int count = row < border ? P0 : P1;
+                float acc = __bfloat162float(parts[i]);
+                for (int p = 1; p < count; ++p) acc = __fadd_rn(acc, __bfloat162float(parts[p * total + i]));
+                out[i] = __float2bfloat16_rn(acc);
+            }
+        }
+    }
+}
+
+// ----------------------------------------------------------------------------------------- SwiGLU pair
+// out[r, c] = bf16(bf16(silu_f32(g[r, c])) * u[r, c]) for row-strided gate and up views
+// (vendor/s1eng/s1eng/fused.py:145-164, the same rounding points as hybrid8_tiles.cuh:676-679).
+__global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ g,
+                                                       const __nv_bfloat16* __restrict__ u,
+                                                       __nv_bfloat16* __restrict__ out, int rows, int cols,
+                                                       long long gs, long long us) {
+    grid_dependency_wait();
+    const long long total = static_cast<long long>(rows) * cols;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+        const long long r = i / cols, c = i % cols;
+        const float gv = __bfloat162float(g[r * gs + c]);
+        const float uv = __bfloat162float(u[r * us + c]);
+        out[i] = swiglu_bf16(gv, uv);
+    }
+}
+
+// table[i] = bf16(silu_f32(bf16 value with bit pattern i)) for all 65536 patterns.
+__global__ void silu_table_kernel(__nv_bfloat16* __restrict__ table) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < 65536) {
+        const float x = __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(i)));
+        table[i] = __float2bfloat16_rn(silu_f32(x));
+    }
+}
+
+// ----------------------------------------------------------------------------------- bounded-wait test
+// Waits on an mbarrier that nothing ever arrives on, with the same bounded wait the GEMM uses; when
+// the limit expires it ORs kStatusSelfTest into *status and returns, leaving the context usable.
+__global__ void selftest_wait_kernel(unsigned* status, unsigned long long timeout_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (!mbar_wait_bounded(&bar, 0, timeout_ns, nullptr)) atomicOr(status, kStatusSelfTest);
+    }
+    __syncthreads();
+}
+
+}  // namespace reax

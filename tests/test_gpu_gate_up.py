@@ -1,0 +1,144 @@
+"""GPU parity of the fused INT8 gate/up + dequant + SwiGLU kernel against the CPU oracle.
+
+INT8 path (KH == 0): the int32 accumulation and the float32 dequant are exact restatements, so the
+bf16 output must be bit-identical to the oracle evaluated with the GPU's own SiLU table (the only
+transcendental, expf, is CUDA's on the device).  Against the oracle's own correctly-rounded SiLU the
+bound is the one north_star states: at most 1 bf16 ulp, with the max abs/rel error reported.
+Hybrid banks (KH > 0) add BF16 outlier columns whose float32 accumulation order is the hardware's:
+tolerance 2 ulps of the output, or 1e-3 of the row's largest output magnitude.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import reax_oracle as ro
+from tests import helpers as H
+
+pytestmark = pytest.mark.gpu
+
+
+def gpu_silu_table():
+    from reax_engine_runtime_v3_b200 import _native
+    t = torch.empty(65536, dtype=torch.bfloat16, device="cuda")
+    _native.check(_native.load().reax_silu_table(t.data_ptr(), _native.stream_handle()))
+    torch.cuda.synchronize()
+    return H.bits(t)
+
+
+_TABLE = None
+
+
+def table():
+    global _TABLE
+    if _TABLE is None:
+        _TABLE = gpu_silu_table()
+    return _TABLE
+
+
+def run_project(x, bank, name="hybrid8_b128n256_s64n256"):
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native
+    out = Native(None).project(x, bank, name)
+    torch.cuda.synchronize()
+    return out
+
+
+def compare_int8(x, bank, rows=None, exact=True):
+    out = run_project(x.cuda(), H.bank_to(bank, "cuda"))
+    nb = H.bank_numpy(bank)
+    xb = H.bits(x)
+    sel = np.arange(x.shape[0]) if rows is None else rows
+    got = H.bits(out)[sel]
+    want_t = ro.gate_up_project(xb[sel], nb, table())
+    want_c = ro.gate_up_project(xb[sel], nb)
+    rep_t = H.ulp_report(got, want_t)
+    rep_c = H.ulp_report(got, want_c)
+    print("vs oracle(GPU silu table):", rep_t, "vs oracle(CPU silu):", rep_c)
+    if exact:
+        assert rep_t["n_diff"] == 0, rep_t
+    assert rep_c["max_ulp"] <= 1, rep_c
+    return out
+
+
+@pytest.mark.parametrize("M", [16, 1, 17])
+def test_cfg1_shape(M):
+    """X [16, 1024] ~ N(0,1), Wg/Wu int8 [2816, 1024], scales U(1e-3, 1e-2)."""
+    g = H.gen(1 + M)
+    compare_int8(H.activations(g, M, 1024), H.int8_bank(g, 1024, 2816))
+
+
+@pytest.mark.parametrize("M", [1, 8, 32, 64])
+def test_cfg2_decode_full_size(M):
+    """BASELINE config 2 at full size: K=4096, H=14336 (stream-K split over all SMs)."""
+    g = H.gen(20 + M)
+    compare_int8(H.activations(g, M, 4096), H.int8_bank(g, 4096, 14336))
+
+
+@pytest.mark.parametrize("M,K,Hh", [(129, 512, 1024), (300, 1024, 8192), (1024, 512, 4096), (2048, 256, 4096),
+                                    (4096, 384, 2560)])
+def test_split_and_wave_shapes(M, K, Hh):
+    """Tile counts below, between and above the SM count (data-parallel waves + stream-K remainder)."""
+    g = H.gen(M + K + Hh)
+    compare_int8(H.activations(g, M, K), H.int8_bank(g, K, Hh))
+
+
+def test_cfg3_prefill_rows_sample():
+    """BASELINE config 3 (M=4096, K=4096, H=14336): full GPU run, oracle on a sample of rows."""
+    g = H.gen(3)
+    rows = np.concatenate([np.arange(0, 64), np.arange(2000, 2040), np.arange(4096 - 64, 4096)])
+    compare_int8(H.activations(g, 4096, 4096), H.int8_bank(g, 4096, 14336), rows=rows)
+
+
+def test_cfg5_outliers():
+    """BASELINE config 5a: Student-t activations with 8 channels x50, buckets 128 / 512 / 2048."""
+    g = H.gen(5)
+    bank = H.int8_bank(g, 4096, 14336)
+    for M in (128, 512):
+        compare_int8(H.activations(g, M, 4096, "student"), bank, rows=np.arange(0, M, 3))
+
+
+def test_hybrid_bank_with_outlier_columns():
+    """Production-style bank: centred, power-of-two smoothing, bias, 128 BF16 outlier columns."""
+    g = H.gen(11)
+    x = H.activations(g, 200, 2560)
+    bank = H.int8_bank(g, 2560, 1024, KH=128, centered=True, pow2_smoothing=True, bias=True)
+    out = run_project(x.cuda(), H.bank_to(bank, "cuda"))
+    nb = H.bank_numpy(bank)
+    got = H.bits(out)
+    want = ro.gate_up_project(H.bits(x), nb, table())
+    d = ro.ulp_distance_bf16(got, want)
+    gf, wf = ro.bf16_to_f32(got), ro.bf16_to_f32(want)
+    tol = 1e-3 * np.abs(wf).max(axis=1, keepdims=True)
+    ok = (d <= 2) | (np.abs(gf - wf) <= tol)
+    print(H.ulp_report(got, want))
+    assert ok.all()
+
+
+def test_batch_invariance_first16():
+    """The reference's screen invariant (resident_gate_up_screen.py:25-31): the first 16 rows computed
+    alone equal rows 0..15 of the full batch, bit for bit."""
+    g = H.gen(16)
+    bank = H.bank_to(H.int8_bank(g, 4096, 14336), "cuda")
+    x = H.activations(g, 768, 4096).cuda()
+    full = run_project(x, bank)
+    first = run_project(x[:16].contiguous(), bank)
+    assert torch.equal(full[:16].view(torch.int16), first.view(torch.int16))
+
+
+def test_repeat_calls_identical_and_status_clean():
+    from reax_engine_runtime_v3_b200 import _native
+    g = H.gen(17)
+    bank = H.bank_to(H.int8_bank(g, 1024, 8192), "cuda")
+    x = H.activations(g, 300, 1024).cuda()
+    a = run_project(x, bank)
+    b = run_project(x, bank)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    assert _native.read_status(_native.workspace(x.device)) == 0
+
+
+def test_rejects_unsupported_shape():
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import gate_up_i8
+    a = torch.zeros(4, 100, dtype=torch.int8, device="cuda")
+    w = torch.zeros(512, 100, dtype=torch.int8, device="cuda")
+    f = torch.zeros(512, device="cuda")
+    with pytest.raises(RuntimeError, match="KL"):
+        gate_up_i8(a, w, None, None, torch.ones(4, device="cuda"), f, f)
