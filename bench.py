@@ -1,0 +1,462 @@
+"""Benchmark of the B200 gate/up path (quantize -> INT8 gate/up GEMM -> dequant -> SwiGLU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg2]
+
+Prints ONE JSON line on rank 0.  A step is one pass of the hot path over one batch of synthetic input
+(the BASELINE config named by ``--workload``; default ``cfg2``: the decode buckets M = 1, 8, 32, 64 at
+K = 4096, H = 14336, one quantize + one gate/up launch each).  Under torchrun (N > 1) the intermediate
+dimension H is sharded over the ranks: rank r owns gate rows [r*H/N, (r+1)*H/N) and the matching up
+rows, every rank quantizes the replicated activations itself, and no collective runs on the path
+(the total work is fixed, so the scaling is strong).  Timing: W warm-up steps, then exactly K steps
+between barriers + synchronizes, CUDA events on the launching stream, max over ranks.  Three copies of
+the weights rotate between steps (3 x 117 MB > 126 MB L2), so no step finds its weights in L2.
+
+``--impl reference`` times the reference arithmetic of the path on the host cores (the reference
+ships no CPU implementation of it; the timed code is the oracle's restatement, ``oracle/``), on
+rank 0 only, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "gate/up+SwiGLU tokens/s"
+
+WORKLOADS = {
+    # name: (buckets of M, K, H, activation kind, weight scale range, description)
+    "cfg1": ((16,), 1024, 2816, "normal", (1e-3, 1e-2), "config 1: X [16, 1024], Wg/Wu int8 [2816, 1024]"),
+    "cfg2": ((1, 8, 32, 64), 4096, 14336, "normal", (1e-3, 1e-2),
+             "config 2 decode buckets M={1,8,32,64}, K=4096, Wg/Wu int8 [14336, 4096]"),
+    "cfg3": ((4096,), 4096, 14336, "normal", (1e-3, 1e-2), "config 3 prefill: X [4096, 4096], Wg/Wu int8 [14336, 4096]"),
+    "cfg4": ((8192,), 8192, 28672, "normal", (5e-4, 5e-3), "config 4: X [8192, 8192], Wg/Wu int8 [28672, 8192]"),
+    "cfg5a": ((128, 512, 2048), 4096, 14336, "student", (1e-3, 1e-2),
+              "config 5a: Student-t X (8 channels x50), buckets M={128,512,2048}, INT8 Wg/Wu [14336, 4096]"),
+    "cfg5b": ((128, 512, 2048), 4096, 14336, "student", None,
+              "config 5b: Student-t X, buckets M={128,512,2048}, BF16 Wg/Wu ~ N(0,0.02) [14336, 4096]"),
+}
+DEFAULT_WORKLOAD = "cfg2"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
+    ap.add_argument("--measure-int8-peak", action="store_true", help="print torch._int_mm int8 throughput and exit")
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3)
+    return a
+
+
+# -------------------------------------------------------------------------------------------------- inputs
+def make_inputs(name: str, rank: int, world: int, copies: int):
+    """Seeded synthetic inputs on the CPU (same on every rank), this rank's H shard on the GPU."""
+    buckets, K, H, kind, srange, _ = WORKLOADS[name]
+    g = torch.Generator().manual_seed(20261201)
+    xs = []
+    for M in buckets:
+        if kind == "normal":
+            x = torch.randn(M, K, generator=g)
+        else:
+            normal = torch.randn(M, K, generator=g)
+            chi2 = torch.randn(M, K, 3, generator=g).square().sum(-1)
+            x = normal / torch.sqrt(chi2 / 3.0)
+            idx = torch.arange(8) * (K // 8) + 3
+            x[:, idx] *= 50.0
+        xs.append(x.to(torch.bfloat16))
+    h = H // world
+    rows = torch.cat([torch.arange(rank * h, (rank + 1) * h), H + torch.arange(rank * h, (rank + 1) * h)])
+    dev = torch.device("cuda", torch.cuda.current_device())
+    banks = []
+    for c in range(copies):
+        gc = torch.Generator().manual_seed(1000 + c)
+        if srange is None:
+            w = (torch.randn(2 * H, K, generator=gc) * 0.02).to(torch.bfloat16)[rows].contiguous()
+            banks.append(dict(w=w.to(dev)))
+        else:
+            w = torch.randint(-127, 128, (2 * H, K), generator=gc, dtype=torch.int8)[rows].contiguous()
+            lo, hi = srange
+            sw = (lo + (hi - lo) * torch.rand(2 * H, generator=gc))[rows].contiguous()
+            from types import SimpleNamespace
+            banks.append(SimpleNamespace(width=K, centered=False, low_columns=torch.arange(K, dtype=torch.int32, device=dev),
+                                         high_columns=torch.zeros(0, dtype=torch.int32, device=dev),
+                                         low_weight=w.to(dev), high_weight=torch.zeros(2 * h, 0, dtype=torch.bfloat16, device=dev),
+                                         smoothing=torch.ones(K, device=dev), centers=torch.zeros(K, device=dev),
+                                         scales=sw.to(dev), bias=torch.zeros(2 * h, device=dev)))
+    return xs, banks, h
+
+
+def gemm_bytes(M, K, h, int8=True):
+    """Algorithmic DRAM bytes of one gate/up GEMM launch: weights + per-channel scale and bias,
+    the activation operand, per-row scales, the bf16 output."""
+    if int8:
+        return 2 * h * K + 2 * h * 8 + M * K + M * 4 + M * h * 2
+    return 2 * h * K * 2 + M * K * 2 + M * h * 2
+
+
+def gemm_ops(M, K, h):
+    return 2 * M * (2 * h) * K
+
+
+# -------------------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        for ln in self.lines:
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# -------------------------------------------------------------------------------------------------- helpers
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def int8_peak():
+    """Measured dense INT8 throughput on this pool (torch._int_mm 8192^3, recorded under profiles/)."""
+    p = ROOT / "profiles" / "int8_peak.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return None
+
+
+def ncu_traffic(workload):
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        return json.loads(p.read_text()).get(workload)
+    return None
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+# -------------------------------------------------------------------------------------------------- CPU legs
+def cpu_run(name: str, budget_s: float = 12.0):
+    """Time the oracle's restatement of the path on the host cores over a bounded sample of the
+    workload (all buckets, a slice of the output columns); returns tokens/s scaled to full width."""
+    from oracle import reax_oracle as ro
+    buckets, K, H, kind, srange, _ = WORKLOADS[name]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = np.random.default_rng(7)
+    cols = min(H, 1024)
+    if srange is None:
+        w = (g.standard_normal((2 * cols, K)) * 0.02).astype(np.float32)
+        wb = ro.f32_to_bf16(w)
+    else:
+        w = g.integers(-127, 128, (2 * cols, K), dtype=np.int8)
+        sw = (1e-3 + 9e-3 * g.random(2 * cols)).astype(np.float32)
+        from types import SimpleNamespace
+        bank = SimpleNamespace(low_columns=np.arange(K), high_columns=np.zeros(0, np.int64), smoothing=np.ones(K, np.float32),
+                               centers=np.zeros(K, np.float32), centered=False, low_weight=w,
+                               high_weight=np.zeros((2 * cols, 0), np.uint16), scales=sw, bias=np.zeros(2 * cols, np.float32))
+    xs = [ro.f32_to_bf16(g.standard_normal((M, K)).astype(np.float32)) for M in buckets]
+    # cap rows so one pass stays bounded on the biggest prefill buckets
+    max_rows = 512
+    xs = [x[:max_rows] for x in xs]
+    tokens = sum(len(x) for x in xs)
+    t0 = time.perf_counter()
+    passes = 0
+    while True:
+        for x in xs:
+            if srange is None:
+                ro.gate_up_bf16(x, wb, 0, dict(parts=1, chunk=K), dict(parts=1, chunk=K))
+            else:
+                ro.gate_up_project(x, bank)
+        passes += 1
+        if time.perf_counter() - t0 > budget_s or passes >= 50:
+            break
+    dt = time.perf_counter() - t0
+    tok_s = tokens * passes / dt * (cols / H)
+    sample = (f"{passes} passes over buckets {list(len(x) for x in xs)} rows x {cols}/{H} output columns "
+              f"(scaled to full width), {dt:.1f} s")
+    return tok_s, threads, sample
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    buckets, K, H, kind, srange, desc = WORKLOADS[args.workload]
+    times = []
+    tok_s = None
+    threads = os.cpu_count() or 1
+    sample = ""
+    for i in range(args.warmup + args.steps):
+        budget = 1.5 if args.steps > 20 else 4.0
+        v, threads, sample = cpu_run(args.workload, budget_s=budget)
+        if i >= args.warmup:
+            times.append(v)
+    tok_s = statistics.median(times)
+    line = {"impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sum(buckets) / tok_s * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "s8" if srange else "bf16",
+            "data": "synthetic", "config": {"workload": desc, "parallelism": "host cores"},
+            "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# -------------------------------------------------------------------------------------------------- GPU leg
+def main():
+    args = parse()
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+    if not torch.cuda.is_available():
+        print(json.dumps({"error": "no CUDA device"}))
+        return 1
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    if args.measure_int8_peak:
+        return measure_int8_peak()
+
+    from reax_engine_runtime_v3_b200 import _native
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native
+    from reax_engine_runtime_v3_b200.runtime.mixed_origin_bf16 import Native as Bf16Native
+
+    buckets, K, H, kind, srange, desc = WORKLOADS[args.workload]
+    int8 = srange is not None
+    copies = 3
+    xs_cpu, banks, h = make_inputs(args.workload, rank, world, copies)
+    dev = torch.device("cuda", local)
+    xs = [x.to(dev) for x in xs_cpu]
+    gate_up = Native(None)
+    bf16 = Bf16Native()
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        b = banks[i % copies]
+        for x in xs:
+            if int8:
+                gate_up.project(x, b, "hybrid8_b128n256_s64n256")
+            else:
+                bf16.gate_up(x, b["w"])
+
+    for i in range(args.warmup):
+        step(i)
+    barrier(world)
+    _native.clear_status(_native.workspace(dev))
+
+    sampler = ClockSampler(local)
+    if rank == 0 or world > 1:
+        sampler.start()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    ev1.record(stream)
+    barrier(world)
+    clocks = sampler.stop()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ms, world)
+    status = _native.read_status(_native.workspace(dev))
+    tokens = sum(buckets)
+    value = tokens / (ms * 1e-3)
+    launches = args.steps * len(buckets) * (2 if int8 else 1)
+
+    # dominant kernel (the GEMM) timed alone, per launch, with events on its stream
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import gate_up_i8, quantize_rows
+    per_bucket = []
+    if int8:
+        pre = [quantize_rows(x, banks[0]) for x in xs]
+    for bi, x in enumerate(xs):
+        M = x.shape[0]
+        evs = []
+        for i in range(args.warmup + args.steps):
+            b = banks[i % copies]
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if int8:
+                low, high, sc = pre[bi]
+                gate_up_i8(low, b.low_weight, high, b.high_weight, sc, b.scales, b.bias)
+            else:
+                bf16.gate_up(x, b["w"])
+            e1.record(stream)
+            if i >= args.warmup:
+                evs.append((e0, e1))
+        torch.cuda.synchronize()
+        d = statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e-3
+        d = max_over_ranks(d, world)
+        per_bucket.append((M, d))
+    peaks, peak_kind = measured_peaks()
+    prefill = min(buckets) >= 512
+    if prefill:
+        ops = sum(gemm_ops(M, K, h) for M, _ in per_bucket)
+        dur = sum(d for _, d in per_bucket)
+        achieved = ops / dur / 1e12
+        if int8:
+            ip = int8_peak()
+            peak = ip["tops"] if ip else 4500.0
+            peak_src = "measured torch._int_mm int8" if ip else "datasheet dense INT8 (no measured int8 peak)"
+        else:
+            peak = peaks["bf16_tflops"]
+            peak_src = f"{peak_kind} bf16_tflops"
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s" if int8 else "TFLOP/s",
+                    "frac": achieved / peak, "peak_source": peak_src}
+    else:
+        by = sum(gemm_bytes(M, K, h, int8) for M, _ in per_bucket)
+        dur = sum(d for _, d in per_bucket)
+        achieved = by / dur / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs"}
+    roofline["traffic"] = ncu_traffic(args.workload)
+    roofline["per_launch_us"] = {str(M): round(d * 1e6, 2) for M, d in per_bucket}
+
+    # end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        xs_host = [x.pin_memory() for x in xs_cpu]
+        outs_host = [torch.empty((x.shape[0], h), dtype=torch.bfloat16).pin_memory() for x in xs_cpu]
+        for i in range(args.warmup):
+            for xh, oh in zip(xs_host, outs_host):
+                xd = xh.to(dev, non_blocking=True)
+                o = gate_up.project(xd, banks[i % copies], "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(xd, banks[i % copies]["w"])
+                oh.copy_(o, non_blocking=True)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            for xh, oh in zip(xs_host, outs_host):
+                xd = xh.to(dev, non_blocking=True)
+                o = gate_up.project(xd, banks[i % copies], "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(xd, banks[i % copies]["w"])
+                oh.copy_(o, non_blocking=True)
+        e1.record(stream)
+        barrier(world)
+        ems = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+        e2e = {"value": tokens / (ems * 1e-3), "unit": "tokens/s",
+               "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs_cpu),
+               "d2h_bytes_per_step": sum(x.shape[0] * h * 2 for x in xs_cpu)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, threads, sample = cpu_run(args.workload)
+        cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong" if world > 1 else "strong", "vs_baseline": None, "dtype": "s8" if int8 else "bf16",
+                "data": "synthetic (seeded N(0,1) or Student-t activations, uniform int8 / N(0,0.02) bf16 weights)",
+                "config": {"workload": desc, "tokens_per_step": tokens, "K": K, "H": H, "H_per_gpu": h,
+                           "parallelism": f"H-shard x{world}" if world > 1 else "1 GPU",
+                           "l2": f"{copies} rotating weight copies ({copies * 2 * h * K * (1 if int8 else 2) / 1e6:.0f} MB > 126 MB L2)"},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
+                "device_status": status}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def measure_int8_peak():
+    """Dense INT8 tensor throughput reference: torch._int_mm at 8192^3, best of 10 (CUDA events)."""
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = None
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) * 1e-3
+        best = t if best is None else min(best, t)
+    print(json.dumps({"what": "torch._int_mm int8 8192^3 best of 10", "tops": 2 * n ** 3 / best / 1e12,
+                      "seconds": best, "torch": torch.__version__}))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

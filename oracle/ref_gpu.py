@@ -1,0 +1,124 @@
+"""Launch the reference's own kernels (compiled from source into ``oracle/_ref`` by ``build_ref.py``).
+
+TEST INFRASTRUCTURE ONLY: the GPU tests and the bench's reference-kernel leg use this to run the
+reference's gate/up kernels on the same B200 and inputs as ours.  The launch arithmetic restates the
+reference's launch contract:
+
+* ``hybrid8_*`` (reaxv2/gate_up.py:11-27): kernel parameters (A, W, AH, WH, sa, sw, bias, out, M, N, K,
+  KH, mb); mb = max(0, M // bm - drop) * bm; blocks = (mb / bm + ceil((M - mb) / small)) * (N / bn);
+  128 threads for the ``w4`` variant, else 256; dynamic shared memory from the config table.
+* ``slice_*`` (reaxv2/sliced.py:20-47): parameters (A, W, AH, WH, sa, sw, bias, partials, M, N, KL, KH,
+  group, hp, mb), grid (blocks, 1, P), dynamic shared memory read from the ``<name>_required_smem``
+  device global of the module.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from pathlib import Path
+
+import torch
+
+REF = Path(__file__).resolve().parent / "_ref"
+
+# (big rows, small rows, N tile, dynamic shared memory) of the hybrid8_* kernels
+HYBRID = {
+    "hybrid8_b128n256_s64n256": (128, 64, 256, 98304),
+    "hybrid8_b64n256_s32n256": (64, 32, 256, 81920),
+    "hybrid8_b128n128_s32n128": (128, 32, 128, 98304),
+    "hybrid8_b128n256k32_s32n256k32": (128, 32, 256, 73728),
+    "hybrid8_b64n128k64_s32n128k64": (64, 32, 128, 49152),
+    "hybrid8_b64n128k32_s32n128k32": (64, 32, 128, 36864),
+    "hybrid8_b64n128k32_min2": (64, 32, 128, 36864),
+    "hybrid8_b32n128k32w4_min3": (32, 16, 128, 30720),
+}
+# (big rows, small rows, N tile, threads) of the slice_* kernels
+SLICE = {
+    "slice_m128n128": (128, 32, 128, 256),
+    "slice_m64n128": (64, 32, 128, 256),
+    "slice_m64n128w4": (64, 32, 128, 128),
+    "slice_m128n256": (128, 32, 256, 256),
+    "slice_m128n128k64": (128, 32, 128, 256),
+}
+_ATTR_MAX_DYNAMIC_SMEM = 8
+
+
+def available(name: str) -> bool:
+    return (REF / name).exists()
+
+
+class Module:
+    def __init__(self, cubin: str):
+        self.cuda = C.CDLL("libcuda.so.1")
+        torch.cuda.init()
+        torch.zeros(1, device="cuda")              # make torch's primary context current
+        self.image = C.create_string_buffer((REF / cubin).read_bytes())
+        self.module = C.c_void_p()
+        self._check(self.cuda.cuModuleLoadData(C.byref(self.module), self.image))
+        self.functions = {}
+
+    @staticmethod
+    def _check(status):
+        if status:
+            raise RuntimeError(f"CUDA driver status {status}")
+
+    def function(self, name: str, smem: int | None):
+        if name not in self.functions:
+            fn = C.c_void_p()
+            self._check(self.cuda.cuModuleGetFunction(C.byref(fn), self.module, name.encode()))
+            if smem is None:
+                ptr, size, val = C.c_void_p(), C.c_size_t(), C.c_uint()
+                self._check(self.cuda.cuModuleGetGlobal_v2(C.byref(ptr), C.byref(size), self.module,
+                                                           (name + "_required_smem").encode()))
+                self._check(self.cuda.cuMemcpyDtoH_v2(C.byref(val), ptr, 4))
+                smem = val.value
+            self._check(self.cuda.cuFuncSetAttribute(fn, _ATTR_MAX_DYNAMIC_SMEM, smem))
+            self.functions[name] = (fn, smem)
+        return self.functions[name]
+
+    def launch(self, fn, grid, threads, smem, pointers, ints):
+        args = [C.c_void_p(p) for p in pointers] + [C.c_int(v) for v in ints]
+        params = (C.c_void_p * len(args))(*[C.cast(C.pointer(a), C.c_void_p) for a in args])
+        stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        self._check(self.cuda.cuLaunchKernel(fn, grid[0], grid[1], grid[2], threads, 1, 1, smem, stream, params, None))
+
+
+class Hybrid8(Module):
+    """The reference's gate/up kernel (kernel-source/legacy-v2/src/native_hybrid8.cu)."""
+
+    def __init__(self):
+        super().__init__("native_hybrid8.cubin")
+
+    def product(self, x, w, xh, wh, sa, sw, bias, name="hybrid8_b128n256_s64n256", drop=0):
+        m, k = x.shape
+        n = w.shape[0]
+        kh = xh.shape[1]
+        bm, small, bn, shared = HYBRID[name]
+        assert k % 128 == 0 and kh % 64 == 0 and n % bn == 0
+        fn, smem = self.function(name, shared)
+        mb = max(0, m // bm - drop) * bm
+        blocks = (mb // bm + math.ceil((m - mb) / small)) * (n // bn)
+        out = torch.empty((m, n // 2), device=x.device, dtype=torch.bfloat16)
+        self.launch(fn, (blocks, 1, 1), 128 if "w4" in name else 256, smem,
+                    [t.data_ptr() for t in (x, w, xh, wh, sa, sw, bias, out)], [m, n, k, kh, mb])
+        return out
+
+
+class Sliced8(Module):
+    """The reference's grouped projection kernel (kernel-source/legacy-v2/src/sliced_linear8.cu)."""
+
+    def __init__(self):
+        super().__init__("sliced_linear8.cubin")
+
+    def partials(self, low, w, high, wh, scales, sw, bias, group, hp, parts, name="slice_m128n256", drop=0):
+        m, n = low.shape[0], w.shape[0]
+        bm, sm, bn, threads = SLICE[name]
+        assert n % bn == 0
+        fn, smem = self.function(name, None)
+        mb = max(0, m // bm - drop) * bm
+        blocks = (mb // bm + math.ceil((m - mb) / sm)) * (n // bn)
+        out = torch.empty((parts, m, n), device=low.device, dtype=torch.bfloat16)
+        self.launch(fn, (blocks, 1, parts), threads, smem,
+                    [t.data_ptr() for t in (low, w, high, wh, scales, sw, bias, out)],
+                    [m, n, parts * group, parts * hp, group, hp, mb])
+        return out

@@ -43,13 +43,28 @@ def run_project(x, bank, name="hybrid8_b128n256_s64n256"):
 
 
 def compare_int8(x, bank, rows=None, exact=True):
-    out = run_project(x.cuda(), H.bank_to(bank, "cuda"))
+    """GPU project (quantize + gate/up) against the oracle's product of the GPU's own codes and scales.
+
+    The quantizer is checked separately against the oracle (test_gpu_quant.py): its scale division
+    follows Triton's fp32 '/' on the GPU, which differs from the oracle's IEEE division by <= 2 ulps
+    on some rows; feeding the GPU's codes and scales makes every later step comparable bit for bit."""
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import quantize_rows
+    xd, bd = x.cuda(), H.bank_to(bank, "cuda")
+    out = run_project(xd, bd)
+    low, high, scales = quantize_rows(xd, bd)
+    torch.cuda.synchronize()
     nb = H.bank_numpy(bank)
-    xb = H.bits(x)
     sel = np.arange(x.shape[0]) if rows is None else rows
+    low_g, high_g, sc_g = low.cpu().numpy()[sel], H.bits(high)[sel], scales.cpu().numpy()[sel]
+    # quantizer: scales within the 2-ulp bound of the oracle's IEEE scales, codes exact for the GPU scales
+    lo_o, hi_o, sc_o = ro.prepare_rows(H.bits(x)[sel], nb.low_columns, nb.high_columns, nb.smoothing, nb.centers,
+                                       nb.centered)
+    ulps = np.abs(sc_g.view(np.int32).astype(np.int64) - sc_o.view(np.int32).astype(np.int64))
+    assert ulps.max(initial=0) <= 2
+    assert np.array_equal(low_g[ulps == 0], lo_o[ulps == 0]) and np.array_equal(high_g, hi_o)
     got = H.bits(out)[sel]
-    want_t = ro.gate_up_project(xb[sel], nb, table())
-    want_c = ro.gate_up_project(xb[sel], nb)
+    want_t = ro.gate_up_product(low_g, nb.low_weight, high_g, nb.high_weight, sc_g, nb.scales, nb.bias, table())
+    want_c = ro.gate_up_product(low_g, nb.low_weight, high_g, nb.high_weight, sc_g, nb.scales, nb.bias)
     rep_t = H.ulp_report(got, want_t)
     rep_c = H.ulp_report(got, want_c)
     print("vs oracle(GPU silu table):", rep_t, "vs oracle(CPU silu):", rep_c)
@@ -98,13 +113,18 @@ def test_cfg5_outliers():
 
 def test_hybrid_bank_with_outlier_columns():
     """Production-style bank: centred, power-of-two smoothing, bias, 128 BF16 outlier columns."""
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import quantize_rows
     g = H.gen(11)
     x = H.activations(g, 200, 2560)
     bank = H.int8_bank(g, 2560, 1024, KH=128, centered=True, pow2_smoothing=True, bias=True)
-    out = run_project(x.cuda(), H.bank_to(bank, "cuda"))
+    bd = H.bank_to(bank, "cuda")
+    out = run_project(x.cuda(), bd)
+    low, high, scales = quantize_rows(x.cuda(), bd)
+    torch.cuda.synchronize()
     nb = H.bank_numpy(bank)
     got = H.bits(out)
-    want = ro.gate_up_project(H.bits(x), nb, table())
+    want = ro.gate_up_product(low.cpu().numpy(), nb.low_weight, H.bits(high), nb.high_weight, scales.cpu().numpy(),
+                              nb.scales, nb.bias, table())
     d = ro.ulp_distance_bf16(got, want)
     gf, wf = ro.bf16_to_f32(got), ro.bf16_to_f32(want)
     tol = 1e-3 * np.abs(wf).max(axis=1, keepdims=True)

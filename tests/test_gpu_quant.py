@@ -121,3 +121,40 @@ def test_quantizer_is_deterministic_and_batch_invariant():
     a = run_prepare(x, bank)
     b = run_prepare(x[:16].contiguous(), bank)
     assert np.array_equal(a[0][:16], b[0]) and np.array_equal(a[2][:16], b[2])
+
+
+def test_scale_division_is_tritons_fp32_division_exhaustive():
+    """The reference computes the scale as ``tl.maximum(amax, 1e-12) / 127.`` in Triton
+    (reaxv2/quantize.py:19).  With smoothing 1 and no centre, amax is a bf16 value, so all 32768
+    non-negative finite bf16 amax values cover the domain: one row per value, the quantizer's scale
+    must equal Triton's fp32 '/' of the same expression on this GPU bit for bit.  (IEEE division
+    differs on part of the domain; the count is printed.)"""
+    triton = pytest.importorskip("triton")
+    import triton.language as tl
+
+    @triton.jit
+    def scale_expr(a, o, n, B: tl.constexpr):
+        i = tl.program_id(0) * B + tl.arange(0, B)
+        m = i < n
+        v = tl.load(a + i, mask=m, other=1.0)
+        tl.store(o + i, tl.maximum(v, 1.e-12) / 127., mask=m)
+
+    patterns = torch.arange(0, 0x7F80, dtype=torch.int32)        # +0 .. largest finite bf16
+    amax = patterns.to(torch.int16).view(torch.bfloat16)
+    M = amax.numel()
+    x = torch.zeros(M, 8, dtype=torch.bfloat16)
+    x[:, 3] = amax
+    from types import SimpleNamespace
+    dev = torch.device("cuda")
+    bank = SimpleNamespace(width=8, centered=False, low_columns=torch.arange(8, dtype=torch.int32, device=dev),
+                           high_columns=torch.zeros(0, dtype=torch.int32, device=dev),
+                           smoothing=torch.ones(8, device=dev), centers=torch.zeros(8, device=dev))
+    low, high, scales = run_prepare(x.to(dev), bank)
+    a32 = amax.float().to(dev)
+    tri = torch.empty_like(a32)
+    scale_expr[(triton.cdiv(M, 1024),)](a32, tri, M, B=1024, enable_fp_fusion=False)
+    torch.cuda.synchronize()
+    tri = tri.cpu().numpy()
+    assert np.array_equal(scales.view(np.uint32), tri.view(np.uint32))
+    ieee = ro.quant_scale(amax.float().numpy())
+    print(f"scales differing from IEEE division: {int((ieee != tri).sum())} of {M}")
