@@ -20,7 +20,7 @@
 namespace {
 
 constexpr int kVersion = 10000;           // 1.0.0
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;
 constexpr int kStages = 4;
 constexpr int kMaxDevices = 64;
 constexpr size_t kStatusBytes = 256;
@@ -57,12 +57,36 @@ struct DeviceInfo {
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mutex;
 
-template <int EPI>
-void* tc_kernel_ptr() {
-    return reinterpret_cast<void*>(&reax::tc_gemm_kernel<kEpiWarps, kStages, EPI>);
+// The kernel variants: (epilogue, mode, BF16 columns added to INT8 accumulators).
+enum Variant : int {
+    kSwigluI8 = 0, kSwigluI8F, kSwigluBf16, kPlainI8, kPlainI8F, kPlainBf16, kSwapI8, kSwapBf16, kVariants
+};
+
+// Activation rows up to which the gate/up kernels use weight-major (swap) tiles.
+constexpr int kSwapMaxRows = 64;
+
+void* tc_kernel_ptr(int v) {
+    using namespace reax;
+    switch (v) {
+        case kSwigluI8: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 0, false, false>);
+        case kSwigluI8F: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 0, true, false>);
+        case kSwigluBf16: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 1, false, false>);
+        case kPlainI8: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiPlain, 0, false, false>);
+        case kPlainI8F: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiPlain, 0, true, false>);
+        case kPlainBf16: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiPlain, 1, false, false>);
+        case kSwapI8: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 0, false, true>);
+        default: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 1, false, true>);
+    }
 }
 
-constexpr size_t tc_smem_bytes() { return static_cast<size_t>(kStages) * reax::kStageBytes + 1024 + 256; }
+int variant_of(int epi, const reax::TcParams& p) {
+    if (p.n_tok > 0) return p.mode == 1 ? kSwapBf16 : kSwapI8;
+    if (epi == reax::kEpiSwiglu) return p.mode == 1 ? kSwigluBf16 : (p.kb_f16 > 0 ? kSwigluI8F : kSwigluI8);
+    return p.mode == 1 ? kPlainBf16 : (p.kb_f16 > 0 ? kPlainI8F : kPlainI8);
+}
+
+// pipeline stages + 1 KiB alignment slack + staged column scales/biases (2 x 2 x 256 floats) + barriers
+constexpr size_t tc_smem_bytes() { return static_cast<size_t>(kStages) * reax::kStageBytes + 1024 + 4096 + 256; }
 
 // Current device, its SM count, and a check that it is sm_100; sets kernel attributes once.
 int current_device(int* dev_out, DeviceInfo** info_out) {
@@ -86,12 +110,10 @@ int current_device(int* dev_out, DeviceInfo** info_out) {
                     d.minor);
     if (!d.smem_set) {
         const int bytes = static_cast<int>(tc_smem_bytes());
-        if ((e = cudaFuncSetAttribute(tc_kernel_ptr<reax::kEpiSwiglu>(), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      bytes)) != cudaSuccess)
-            return cuda_fail(e, "cudaFuncSetAttribute(swiglu kernel smem)");
-        if ((e = cudaFuncSetAttribute(tc_kernel_ptr<reax::kEpiPlain>(), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      bytes)) != cudaSuccess)
-            return cuda_fail(e, "cudaFuncSetAttribute(plain kernel smem)");
+        for (int v = 0; v < kVariants; ++v)
+            if ((e = cudaFuncSetAttribute(tc_kernel_ptr(v), cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)) !=
+                cudaSuccess)
+                return cuda_fail(e, "cudaFuncSetAttribute(tcgen05 kernel smem)");
         d.smem_set = true;
     }
     *dev_out = dev;
@@ -120,16 +142,16 @@ int get_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
     return REAX_OK;
 }
 
-// 2-D map of a row-major [rows, inner] tensor, box = 128 bytes of the inner dimension x 128 rows,
+// 2-D map of a row-major [rows, inner] tensor, box = 128 bytes of the inner dimension x box_rows rows,
 // 128-byte swizzle, zero fill out of bounds.
 int make_map(CUtensorMap* map, CUtensorMapDataType dt, size_t elem, const void* base, uint64_t inner, uint64_t rows,
-             uint64_t row_stride_elems) {
+             uint64_t row_stride_elems, uint32_t box_rows = 128) {
     PFN_cuTensorMapEncodeTiled_v12000 enc;
     int rc = get_encoder(&enc);
     if (rc != REAX_OK) return rc;
     cuuint64_t dims[2] = {inner, rows};
     cuuint64_t strides[1] = {row_stride_elems * elem};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(reax::kRowBytes / elem), 128};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(reax::kRowBytes / elem), box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -199,11 +221,8 @@ int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e;
-    if (epi == reax::kEpiSwiglu)
-        e = cudaLaunchKernelEx(&cfg, reax::tc_gemm_kernel<kEpiWarps, kStages, reax::kEpiSwiglu>, p);
-    else
-        e = cudaLaunchKernelEx(&cfg, reax::tc_gemm_kernel<kEpiWarps, kStages, reax::kEpiPlain>, p);
+    void* args[1] = {const_cast<reax::TcParams*>(&p)};
+    cudaError_t e = cudaLaunchKernelExC(&cfg, tc_kernel_ptr(variant_of(epi, p)), args);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
     return REAX_OK;
 }
@@ -385,8 +404,12 @@ int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, const void
 
     reax::TcParams p;
     init_params(p);
+    // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
+    const bool swap = KH == 0 && M <= kSwapMaxRows;
+    p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
     if (KL) {
-        if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
+            return rc;
         if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL)) != REAX_OK) return rc;
     }
     if (KH) {
@@ -442,7 +465,10 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
     reax::TcParams p;
     init_params(p);
-    if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K)) != REAX_OK) return rc;
+    const bool swap = M <= kSwapMaxRows;
+    p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
+    if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : 128)) != REAX_OK)
+        return rc;
     if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K)) != REAX_OK) return rc;
     p.tm_a = p.tm_ah;
     p.tm_b = p.tm_bh;

@@ -189,6 +189,28 @@ REAX_DEVI void tmem_ld_x32_sync(uint32_t taddr, uint32_t (&r)[32]) {
         : "memory");
 }
 
+// 32 lanes x 8 columns, with the wait in the same asm block.
+REAX_DEVI void tmem_ld_x8_sync(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+}
+
+// Two 8-column loads and one wait.
+REAX_DEVI void tmem_ld_x8_pair_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[8], uint32_t (&b)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%16];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%17];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]),
+          "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7])
+        : "r"(ta), "r"(tb)
+        : "memory");
+}
+
 // Two 32-column loads (e.g. the gate and the up half of one output chunk) and one wait.
 REAX_DEVI void tmem_ld2_x32_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[32], uint32_t (&b)[32]) {
     asm volatile(
@@ -225,8 +247,142 @@ REAX_DEVI float bf16_round(float v) { return __bfloat162float(__float2bfloat16_r
 // float32: the arithmetic of the reference's silu_f32 (hybrid8_tiles.cuh:675).
 REAX_DEVI float silu_f32(float x) { return __fdiv_rn(x, 1.0f + expf(-x)); }
 
+// bf16(silu_f32(x)), bit-identical to rounding the accurate formula above, at a fraction of its cost.
+//
+// Ziv's rounding test.  A cheap approximation s ~ x * rcp(1 + 2^(-x log2 e)) is formed with the
+// hardware ex2 / rcp approximations; -x log2 e is carried as an unevaluated pair t_hi + t_lo (FMA-exact
+// product plus the constant's residual), so the approximation error is essentially that of ex2, rcp
+// and three roundings: about 2^-21 relative, i.e. <= 16 float32 ulps of s.  The accurate formula (CUDA
+// expf <= 2 ulp, two IEEE-rounded ops) is within about 2^-21.4 of silu(x) too, so both round to the
+// same bf16 value unless s lies within kSiluMargin ulps of a bf16 rounding midpoint (low 16 bits
+// 0x8000).  Then, and outside the fast domain, the accurate formula is evaluated.  Two saturated ends
+// are exact without evaluating it: for x >= 17, expf(-x) < 2^-24 so 1 + expf(-x) rounds to 1 and the
+// quotient is x; for x <= -89, expf(-x) overflows to +inf and x / inf = -0.
+// Only bf16 inputs reach this function; the 65536-pattern domain test checks every one of them.
+constexpr uint32_t kSiluMargin = 32;   // float32 ulps, about twice the error bound above
+
+REAX_DEVI float silu_bf16_value(float x) {
+    constexpr float kNegLog2eHi = -1.44269502162933349609375f;          // float32(-log2 e)
+    constexpr float kNegLog2eLo = -1.925963033500011079e-08f;           // -log2 e - kNegLog2eHi
+    constexpr float kLn2 = 0.693147180559945309f;
+    if (x >= 17.0f && x <= 3.402823466e38f) return x;
+    if (x > -86.0f && x < 17.0f) {
+        const float t_hi = __fmul_rn(x, kNegLog2eHi);
+        const float t_lo = __fmaf_rn(x, kNegLog2eHi, -t_hi) + x * kNegLog2eLo;   // exact product residual
+        float e, r;
+        asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(t_hi));
+        e = __fmaf_rn(e, t_lo * kLn2, e);                                     // 2^t_lo ~ 1 + t_lo ln 2
+        const float d = __fadd_rn(1.0f, e);
+        asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(d));
+        const float s = __fmul_rn(x, r);
+        const uint32_t low = __float_as_uint(s) & 0xFFFFu;
+        const uint32_t dist = low > 0x8000u ? low - 0x8000u : 0x8000u - low;
+        if (dist > kSiluMargin) return bf16_round(s);
+    } else if (x <= -89.0f && x >= -3.402823466e38f) {
+        return -0.0f;
+    }
+    return bf16_round(silu_f32(x));
+}
+
 // out = bf16(float(bf16(silu_f32(g))) * u) for bf16-valued g and u (hybrid8_tiles.cuh:676-679).
 REAX_DEVI __nv_bfloat16 swiglu_bf16(float g_bf16_value, float u_bf16_value) {
+    return __float2bfloat16_rn(silu_bf16_value(g_bf16_value) * u_bf16_value);
+}
+
+// ------------------------------------------------------------------------------------- packed float32 pairs
+// sm_100 executes two float32 lanes per instruction (add/mul/fma .rn.f32x2); each lane is rounded
+// exactly like the scalar IEEE op, so packed arithmetic keeps every result bit-identical.
+REAX_DEVI uint64_t f2(float lo, float hi) {
+    return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+REAX_DEVI float f2_lo(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+REAX_DEVI float f2_hi(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+REAX_DEVI uint64_t mul2_rn(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+REAX_DEVI uint64_t add2_rn(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+REAX_DEVI uint64_t fma2_rn(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+// two float32 -> packed bf16x2 (round to nearest even), low lane first
+REAX_DEVI uint32_t bf16x2_rn(uint64_t v) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(f2_lo(v), f2_hi(v));
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// packed bf16x2 -> the two values as a float32 pair (exact)
+REAX_DEVI uint64_t bf16x2_to_f2(uint32_t w) { return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u)); }
+
+// INT8 dequant of two accumulators, lane-wise ((acc * sa) * sw) + bias with three IEEE roundings.
+// Only the first product is packed: ptxas contracts a packed mul.rn.f32x2 feeding a packed
+// add.rn.f32x2 into one fused multiply-add (measured on sm_100a with CUDA 12.9), which would round
+// (t * sw + bias) once instead of twice; the scalar mul.rn / add.rn pair is never contracted.
+REAX_DEVI uint64_t dequant2(uint32_t a0, uint32_t a1, uint64_t sa2, uint64_t sw2, uint64_t b2) {
+    const uint64_t raw = f2(__int2float_rn(static_cast<int>(a0)), __int2float_rn(static_cast<int>(a1)));
+    const uint64_t t = mul2_rn(raw, sa2);
+    const float v0 = __fadd_rn(__fmul_rn(f2_lo(t), f2_lo(sw2)), f2_lo(b2));
+    const float v1 = __fadd_rn(__fmul_rn(f2_hi(t), f2_hi(sw2)), f2_hi(b2));
+    return f2(v0, v1);
+}
+
+// Scalar entry of the exact pair path below, kept out of line so the unrolled epilogue stays small.
+__device__ __noinline__ float silu_bf16_value_slow(float x) { return silu_bf16_value(x); }
+
+// bf16(silu_f32(x)) for two bf16-valued inputs, as a float32 pair; bit-identical to silu_bf16_value.
+// Classes per lane: x >= 17 -> x; -inf < x <= -89 -> -0; -86 < x < 17 -> the approximation, accepted
+// when it passes the rounding test; anything else (NaN, +-inf, (-89, -86], a failed test) sends the
+// pair through silu_bf16_value.
+REAX_DEVI uint64_t silu2_bf16(float x0, float x1) {
+    constexpr float kNegLog2eHi = -1.44269502162933349609375f;
+    constexpr float kNegLog2eLo = -1.925963033500011079e-08f;
+    constexpr float kLn2 = 0.693147180559945309f;
+    const uint64_t x2 = f2(fminf(fmaxf(x0, -86.0f), 17.0f), fminf(fmaxf(x1, -86.0f), 17.0f));
+    const uint64_t c_hi = f2(kNegLog2eHi, kNegLog2eHi);
+    const uint64_t t_hi = mul2_rn(x2, c_hi);
+    const uint64_t resid = fma2_rn(x2, c_hi, t_hi ^ 0x8000000080000000ull);       // x*C - t_hi, exact
+    const uint64_t t_lo = fma2_rn(x2, f2(kNegLog2eLo, kNegLog2eLo), resid);
+    float e0, e1, r0, r1;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(f2_lo(t_hi)));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(f2_hi(t_hi)));
+    uint64_t e2 = f2(e0, e1);
+    e2 = fma2_rn(e2, mul2_rn(t_lo, f2(kLn2, kLn2)), e2);
+    const uint64_t d2 = add2_rn(f2(1.0f, 1.0f), e2);
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(f2_lo(d2)));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(f2_hi(d2)));
+    const uint64_t s2 = mul2_rn(x2, f2(r0, r1));
+    const uint32_t b0 = static_cast<uint32_t>(s2), b1 = static_cast<uint32_t>(s2 >> 32);
+    // rounding test: |low 16 bits - 0x8000| > margin  <=>  ((bits - (0x8000 - margin)) & 0xFFFF) > 2 margin
+    const bool near0 = ((b0 - (0x8000u - kSiluMargin)) & 0xFFFFu) <= 2 * kSiluMargin;
+    const bool near1 = ((b1 - (0x8000u - kSiluMargin)) & 0xFFFFu) <= 2 * kSiluMargin;
+    const bool hi0 = x0 >= 17.0f, hi1 = x1 >= 17.0f;
+    const bool lo0 = x0 <= -89.0f && x0 > -INFINITY, lo1 = x1 <= -89.0f && x1 > -INFINITY;
+    const bool mid0 = x0 > -86.0f && x0 < 17.0f && !near0, mid1 = x1 > -86.0f && x1 < 17.0f && !near1;
+    float s0 = hi0 ? x0 : (lo0 ? -0.0f : __uint_as_float(b0));
+    float s1 = hi1 ? x1 : (lo1 ? -0.0f : __uint_as_float(b1));
+    uint32_t w = bf16x2_rn(f2(s0, s1));
+    if (!((hi0 || lo0 || mid0) && (hi1 || lo1 || mid1))) {
+        w = bf16x2_rn(f2(silu_bf16_value_slow(x0), silu_bf16_value_slow(x1)));
+    }
+    return bf16x2_to_f2(w);
+}
+
+// SwiGLU of two (gate, up) float32 pairs: bf16x2 of bf16(bf16(silu(bf16(g))) * bf16(u)).
+REAX_DEVI uint32_t swiglu2(uint64_t vg2, uint64_t vu2) {
+    const uint64_t g2 = bf16x2_to_f2(bf16x2_rn(vg2));
+    const uint64_t u2 = bf16x2_to_f2(bf16x2_rn(vu2));
+    const uint64_t s2 = silu2_bf16(f2_lo(g2), f2_hi(g2));
+    return bf16x2_rn(mul2_rn(s2, u2));
+}
+
+// The same value through the accurate formula only (the domain reference for the test above).
+REAX_DEVI __nv_bfloat16 swiglu_bf16_accurate(float g_bf16_value, float u_bf16_value) {
     const float s = bf16_round(silu_f32(g_bf16_value));
     return __float2bfloat16_rn(s * u_bf16_value);
 }

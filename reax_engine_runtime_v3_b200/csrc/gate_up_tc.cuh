@@ -68,6 +68,7 @@ struct TcParams {
     unsigned* status;    // OR-ed error bits (kStatus*)
     unsigned long long timeout_ns;
     int evict_first_b;   // stream B with an evict-first L2 policy (weights read once)
+    int n_tok;           // weight-major (swap) kernels: token columns per accumulator, a multiple of 16 >= M
     // Mixed-origin slicing (BF16 partials): parts = P0 + P1 and part z < P0 is slice z of plan 0 (rows
     // < *split), part z >= P0 is slice z - P0 of plan 1 (rows >= *split).  Slice s of a plan covers K
     // blocks [s * chunk_kb, (s + 1) * chunk_kb) clipped to the K extent; its output part is s.
@@ -198,13 +199,91 @@ REAX_DEVI float dequant1(uint32_t acc_bits, float sa_row, float sw_col, float bi
     return __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(acc_bits)), sa_row), sw_col), bias_col);
 }
 
-template <int EPI_WARPS, int STAGES, int EPI>
+// Split-tile helper shared by both epilogues: publish this CTA's int32 partial of accumulator columns
+// [c_lo, c_hi) (and [c_lo + pair_off, c_hi + pair_off) when pair_off > 0: the up half of a SwiGLU
+// tile), valid lanes only, then learn whether this CTA completes the tile.  W = columns per TMEM load.
+template <int EPI_WARPS, int W>
+REAX_DEVI bool publish_partial(const TcParams& p, const Segment& seg, int st, uint32_t t_acc, int c_lo, int c_hi,
+                               int pair_off, int lane_row, bool lane_ok, int* last_flag) {
+    const int KB = p.kb_int + p.kb_f16;
+    int4* slot = reinterpret_cast<int4*>(p.ws_partials +
+                                         (static_cast<size_t>(blockIdx.x) * 2 + sk_slot(p, blockIdx.x, st)) * kSlotInts);
+    for (int h = 0; h < (pair_off > 0 ? 2 : 1); ++h) {
+        const int off = h * pair_off;
+        for (int cc = c_lo + off; cc < c_hi + off; cc += W) {
+            uint32_t a[W];
+            if constexpr (W == 32) tmem_ld_x32_sync(t_acc + cc, a);
+            else tmem_ld_x8_sync(t_acc + cc, a);
+            if (lane_ok) {
+#pragma unroll
+                for (int i = 0; i < W; i += 4)
+                    __stcg(slot + ((cc + i) / 4) * kBM + lane_row, make_int4(a[i], a[i + 1], a[i + 2], a[i + 3]));
+            }
+        }
+    }
+    __threadfence();
+    named_bar_sync(1, EPI_WARPS * 32);
+    if (threadIdx.x == 64) {
+        const int n = seg.k1 - seg.k0;
+        const int old = atomicAdd(p.ws_counters + st, n);
+        *last_flag = (old + n == KB) ? 1 : 0;
+    }
+    named_bar_sync(1, EPI_WARPS * 32);
+    const bool finish = *reinterpret_cast<volatile int*>(last_flag) != 0;
+    if (finish) __threadfence();
+    return finish;
+}
+
+// Slots of a split tile's other contributors (CTA order), resolved once per tile.
+constexpr int kMaxContrib = 8;
+REAX_DEVI int contributors(const TcParams& p, int st, const int4* (&contrib)[kMaxContrib]) {
+    const int KB = p.kb_int + p.kb_f16;
+    const int c_first = sk_owner(p, static_cast<long long>(st) * KB);
+    const int c_last = sk_owner(p, static_cast<long long>(st + 1) * KB - 1);
+    int n = 0;
+    for (int c = c_first; c <= c_last && n < kMaxContrib; ++c) {
+        if (c == static_cast<int>(blockIdx.x)) continue;
+        if (sk_begin(p, c + 1) <= sk_begin(p, c)) continue;
+        contrib[n++] = reinterpret_cast<const int4*>(p.ws_partials +
+                                                      (static_cast<size_t>(c) * 2 + sk_slot(p, c, st)) * kSlotInts);
+    }
+    return n;
+}
+
+// Add the other contributors' partials of accumulator columns [col, col + W) to a[].
+template <int W>
+REAX_DEVI void add_partials(const int4* const (&contrib)[kMaxContrib], int n, int col, int lane_row, uint32_t (&a)[W]) {
+    for (int ci = 0; ci < n; ++ci) {
+#pragma unroll
+        for (int i = 0; i < W; i += 4) {
+            const int4 v = __ldcg(contrib[ci] + ((col + i) / 4) * kBM + lane_row);
+            a[i] += v.x;
+            a[i + 1] += v.y;
+            a[i + 2] += v.z;
+            a[i + 3] += v.w;
+        }
+    }
+}
+
+// MODE 0: INT8 accumulators with dequant (ADD_F: plus a float32 region of BF16 columns);
+// MODE 1: float32 accumulators of BF16 operands.  p.mode / p.kb_f16 must agree with the template.
+// SWAP: weight-major tiles for small M (SwiGLU only, no BF16 column region): the 128 gate rows and the
+// 128 up rows of the tile are the A operands of two MMAs (M=128, N=n_tok) whose B operand is the
+// activation tile (n_tok token rows); TMEM lanes are weight rows, columns [0, n_tok) gate and
+// [n_tok, 2 n_tok) up, one column per token.  Every TMEM lane quarter then holds real rows even when
+// only a few tokens exist, so all four SM sub-partitions share the epilogue.
+template <int EPI_WARPS, int STAGES, int EPI, int MODE, bool ADD_F, bool SWAP>
 __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    static_assert(!SWAP || (EPI == kEpiSwiglu && !ADD_F), "weight-major tiles: SwiGLU without BF16 columns");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage_a = smem;
     uint8_t* stage_b = smem + STAGES * kAStage;
-    uint64_t* full = reinterpret_cast<uint64_t*>(stage_b + STAGES * kBStage);
+    // per accumulator buffer: the tile's per-column scale and bias (token-major) or per-token scale
+    // (weight-major), staged before the accumulator is ready
+    float* stage_sw = reinterpret_cast<float*>(stage_b + STAGES * kBStage);   // [2][kBN]
+    float* stage_bias = stage_sw + 2 * kBN;                                    // [2][kBN]
+    uint64_t* full = reinterpret_cast<uint64_t*>(stage_bias + 2 * kBN);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 2;
@@ -250,6 +329,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
     // (programmatic dependent launch): everything above overlapped that kernel's tail.
     grid_dependency_wait();
     const int split = p.slice_mode ? min(max(__ldg(p.split), 0), p.M) : 0;
+    // bytes a stage receives: weight-major tiles load n_tok activation rows instead of 128
+    const uint32_t stage_tx = SWAP ? static_cast<uint32_t>(kBStage + p.n_tok * kRowBytes) : kStageBytes;
 
     if (warp == 0) {
         // ------------------------------------------------------------------------------ TMA producer
@@ -275,7 +356,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                    mbar_arrive_expect_tx(&full[stage], stage_tx);
                     uint8_t* sa_ = stage_a + stage * kAStage;
                     uint8_t* sb_ = stage_b + stage * kBStage;
                     if (kb < p.kb_int) {
@@ -309,8 +390,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
     } else if (warp == 1) {
         // ------------------------------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            const uint32_t idesc_i8 = idesc_i8_s32(kBM, kBN);
-            const uint32_t idesc_f16 = idesc_bf16_f32(kBM, kBN);
+            const uint32_t idesc_i8 = SWAP ? idesc_i8_s32(kBM, p.n_tok) : idesc_i8_s32(kBM, kBN);
+            const uint32_t idesc_f16 = SWAP ? idesc_bf16_f32(kBM, p.n_tok) : idesc_bf16_f32(kBM, kBN);
             int stage = 0;
             uint32_t phase = 0;
             int buf = 0;
@@ -325,7 +406,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
                 }
                 tc_fence_after();
                 const uint32_t d_int = tmem_base + buf * kBN;
-                const uint32_t d_f32 = (p.mode == 1) ? tmem_base + buf * kBN : tmem_base + kBN;
+                const uint32_t d_f32 = (MODE == 1) ? tmem_base + buf * kBN : tmem_base + kBN;
                 const int first_f = max(seg.k0, p.kb_int);
                 for (int kb = seg.k0; kb < seg.k1; ++kb) {
                     if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns, vabort)) {
@@ -336,14 +417,29 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
                     tc_fence_after();
                     const uint64_t ad = sw128_kmajor_desc(smem_u32(stage_a + stage * kAStage));
                     const uint64_t bd = sw128_kmajor_desc(smem_u32(stage_b + stage * kBStage));
+                    const uint64_t bd_up = sw128_kmajor_desc(smem_u32(stage_b + stage * kBStage + kBStage / 2));
                     if (kb < p.kb_int) {
 #pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            umma_i8(d_int, ad + 2 * k, bd + 2 * k, idesc_i8, (kb > seg.k0 || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < 4; ++k) {
+                            const uint32_t acc = (kb > seg.k0 || k > 0) ? 1u : 0u;
+                            if constexpr (SWAP) {
+                                umma_i8(d_int, bd + 2 * k, ad + 2 * k, idesc_i8, acc);
+                                umma_i8(d_int + p.n_tok, bd_up + 2 * k, ad + 2 * k, idesc_i8, acc);
+                            } else {
+                                umma_i8(d_int, ad + 2 * k, bd + 2 * k, idesc_i8, acc);
+                            }
+                        }
                     } else {
 #pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            umma_f16(d_f32, ad + 2 * k, bd + 2 * k, idesc_f16, (kb > first_f || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < 4; ++k) {
+                            const uint32_t acc = (kb > first_f || k > 0) ? 1u : 0u;
+                            if constexpr (SWAP) {
+                                umma_f16(d_f32, bd + 2 * k, ad + 2 * k, idesc_f16, acc);
+                                umma_f16(d_f32 + p.n_tok, bd_up + 2 * k, ad + 2 * k, idesc_f16, acc);
+                            } else {
+                                umma_f16(d_f32, ad + 2 * k, bd + 2 * k, idesc_f16, acc);
+                            }
+                        }
                     }
                     umma_commit(&empty[stage]);
                     if (++stage == STAGES) {
@@ -368,14 +464,11 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
     } else {
         // --------------------------------------------------------------------------------- epilogue
         // Epilogue warps only ever stop at the accumulator wait, and only on its own timeout (no abort
-        // flag), so either all of them pass a segment or none does: the named barriers below stay matched.
+        // flag), so either all of them pass a segment or none does: the named barriers stay matched.
         const int e = warp - 2;
         const int q = warp & 3;                      // TMEM lane quarter this warp may access
         const int r_tile = q * 32 + lane;            // accumulator row (= TMEM lane) of this thread
-        constexpr int kCols = (EPI == kEpiSwiglu) ? kBN / 2 : kBN;   // output columns of a tile
         constexpr int kSplit = EPI_WARPS / 4;        // warps sharing one lane quarter split the columns
-        const int c_lo = (e / 4) * (kCols / kSplit);
-        const int c_hi = c_lo + kCols / kSplit;
         const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
         int buf = 0;
         uint32_t acc_phase = 0;
@@ -385,175 +478,180 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
             int part, mt, nt;
             tile_coords(p, seg.tile, part, mt, nt);
             const int m0 = mt * kBM;
-            if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
-                raise_error(p, abort_flag, kStatusTimeoutAccFull);
-                break;
-            }
-            tc_fence_after();
             int row_lo, row_hi, out_part;
             tile_plan(p, part, split, row_lo, row_hi, out_part);
-            const int grow = m0 + r_tile;
-            const bool row_ok = grow >= row_lo && grow < row_hi;
-            const uint32_t t_int = tmem_base + buf * kBN + lane_off;
-            const uint32_t t_f32 = ((p.mode == 1) ? tmem_base + buf * kBN : tmem_base + kBN) + lane_off;
+            float* s_sw = stage_sw + buf * kBN;
+            float* s_bias = stage_bias + buf * kBN;
             const bool whole = seg.whole;
-
-            // Split tile: publish this CTA's int32 partial, then find out whether it completes the tile.
-            bool finish = whole;
             const int st = seg.tile - p.dp_tiles;
-            if (!whole) {
-                int4* slot = reinterpret_cast<int4*>(
-                    p.ws_partials + (static_cast<size_t>(blockIdx.x) * 2 + sk_slot(p, blockIdx.x, st)) * kSlotInts);
-                for (int cc = c_lo; cc < c_hi; cc += 32) {
-                    uint32_t a[32];
-                    tmem_ld_x32_sync(t_int + cc, a);
-                    if (row_ok) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4)
-                            __stcg(slot + ((cc + i) / 4) * kBM + r_tile, make_int4(a[i], a[i + 1], a[i + 2], a[i + 3]));
-                    }
-                    if (EPI == kEpiSwiglu) {
-                        tmem_ld_x32_sync(t_int + kBN / 2 + cc, a);
-                        if (row_ok) {
-#pragma unroll
-                            for (int i = 0; i < 32; i += 4)
-                                __stcg(slot + ((kBN / 2 + cc + i) / 4) * kBM + r_tile,
-                                       make_int4(a[i], a[i + 1], a[i + 2], a[i + 3]));
-                        }
-                    }
-                }
-                __threadfence();
-                named_bar_sync(1, EPI_WARPS * 32);
-                if (threadIdx.x == 64) {
-                    const int n = seg.k1 - seg.k0;
-                    const int old = atomicAdd(p.ws_counters + st, n);
-                    *last_flag = (old + n == KB) ? 1 : 0;
-                }
-                named_bar_sync(1, EPI_WARPS * 32);
-                finish = *reinterpret_cast<volatile int*>(last_flag) != 0;
-                if (finish) __threadfence();
-            }
+            const uint32_t t_int = tmem_base + buf * kBN + lane_off;
+            const uint32_t t_f32 = ((MODE == 1) ? tmem_base + buf * kBN : tmem_base + kBN) + lane_off;
+            const uint32_t t_acc = (MODE == 0) ? t_int : t_f32;
 
-            if (finish) {
-                // Contributors of a split tile other than this CTA, in CTA order.
-                int c_first = 0, c_last = -1;
-                if (!whole) {
-                    c_first = sk_owner(p, static_cast<long long>(st) * KB);
-                    c_last = sk_owner(p, static_cast<long long>(st + 1) * KB - 1);
-                }
-                const float sa_row = (p.mode == 0 && row_ok) ? p.sa[part * p.sa_part_stride + grow] : 0.f;
-                const bool add_f = (p.mode == 0 && p.kb_f16 > 0);
-                const uint32_t t_acc = (p.mode == 0) ? t_int : t_f32;
-                for (int cc = c_lo; cc < c_hi; cc += 32) {
-                    uint32_t g[32];
-                    uint32_t u[32];
-                    uint32_t fg[32];
-                    uint32_t fu[32];
-                    if (EPI == kEpiSwiglu) {
-                        tmem_ld2_x32_sync(t_acc + cc, t_acc + kBN / 2 + cc, g, u);
-                        if (add_f) tmem_ld2_x32_sync(t_f32 + cc, t_f32 + kBN / 2 + cc, fg, fu);
-                    } else {
-                        tmem_ld_x32_sync(t_acc + cc, g);
-                        if (add_f) tmem_ld_x32_sync(t_f32 + cc, fg);
-                    }
-                    if (!row_ok) continue;
-                    if (!whole) {
-                        for (int c = c_first; c <= c_last; ++c) {
-                            if (c == static_cast<int>(blockIdx.x)) continue;
-                            if (sk_begin(p, c + 1) <= sk_begin(p, c)) continue;
-                            const int4* slot = reinterpret_cast<const int4*>(
-                                p.ws_partials + (static_cast<size_t>(c) * 2 + sk_slot(p, c, st)) * kSlotInts);
-#pragma unroll
-                            for (int i = 0; i < 32; i += 4) {
-                                const int4 v = __ldcg(slot + ((cc + i) / 4) * kBM + r_tile);
-                                g[i] += v.x; g[i + 1] += v.y; g[i + 2] += v.z; g[i + 3] += v.w;
-                            }
-                            if (EPI == kEpiSwiglu) {
-#pragma unroll
-                                for (int i = 0; i < 32; i += 4) {
-                                    const int4 v = __ldcg(slot + ((kBN / 2 + cc + i) / 4) * kBM + r_tile);
-                                    u[i] += v.x; u[i + 1] += v.y; u[i + 2] += v.z; u[i + 3] += v.w;
-                                }
-                            }
-                        }
-                    }
-                    uint32_t packed[16];
-                    __nv_bfloat16* dst;
-                    if (EPI == kEpiSwiglu) {
-                        const int n0 = nt * (kBN / 2);
-                        const int colg = part * p.n_part_stride + n0 + cc;
-                        const int colu = colg + p.H;
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            float vg[4], vu[4];
-                            if (p.mode == 0) {
-                                const float4 swg = __ldg(reinterpret_cast<const float4*>(p.sw + colg + i));
-                                const float4 swu = __ldg(reinterpret_cast<const float4*>(p.sw + colu + i));
-                                const float4 bg = __ldg(reinterpret_cast<const float4*>(p.bias + colg + i));
-                                const float4 bu = __ldg(reinterpret_cast<const float4*>(p.bias + colu + i));
-                                vg[0] = dequant1(g[i], sa_row, swg.x, bg.x);
-                                vg[1] = dequant1(g[i + 1], sa_row, swg.y, bg.y);
-                                vg[2] = dequant1(g[i + 2], sa_row, swg.z, bg.z);
-                                vg[3] = dequant1(g[i + 3], sa_row, swg.w, bg.w);
-                                vu[0] = dequant1(u[i], sa_row, swu.x, bu.x);
-                                vu[1] = dequant1(u[i + 1], sa_row, swu.y, bu.y);
-                                vu[2] = dequant1(u[i + 2], sa_row, swu.z, bu.z);
-                                vu[3] = dequant1(u[i + 3], sa_row, swu.w, bu.w);
-                                if (add_f) {
-#pragma unroll
-                                    for (int j = 0; j < 4; ++j) {
-                                        vg[j] = __fadd_rn(vg[j], __uint_as_float(fg[i + j]));
-                                        vu[j] = __fadd_rn(vu[j], __uint_as_float(fu[i + j]));
-                                    }
-                                }
-                            } else {
-#pragma unroll
-                                for (int j = 0; j < 4; ++j) {
-                                    vg[j] = __uint_as_float(g[i + j]);
-                                    vu[j] = __uint_as_float(u[i + j]);
-                                }
-                            }
-                            __nv_bfloat16 o[4];
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) o[j] = swiglu_bf16(bf16_round(vg[j]), bf16_round(vu[j]));
-                            packed[i / 2] = pack_bf16x2(o[0], o[1]);
-                            packed[i / 2 + 1] = pack_bf16x2(o[2], o[3]);
-                        }
-                        dst = p.out + static_cast<size_t>(grow) * p.ldo + n0 + cc;
-                    } else {
-                        const int n0 = nt * kBN;
-                        const int col = part * p.n_part_stride + n0 + cc;
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            float v[4];
-                            if (p.mode == 0) {
-                                const float4 s4 = __ldg(reinterpret_cast<const float4*>(p.sw + col + i));
-                                const float4 b4 = __ldg(reinterpret_cast<const float4*>(p.bias + col + i));
-                                v[0] = dequant1(g[i], sa_row, s4.x, b4.x);
-                                v[1] = dequant1(g[i + 1], sa_row, s4.y, b4.y);
-                                v[2] = dequant1(g[i + 2], sa_row, s4.z, b4.z);
-                                v[3] = dequant1(g[i + 3], sa_row, s4.w, b4.w);
-                                if (add_f) {
-#pragma unroll
-                                    for (int j = 0; j < 4; ++j) v[j] = __fadd_rn(v[j], __uint_as_float(fg[i + j]));
-                                }
-                            } else {
-#pragma unroll
-                                for (int j = 0; j < 4; ++j) v[j] = __uint_as_float(g[i + j]);
-                            }
-                            packed[i / 2] = pack_bf16x2(__float2bfloat16_rn(v[0]), __float2bfloat16_rn(v[1]));
-                            packed[i / 2 + 1] = pack_bf16x2(__float2bfloat16_rn(v[2]), __float2bfloat16_rn(v[3]));
-                        }
-                        dst = p.out + out_part * p.out_part_stride + static_cast<size_t>(grow) * p.ldo + n0 + cc;
-                    }
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        reinterpret_cast<uint4*>(dst)[i] =
-                            make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-                }
-                if (!whole) {
+            if constexpr (SWAP) {
+                // ---------------------------------------------- weight-major tile: lanes are weight rows
+                const int n_tok = p.n_tok;
+                const int n0 = nt * (kBN / 2);                 // gate row (= output column) of lane 0
+                const int j = n0 + r_tile;                     // this thread's output column
+                const int tok_lo = (e / 4) * (n_tok / kSplit), tok_hi = tok_lo + n_tok / kSplit;
+                float swg = 0.f, swu = 0.f, bg = 0.f, bu = 0.f;
+                if constexpr (MODE == 0) {
+                    swg = __ldg(p.sw + j);
+                    swu = __ldg(p.sw + p.H + j);
+                    bg = __ldg(p.bias + j);
+                    bu = __ldg(p.bias + p.H + j);
+                    for (int t = threadIdx.x - 64; t < n_tok; t += EPI_WARPS * 32)
+                        s_sw[t] = t < p.M ? __ldg(p.sa + t) : 0.f;
                     named_bar_sync(1, EPI_WARPS * 32);
-                    if (threadIdx.x == 64) p.ws_counters[st] = 0;
+                }
+                if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
+                    raise_error(p, abort_flag, kStatusTimeoutAccFull);
+                    break;
+                }
+                tc_fence_after();
+                bool finish = whole;
+                if (!whole) {
+                    // the gate columns of this warp's token range and the matching up columns
+                    finish = publish_partial<EPI_WARPS, 8>(p, seg, st, t_acc, tok_lo, tok_hi, n_tok, r_tile, true,
+                                                           last_flag);
+                }
+                if (finish) {
+                    const int4* contrib[kMaxContrib];
+                    const int n_contrib = whole ? 0 : contributors(p, st, contrib);
+                    const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
+                    for (int cc = tok_lo; cc < tok_hi && cc < p.M; cc += 8) {
+                        uint32_t g[8], u[8];
+                        tmem_ld_x8_pair_sync(t_acc + cc, t_acc + n_tok + cc, g, u);
+                        if (!whole) {
+                            add_partials<8>(contrib, n_contrib, cc, r_tile, g);
+                            add_partials<8>(contrib, n_contrib, n_tok + cc, r_tile, u);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; i += 2) {
+                            const int t = cc + i;
+                            uint32_t o;
+                            if constexpr (MODE == 0) {
+                                const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sw + t);
+                                o = swiglu2(dequant2(g[i], g[i + 1], sa2, swg2, bg2),
+                                            dequant2(u[i], u[i + 1], sa2, swu2, bu2));
+                            } else {
+                                o = swiglu2(f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1])),
+                                            f2(__uint_as_float(u[i]), __uint_as_float(u[i + 1])));
+                            }
+                            if (t < p.M) p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o & 0xFFFFu);
+                            if (t + 1 < p.M)
+                                p.out[static_cast<size_t>(t + 1) * p.ldo + j] = __ushort_as_bfloat16(o >> 16);
+                        }
+                    }
+                    if (!whole) {
+                        named_bar_sync(1, EPI_WARPS * 32);
+                        if (threadIdx.x == 64) p.ws_counters[st] = 0;
+                    }
+                }
+            } else {
+                // ------------------------------------------------ token-major tile: lanes are token rows
+                constexpr int kCols = (EPI == kEpiSwiglu) ? kBN / 2 : kBN;   // output columns of a tile
+                const int c_lo = (e / 4) * (kCols / kSplit);
+                const int c_hi = c_lo + kCols / kSplit;
+                const int grow = m0 + r_tile;
+                const bool row_ok = grow >= row_lo && grow < row_hi;
+                // Stage this tile's column scales / biases and this row's scale while the MMAs still run.
+                float sa_row = 0.f;
+                if constexpr (MODE == 0) {
+                    for (int t = threadIdx.x - 64; t < kBN; t += EPI_WARPS * 32) {
+                        int col;
+                        if constexpr (EPI == kEpiSwiglu)
+                            col = part * p.n_part_stride + nt * (kBN / 2) + (t < kBN / 2 ? t : p.H + t - kBN / 2);
+                        else
+                            col = part * p.n_part_stride + nt * kBN + t;
+                        s_sw[t] = __ldg(p.sw + col);
+                        s_bias[t] = __ldg(p.bias + col);
+                    }
+                    if (row_ok) sa_row = __ldg(p.sa + part * p.sa_part_stride + grow);
+                    named_bar_sync(1, EPI_WARPS * 32);
+                }
+                if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
+                    raise_error(p, abort_flag, kStatusTimeoutAccFull);
+                    break;
+                }
+                tc_fence_after();
+                bool finish = whole;
+                if (!whole) {
+                    // SwiGLU tiles publish the gate columns [c_lo, c_hi) and the up columns 128 + [c_lo, c_hi)
+                    finish = publish_partial<EPI_WARPS, 32>(p, seg, st, t_int, c_lo, c_hi,
+                                                            EPI == kEpiSwiglu ? kBN / 2 : 0, r_tile, row_ok, last_flag);
+                }
+                if (finish) {
+                    const int4* contrib[kMaxContrib];
+                    const int n_contrib = whole ? 0 : contributors(p, st, contrib);
+                    constexpr bool add_f = (MODE == 0 && ADD_F);
+                    const uint64_t sa2 = f2(sa_row, sa_row);
+                    for (int cc = c_lo; cc < c_hi; cc += 32) {
+                        uint32_t g[32];
+                        uint32_t u[32];
+                        uint32_t fg[32];
+                        uint32_t fu[32];
+                        if constexpr (EPI == kEpiSwiglu) {
+                            tmem_ld2_x32_sync(t_acc + cc, t_acc + kBN / 2 + cc, g, u);
+                            if constexpr (add_f) tmem_ld2_x32_sync(t_f32 + cc, t_f32 + kBN / 2 + cc, fg, fu);
+                        } else {
+                            tmem_ld_x32_sync(t_acc + cc, g);
+                            if constexpr (add_f) tmem_ld_x32_sync(t_f32 + cc, fg);
+                        }
+                        if (!row_ok) continue;
+                        if (!whole) {
+                            add_partials<32>(contrib, n_contrib, cc, r_tile, g);
+                            if constexpr (EPI == kEpiSwiglu) add_partials<32>(contrib, n_contrib, kBN / 2 + cc, r_tile, u);
+                        }
+                        uint32_t packed[16];
+                        __nv_bfloat16* dst;
+                        if constexpr (EPI == kEpiSwiglu) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 2) {
+                                uint64_t vg, vu;
+                                if constexpr (MODE == 0) {
+                                    const uint64_t swg = *reinterpret_cast<const uint64_t*>(s_sw + cc + i);
+                                    const uint64_t swu = *reinterpret_cast<const uint64_t*>(s_sw + kBN / 2 + cc + i);
+                                    const uint64_t bgv = *reinterpret_cast<const uint64_t*>(s_bias + cc + i);
+                                    const uint64_t buv = *reinterpret_cast<const uint64_t*>(s_bias + kBN / 2 + cc + i);
+                                    vg = dequant2(g[i], g[i + 1], sa2, swg, bgv);
+                                    vu = dequant2(u[i], u[i + 1], sa2, swu, buv);
+                                    if constexpr (add_f) {
+                                        vg = add2_rn(vg, f2(__uint_as_float(fg[i]), __uint_as_float(fg[i + 1])));
+                                        vu = add2_rn(vu, f2(__uint_as_float(fu[i]), __uint_as_float(fu[i + 1])));
+                                    }
+                                } else {
+                                    vg = f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1]));
+                                    vu = f2(__uint_as_float(u[i]), __uint_as_float(u[i + 1]));
+                                }
+                                packed[i / 2] = swiglu2(vg, vu);
+                            }
+                            dst = p.out + static_cast<size_t>(grow) * p.ldo + nt * (kBN / 2) + cc;
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 2) {
+                                uint64_t v;
+                                if constexpr (MODE == 0) {
+                                    const uint64_t s2 = *reinterpret_cast<const uint64_t*>(s_sw + cc + i);
+                                    const uint64_t b2 = *reinterpret_cast<const uint64_t*>(s_bias + cc + i);
+                                    v = dequant2(g[i], g[i + 1], sa2, s2, b2);
+                                    if constexpr (add_f) v = add2_rn(v, f2(__uint_as_float(fg[i]), __uint_as_float(fg[i + 1])));
+                                } else {
+                                    v = f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1]));
+                                }
+                                packed[i / 2] = bf16x2_rn(v);
+                            }
+                            dst = p.out + out_part * p.out_part_stride + static_cast<size_t>(grow) * p.ldo + nt * kBN + cc;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            reinterpret_cast<uint4*>(dst)[i] =
+                                make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                    }
+                    if (!whole) {
+                        named_bar_sync(1, EPI_WARPS * 32);
+                        if (threadIdx.x == 64) p.ws_counters[st] = 0;
+                    }
                 }
             }
             tc_fence_before();

@@ -36,7 +36,7 @@ def activations(g: torch.Generator, M: int, K: int, kind: str = "normal") -> tor
 
 
 def int8_bank(g: torch.Generator, K: int, H: int, scale_lo=1e-3, scale_hi=1e-2, KH: int = 0, centered=False,
-              pow2_smoothing=False, bias=False):
+              pow2_smoothing=False, bias=True):
     """A gate/up bank in the reference's layout (earlier_gate_up_screen.py:30-33): W = [Wg; Wu] int8
     [2H, KL] uniform in [-127, 127], per-output-channel scales U(lo, hi).  KH > 0 adds BF16 outlier
     columns (high_columns) and their weights."""
@@ -49,7 +49,8 @@ def int8_bank(g: torch.Generator, K: int, H: int, scale_lo=1e-3, scale_hi=1e-2, 
     KL = len(low)
     w = torch.randint(-127, 128, (N2, KL), generator=g, dtype=torch.int32).to(torch.int8)
     sw = (scale_lo + (scale_hi - scale_lo) * torch.rand(N2, generator=g)).float()
-    b = (torch.randn(N2, generator=g) * 0.05).float() if bias else torch.zeros(N2)
+    # a non-zero bias makes the dequant's final add observable (bias = centers @ W_low^T in real banks)
+    b = (torch.randn(N2, generator=g) * 0.5).float() if bias else torch.zeros(N2)
     wh = (torch.randn(N2, KH, generator=g) * 0.02).to(torch.bfloat16)
     smoothing = (2.0 ** torch.randint(-2, 3, (KL,), generator=g).float()) if pow2_smoothing else torch.ones(KL)
     centers = (torch.randn(KL, generator=g) * 0.05) if centered else torch.zeros(KL)
