@@ -108,6 +108,21 @@ REAX_API int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, c
                     const float* sw, const float* bias, void* out, int M, int N2, int KL, int KH, int ldo,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- a5-a9 without a caller workspace ----------------------------------------------------------------
+ * No counterpart in the reference: the same INT8 gate/up + dequant + SwiGLU as reax_gate_up_i8, for
+ * callers that cannot allocate device memory for a workspace - e.g. a serving process that has handed
+ * all GPU memory to its own pool at start-up, or a plugin host that passes only input and output
+ * buffers.  It allocates nothing: its split-tile scratch is a fixed 16 MiB static device array that
+ * every GPU loading this library holds until exit; plans that split tiles are limited to 63 CTAs so
+ * their partials fit, and a plan needing more scratch is rejected with REAX_ERR_WORKSPACE.
+ * The first call on a device resolves the array's device address (cudaGetSymbolAddress) and should
+ * come before any stream capture.  All calls share the array and each call clears its status word
+ * and counters, so calls that overlap on the GPU (other streams, other threads) race: serialize them.
+ * Arguments and requirements as reax_gate_up_i8, without workspace / workspace_bytes. */
+REAX_API int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, const void* WH,
+                                     const float* sa, const float* sw, const float* bias, void* out, int M, int N2,
+                                     int KL, int KH, int ldo, void* stream);
+
 /* ---- a12 (fused): BF16-weight gate/up GEMM + SwiGLU, unsplit plan ------------------------------------
  * The mixed-origin BF16 projection with parts = 1 on both origins (runtime/mixed_origin_bf16.py:19-48:
  * one float32 accumulation over K, one bf16 rounding) of [Wg; Wu], followed by the silu_mul SwiGLU.

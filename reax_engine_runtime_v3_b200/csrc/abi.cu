@@ -260,6 +260,35 @@ int elementwise_grid(long long work, int sms) {
     return static_cast<int>(g);
 }
 
+// ------------------------------------------------------------------------ allocation-free variant
+// Scratch of reax_gate_up_i8_noalloc: one array per GPU that loads this library, held until exit.
+// It keeps the layout of a caller workspace (status word, split counters, split partials) sized for
+// kNoAllocMaxCtas CTAs; larger grids are planned down to that count.
+constexpr size_t kNoAllocScratchBytes = 16u << 20;   // 16 MiB
+constexpr int kNoAllocMaxCtas = 63;                  // split partials of 63 CTAs (2 x 128 KiB each) fit
+static_assert(kStatusBytes + 512 + static_cast<size_t>(kNoAllocMaxCtas) * 2 * reax::kSlotInts * sizeof(int) <=
+                  kNoAllocScratchBytes,
+              "no-alloc scratch too small for its CTA cap");
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+void* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mutex;
+
+// Device address of the scratch array on `dev` (the current device); resolved once per device.
+// In host code g_noalloc_scratch only names a host-side stand-in, so the address must come from
+// cudaGetSymbolAddress with that device current.
+int noalloc_scratch(int dev, void** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return REAX_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -630,6 +659,86 @@ int reax_selftest_wait(void* workspace, unsigned long long timeout_ns, void* str
     if (rc != REAX_OK) return rc;
     return launch_plain("selftest_wait launch", reax::selftest_wait_kernel, dim3(1), dim3(32),
                         static_cast<cudaStream_t>(stream), static_cast<unsigned*>(workspace), timeout_ns);
+}
+
+int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa,
+                            const float* sw, const float* bias, void* out, int M, int N2, int KL, int KH, int ldo,
+                            void* stream) {
+    if (M < 0 || N2 <= 0 || KL < 0 || KH < 0 || KL + KH == 0)
+        return fail(REAX_ERR_INVALID, "gate_up_i8_noalloc: bad sizes M=%d N2=%d KL=%d KH=%d", M, N2, KL, KH);
+    if (KL % 128 != 0 || KH % 64 != 0 || N2 % 256 != 0)
+        return fail(REAX_ERR_INVALID,
+                    "gate_up_i8_noalloc: needs KL %% 128 == 0, KH %% 64 == 0, N2 %% 256 == 0 (KL=%d KH=%d N2=%d)", KL,
+                    KH, N2);
+    if (ldo < N2 / 2 || ldo % 8 != 0)
+        return fail(REAX_ERR_INVALID, "gate_up_i8_noalloc: ldo=%d (needs >= N2/2, %% 8 == 0)", ldo);
+    if (KL == 0) return fail(REAX_ERR_INVALID, "gate_up_i8_noalloc: KL must be > 0");
+    if (M == 0) return REAX_OK;
+    if (!out || !sw || !bias || !A || !W || !sa || (KH && (!AH || !WH)))
+        return fail(REAX_ERR_INVALID, "gate_up_i8_noalloc: NULL pointer argument");
+    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(AH, 16) || !aligned(WH, 16) || !aligned(sw, 16) ||
+        !aligned(bias, 16) || !aligned(out, 16))
+        return fail(REAX_ERR_ALIGN, "gate_up_i8_noalloc: operands, sw, bias and out must be 16-byte aligned");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    void* scratch = nullptr;
+    if ((rc = noalloc_scratch(dev, &scratch)) != REAX_OK) return rc;
+
+    reax::TcParams p;
+    init_params(p);
+    const bool swap = KH == 0 && M <= kSwapMaxRows;
+    p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
+    if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
+        return rc;
+    if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL)) != REAX_OK) return rc;
+    if (KH) {
+        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH)) != REAX_OK) return rc;
+    } else {
+        p.tm_ah = p.tm_a;
+        p.tm_bh = p.tm_b;
+    }
+    p.sa = sa;
+    p.sw = sw;
+    p.bias = bias;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.M = M;
+    p.H = N2 / 2;
+    p.ldo = ldo;
+    p.kb_int = KL / 128;
+    p.kb_f16 = KH / 64;
+    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
+    p.n_tiles = (N2 / 2) / (reax::kBN / 2);
+    p.tiles = p.m_tiles * p.n_tiles;
+    p.mode = 0;
+    p.acc_bufs = KH ? 1 : 2;
+    p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
+    // Whole-tile plans need no partials; a plan that splits tiles is re-planned for at most
+    // kNoAllocMaxCtas CTAs, whose partials the static scratch holds.
+    int grid = 0;
+    plan_schedule(p, info->sms, KH == 0, &grid);
+    int ctas = grid;
+    if (p.sk_iters > 0 && grid > kNoAllocMaxCtas) {
+        plan_schedule(p, kNoAllocMaxCtas, true, &grid);
+        ctas = grid;
+    }
+    const int slots = p.sk_iters > 0 ? ctas : 0;
+    const size_t counter_bytes = ((static_cast<size_t>(2 * (slots > 0 ? slots : 1)) * sizeof(int)) + 255) / 256 * 256;
+    const size_t need = kStatusBytes + counter_bytes + static_cast<size_t>(slots) * 2 * reax::kSlotInts * sizeof(int);
+    if (need > kNoAllocScratchBytes)
+        return fail(REAX_ERR_WORKSPACE, "gate_up_i8_noalloc: plan needs %zu bytes of scratch, the maximum is %zu", need,
+                    kNoAllocScratchBytes);
+    uint8_t* b = static_cast<uint8_t*>(scratch);
+    p.status = reinterpret_cast<unsigned*>(b);
+    p.ws_counters = reinterpret_cast<int*>(b + kStatusBytes);
+    p.ws_partials = reinterpret_cast<int*>(b + kStatusBytes + counter_bytes);
+    // The array keeps the previous call's contents: the status word and the split counters must start at zero.
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const cudaError_t e = cudaMemsetAsync(scratch, 0, kStatusBytes + counter_bytes, s);
+    if (e != cudaSuccess) return cuda_fail(e, "gate_up_i8_noalloc: clearing the scratch");
+    return launch_tc(reax::kEpiSwiglu, p, grid, s);
 }
 
 }  // extern "C"
