@@ -63,7 +63,7 @@ enum Variant : int {
 };
 
 // Activation rows up to which the gate/up kernels use weight-major (swap) tiles.
-constexpr int kSwapMaxRows = 64;
+constexpr int kSwapMaxRows = reax::kSwapMaxTok;
 
 void* tc_kernel_ptr(int v) {
     using namespace reax;

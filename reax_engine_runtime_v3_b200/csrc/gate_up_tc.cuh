@@ -35,6 +35,7 @@ constexpr int kBStage = kBN * kRowBytes;        // 32 KiB
 constexpr int kStageBytes = kAStage + kBStage;  // 48 KiB
 constexpr int kTmemCols = 512;
 constexpr int kSlotInts = kBM * kBN;            // one split-tile partial: 128 x 256 int32 (128 KiB)
+constexpr int kSwapMaxTok = 64;                 // weight-major tiles: at most 64 token columns per accumulator
 
 enum EpilogueKind : int { kEpiSwiglu = 0, kEpiPlain = 1 };
 
@@ -202,10 +203,29 @@ REAX_DEVI float dequant1(uint32_t acc_bits, float sa_row, float sw_col, float bi
 // Split-tile helper shared by both epilogues: publish this CTA's int32 partial of accumulator columns
 // [c_lo, c_hi) (and [c_lo + pair_off, c_hi + pair_off) when pair_off > 0: the up half of a SwiGLU
 // tile), valid lanes only, then learn whether this CTA completes the tile.  W = columns per TMEM load.
+//
+// Before publishing, the counter is read: when every other contributor has already published (their
+// K-block counts add up to KB minus ours) this CTA is the one that completes the tile and skips its
+// own publication; it then resets the counter after its epilogue like any finishing CTA.  Nobody
+// else can reach KB afterwards because all other contributors have already counted.
+REAX_DEVI int ld_acquire_gpu(const int* ptr) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
 template <int EPI_WARPS, int W>
 REAX_DEVI bool publish_partial(const TcParams& p, const Segment& seg, int st, uint32_t t_acc, int c_lo, int c_hi,
                                int pair_off, int lane_row, bool lane_ok, int* last_flag) {
     const int KB = p.kb_int + p.kb_f16;
+    if (threadIdx.x == 64) *last_flag = (ld_acquire_gpu(p.ws_counters + st) + (seg.k1 - seg.k0) == KB) ? 1 : 0;
+    named_bar_sync(1, EPI_WARPS * 32);
+    if (*reinterpret_cast<volatile int*>(last_flag) != 0) {
+        __threadfence();
+        named_bar_sync(1, EPI_WARPS * 32);   // every thread has read the flag before it is reused
+        return true;
+    }
+    named_bar_sync(1, EPI_WARPS * 32);
     int4* slot = reinterpret_cast<int4*>(p.ws_partials +
                                          (static_cast<size_t>(blockIdx.x) * 2 + sk_slot(p, blockIdx.x, st)) * kSlotInts);
     for (int h = 0; h < (pair_off > 0 ? 2 : 1); ++h) {
@@ -293,7 +313,6 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
     int* last_flag = abort_flag + 1;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int KB = p.kb_int + p.kb_f16;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -519,24 +538,52 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
                     const int4* contrib[kMaxContrib];
                     const int n_contrib = whole ? 0 : contributors(p, st, contrib);
                     const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
-                    for (int cc = tok_lo; cc < tok_hi && cc < p.M; cc += 8) {
-                        uint32_t g[8], u[8];
-                        tmem_ld_x8_pair_sync(t_acc + cc, t_acc + n_tok + cc, g, u);
-                        if (!whole) {
-                            add_partials<8>(contrib, n_contrib, cc, r_tile, g);
-                            add_partials<8>(contrib, n_contrib, n_tok + cc, r_tile, u);
-                        }
+                    // this warp's tokens: up to 4 chunks of 8; all TMEM loads, then all partial loads, are
+                    // issued before any use, so the L2 round trips of the chunks overlap
+                    constexpr int kChunks = kSwapMaxTok / 2 / 8;
+                    const int tok_end = min(tok_hi, p.M);
+                    uint32_t g[kChunks][8], u[kChunks][8];
+#pragma unroll
+                    for (int c = 0; c < kChunks; ++c)
+                        if (tok_lo + 8 * c < tok_end)
+                            tmem_ld_x8_pair_sync(t_acc + tok_lo + 8 * c, t_acc + n_tok + tok_lo + 8 * c, g[c], u[c]);
+                    for (int ci = 0; ci < n_contrib; ++ci) {
+                        int4 pg[kChunks][2], pu[kChunks][2];
+#pragma unroll
+                        for (int c = 0; c < kChunks; ++c)
+                            if (tok_lo + 8 * c < tok_end) {
+#pragma unroll
+                                for (int h = 0; h < 2; ++h) {
+                                    pg[c][h] = __ldcg(contrib[ci] + ((tok_lo + 8 * c + 4 * h) / 4) * kBM + r_tile);
+                                    pu[c][h] = __ldcg(contrib[ci] + ((n_tok + tok_lo + 8 * c + 4 * h) / 4) * kBM + r_tile);
+                                }
+                            }
+#pragma unroll
+                        for (int c = 0; c < kChunks; ++c)
+                            if (tok_lo + 8 * c < tok_end) {
+#pragma unroll
+                                for (int h = 0; h < 2; ++h) {
+                                    g[c][4 * h] += pg[c][h].x; g[c][4 * h + 1] += pg[c][h].y;
+                                    g[c][4 * h + 2] += pg[c][h].z; g[c][4 * h + 3] += pg[c][h].w;
+                                    u[c][4 * h] += pu[c][h].x; u[c][4 * h + 1] += pu[c][h].y;
+                                    u[c][4 * h + 2] += pu[c][h].z; u[c][4 * h + 3] += pu[c][h].w;
+                                }
+                            }
+                    }
+#pragma unroll
+                    for (int c = 0; c < kChunks; ++c) {
+                        if (tok_lo + 8 * c >= tok_end) continue;
 #pragma unroll
                         for (int i = 0; i < 8; i += 2) {
-                            const int t = cc + i;
+                            const int t = tok_lo + 8 * c + i;
                             uint32_t o;
                             if constexpr (MODE == 0) {
                                 const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sw + t);
-                                o = swiglu2(dequant2(g[i], g[i + 1], sa2, swg2, bg2),
-                                            dequant2(u[i], u[i + 1], sa2, swu2, bu2));
+                                o = swiglu2(dequant2(g[c][i], g[c][i + 1], sa2, swg2, bg2),
+                                            dequant2(u[c][i], u[c][i + 1], sa2, swu2, bu2));
                             } else {
-                                o = swiglu2(f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1])),
-                                            f2(__uint_as_float(u[i]), __uint_as_float(u[i + 1])));
+                                o = swiglu2(f2(__uint_as_float(g[c][i]), __uint_as_float(g[c][i + 1])),
+                                            f2(__uint_as_float(u[c][i]), __uint_as_float(u[c][i + 1])));
                             }
                             if (t < p.M) p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o & 0xFFFFu);
                             if (t + 1 < p.M)
