@@ -7,8 +7,10 @@ Prints ONE JSON line on rank 0.  A step is one pass of the hot path over one bat
 K = 4096, H = 14336, one quantize + one gate/up launch each).  Under torchrun (N > 1) the intermediate
 dimension H is sharded over the ranks: rank r owns gate rows [r*H/N, (r+1)*H/N) and the matching up
 rows, every rank quantizes the replicated activations itself, and no collective runs on the path
-(the total work is fixed, so the scaling is strong).  Timing: W warm-up steps, then exactly K steps
-between barriers + synchronizes, CUDA events on the launching stream, max over ranks.  Three copies of
+(the total work is fixed, so the scaling is strong).  The step's public API calls are captured once
+per rotating weight copy into CUDA graphs (as the reference runtime captures its decode steps) and
+replayed.  Timing: W warm-up steps, then exactly K graph replays between barriers + synchronizes,
+CUDA events on the launching stream, max over ranks.  Three copies of
 the weights rotate between steps (3 x 117 MB > 126 MB L2), so no step finds its weights in L2.
 
 ``--impl reference`` times the reference arithmetic of the path on the host cores (the reference
@@ -312,61 +314,100 @@ def main():
     bf16 = Bf16Native()
     stream = torch.cuda.current_stream()
 
-    def step(i):
+    def step(i, inputs=None):
         b = banks[i % copies]
-        for x in xs:
+        for x in (inputs or xs):
             if int8:
                 gate_up.project(x, b, "hybrid8_b128n256_s64n256")
             else:
                 bf16.gate_up(x, b["w"])
 
-    for i in range(args.warmup):
-        step(i)
+    # Every timed loop replays CUDA graphs captured from the public API calls, as the reference runtime
+    # replays its captured decode steps (runtime/capture.py); one graph per rotating weight copy.  The
+    # capture stream gets its workspace during the eager warm-up, so nothing is allocated or zeroed
+    # inside a graph.
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(cap):
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        # eager steps, for reference only (host launch overhead included)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cap)
+        for i in range(args.warmup):
+            step(i)
+        e1.record(cap)
+        torch.cuda.synchronize()
+        eager_ms = e0.elapsed_time(e1) / args.warmup
+        graphs = []
+        for c in range(copies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                step(c)
+            graphs.append(g)
+        for i in range(args.warmup):
+            graphs[i % copies].replay()
+        _native.clear_status(_native.workspace(dev))
     barrier(world)
-    _native.clear_status(_native.workspace(dev))
 
     sampler = ClockSampler(local)
     if rank == 0 or world > 1:
         sampler.start()
     barrier(world)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    ev1.record(stream)
+    with torch.cuda.stream(cap):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(cap)
+        for i in range(args.steps):
+            graphs[i % copies].replay()
+        ev1.record(cap)
     barrier(world)
     clocks = sampler.stop()
     ms = ev0.elapsed_time(ev1) / args.steps
     ms = max_over_ranks(ms, world)
-    status = _native.read_status(_native.workspace(dev))
+    with torch.cuda.stream(cap):
+        status = _native.read_status(_native.workspace(dev))
     tokens = sum(buckets)
     value = tokens / (ms * 1e-3)
     launches = args.steps * len(buckets) * (2 if int8 else 1)
 
-    # dominant kernel (the GEMM) timed alone, per launch, with events on its stream
+    # dominant kernel (the GEMM) alone: a graph of back-to-back launches over the rotating weight
+    # copies, timed with events on its stream; per launch = replay time / launches (gaps included)
     from reax_engine_runtime_v3_b200.reaxv2.gate_up import gate_up_i8, quantize_rows
     per_bucket = []
-    if int8:
-        pre = [quantize_rows(x, banks[0]) for x in xs]
-    for bi, x in enumerate(xs):
-        M = x.shape[0]
-        evs = []
-        for i in range(args.warmup + args.steps):
-            b = banks[i % copies]
+    reps = 3 * copies
+    with torch.cuda.stream(cap):
+        pre = [quantize_rows(x, banks[0]) for x in xs] if int8 else None
+        for bi, x in enumerate(xs):
+            M = x.shape[0]
+
+            def gemm(r):
+                b = banks[r % copies]
+                if int8:
+                    low, high, sc = pre[bi]
+                    gate_up_i8(low, b.low_weight, high, b.high_weight, sc, b.scales, b.bias)
+                else:
+                    bf16.gate_up(x, b["w"])
+            gemm(0)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                for r in range(reps):
+                    gemm(r)
+            for _ in range(2):
+                g.replay()
+            torch.cuda.synchronize()
+            n_rep = max(1, args.steps // reps) + 2
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            if int8:
-                low, high, sc = pre[bi]
-                gate_up_i8(low, b.low_weight, high, b.high_weight, sc, b.scales, b.bias)
-            else:
-                bf16.gate_up(x, b["w"])
-            e1.record(stream)
-            if i >= args.warmup:
-                evs.append((e0, e1))
-        torch.cuda.synchronize()
-        d = statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e-3
-        d = max_over_ranks(d, world)
-        per_bucket.append((M, d))
+            e0.record(cap)
+            for _ in range(n_rep):
+                g.replay()
+            e1.record(cap)
+            torch.cuda.synchronize()
+            d = e0.elapsed_time(e1) * 1e-3 / (n_rep * reps)
+            d = max_over_ranks(d, world)
+            per_bucket.append((M, d))
+            del g
     peaks, peak_kind = measured_peaks()
     prefill = min(buckets) >= 512
     if prefill:
@@ -391,30 +432,47 @@ def main():
     roofline["traffic"] = ncu_traffic(args.workload)
     roofline["per_launch_us"] = {str(M): round(d * 1e6, 2) for M, d in per_bucket}
 
-    # end to end through the public API with host buffers
+    # end to end through the public API with host buffers: every step copies its inputs from pinned
+    # host memory, runs the path and reads every output back to pinned host memory, all inside the
+    # replayed graph
     e2e = None
     if not args.no_e2e:
         xs_host = [x.pin_memory() for x in xs_cpu]
         outs_host = [torch.empty((x.shape[0], h), dtype=torch.bfloat16).pin_memory() for x in xs_cpu]
-        for i in range(args.warmup):
-            for xh, oh in zip(xs_host, outs_host):
-                xd = xh.to(dev, non_blocking=True)
-                o = gate_up.project(xd, banks[i % copies], "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(xd, banks[i % copies]["w"])
+        xs_dev = [torch.empty_like(x, device=dev) for x in xs_cpu]
+
+        def e2e_step(i):
+            b = banks[i % copies]
+            for xh, xd, oh in zip(xs_host, xs_dev, outs_host):
+                xd.copy_(xh, non_blocking=True)
+                o = gate_up.project(xd, b, "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(xd, b["w"])
                 oh.copy_(o, non_blocking=True)
+        with torch.cuda.stream(cap):
+            e2e_step(0)
+            torch.cuda.synchronize()
+            egraphs = []
+            for c in range(copies):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cap):
+                    e2e_step(c)
+                egraphs.append(g)
+            for i in range(args.warmup):
+                egraphs[i % copies].replay()
         barrier(world)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for i in range(args.steps):
-            for xh, oh in zip(xs_host, outs_host):
-                xd = xh.to(dev, non_blocking=True)
-                o = gate_up.project(xd, banks[i % copies], "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(xd, banks[i % copies]["w"])
-                oh.copy_(o, non_blocking=True)
-        e1.record(stream)
+        with torch.cuda.stream(cap):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cap)
+            for i in range(args.steps):
+                egraphs[i % copies].replay()
+            e1.record(cap)
         barrier(world)
         ems = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
         e2e = {"value": tokens / (ems * 1e-3), "unit": "tokens/s",
                "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs_cpu),
-               "d2h_bytes_per_step": sum(x.shape[0] * h * 2 for x in xs_cpu)}
+               "d2h_bytes_per_step": sum(x.shape[0] * h * 2 for x in xs_cpu),
+               "how": "public API calls captured once per weight copy into CUDA graphs, replayed per step"}
+        del egraphs
+    del graphs
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -430,7 +488,8 @@ def main():
                            "parallelism": f"H-shard x{world}" if world > 1 else "1 GPU",
                            "l2": f"{copies} rotating weight copies ({copies * 2 * h * K * (1 if int8 else 2) / 1e6:.0f} MB > 126 MB L2)"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
-                "device_status": status}
+                "device_status": status, "timing": "CUDA-graph replay of the captured step",
+                "eager_ms_per_step": eager_ms}
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

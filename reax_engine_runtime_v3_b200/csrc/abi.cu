@@ -85,8 +85,11 @@ int variant_of(int epi, const reax::TcParams& p) {
     return p.mode == 1 ? kPlainBf16 : (p.kb_f16 > 0 ? kPlainI8F : kPlainI8);
 }
 
-// pipeline stages + 1 KiB alignment slack + staged column scales/biases (2 x 2 x 256 floats) + barriers
-constexpr size_t tc_smem_bytes() { return static_cast<size_t>(kStages) * reax::kStageBytes + 1024 + 4096 + 256; }
+// pipeline stages + weight-major output staging + 1 KiB alignment slack + staged column scales/biases
+// (2 x 2 x 256 floats) + barriers
+constexpr size_t tc_smem_bytes() {
+    return static_cast<size_t>(kStages) * reax::kStageBytes + reax::kOutStageBytes + 1024 + 4096 + 256;
+}
 
 // Current device, its SM count, and a check that it is sm_100; sets kernel attributes once.
 int current_device(int* dev_out, DeviceInfo** info_out) {
@@ -114,6 +117,18 @@ int current_device(int* dev_out, DeviceInfo** info_out) {
             if ((e = cudaFuncSetAttribute(tc_kernel_ptr(v), cudaFuncAttributeMaxDynamicSharedMemorySize, bytes)) !=
                 cudaSuccess)
                 return cuda_fail(e, "cudaFuncSetAttribute(tcgen05 kernel smem)");
+        // The kernels move registers from the control warps to the epilogue warps (setmaxnreg): refuse
+        // to launch a build whose register count cannot cover the split, since the grow would never return.
+        for (int v = 0; v < kVariants; ++v) {
+            cudaFuncAttributes fa{};
+            if ((e = cudaFuncGetAttributes(&fa, tc_kernel_ptr(v))) != cudaSuccess)
+                return cuda_fail(e, "cudaFuncGetAttributes(tcgen05 kernel)");
+            const int warps = reax::kCtlWarps + kEpiWarps;
+            if (fa.numRegs < reax::kCtlRegs || fa.numRegs > reax::kEpiRegs ||
+                fa.numRegs * warps < reax::kCtlRegs * reax::kCtlWarps + reax::kEpiRegs * kEpiWarps)
+                return fail(REAX_ERR_DEVICE, "tcgen05 kernel variant %d compiled to %d registers per thread, which "
+                            "cannot cover the %d/%d register split", v, fa.numRegs, reax::kCtlRegs, reax::kEpiRegs);
+        }
         d.smem_set = true;
     }
     *dev_out = dev;
@@ -213,7 +228,7 @@ void plan_schedule(reax::TcParams& p, int sms, bool allow_split, int* grid) {
 int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3(64 + 32 * kEpiWarps, 1, 1);
+    cfg.blockDim = dim3(reax::kCtlThreads + 32 * kEpiWarps, 1, 1);
     cfg.dynamicSmemBytes = tc_smem_bytes();
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -436,6 +451,7 @@ int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, const void
     // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
     const bool swap = KH == 0 && M <= kSwapMaxRows;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
+    p.out_vec16 = 1;   // out 16-byte aligned and ldo % 8 == 0, checked above
     if (KL) {
         if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
             return rc;
@@ -496,6 +512,7 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     init_params(p);
     const bool swap = M <= kSwapMaxRows;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
+    p.out_vec16 = 1;   // out 16-byte aligned and ldo % 8 == 0, checked above
     if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : 128)) != REAX_OK)
         return rc;
     if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K)) != REAX_OK) return rc;
@@ -690,6 +707,7 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     init_params(p);
     const bool swap = KH == 0 && M <= kSwapMaxRows;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
+    p.out_vec16 = 1;   // out 16-byte aligned and ldo % 8 == 0, checked above
     if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
         return rc;
     if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL)) != REAX_OK) return rc;

@@ -211,6 +211,11 @@ REAX_DEVI void tmem_ld_x8_pair_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[8], 
         : "memory");
 }
 
+// The same into the first 8 entries of 32-entry arrays.
+REAX_DEVI void tmem_ld_x8_pair_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[32], uint32_t (&b)[32]) {
+    tmem_ld_x8_pair_sync(ta, tb, *reinterpret_cast<uint32_t(*)[8]>(a), *reinterpret_cast<uint32_t(*)[8]>(b));
+}
+
 // Two 32-column loads (e.g. the gate and the up half of one output chunk) and one wait.
 REAX_DEVI void tmem_ld2_x32_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[32], uint32_t (&b)[32]) {
     asm volatile(
@@ -235,6 +240,12 @@ REAX_DEVI void tmem_ld2_x32_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[32], ui
 
 // Named barrier over `count` threads (a multiple of 32).
 REAX_DEVI void named_bar_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
+
+// Per-warpgroup register split (setmaxnreg; every thread of the warpgroup executes it).  A grow waits
+// until other warps of the CTA have released enough registers, so callers pair it with shrinks whose
+// total covers it.
+template <int N> REAX_DEVI void regs_shrink() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N> REAX_DEVI void regs_grow() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
 
 // Programmatic dependent launch: wait for the preceding grid's memory to be visible.
 REAX_DEVI void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -332,14 +343,12 @@ REAX_DEVI uint64_t dequant2(uint32_t a0, uint32_t a1, uint64_t sa2, uint64_t sw2
     return f2(v0, v1);
 }
 
-// Scalar entry of the exact pair path below, kept out of line so the unrolled epilogue stays small.
-__device__ __noinline__ float silu_bf16_value_slow(float x) { return silu_bf16_value(x); }
-
-// bf16(silu_f32(x)) for two bf16-valued inputs, as a float32 pair; bit-identical to silu_bf16_value.
+// bf16(silu_f32(x)) for two bf16-valued inputs, as a float32 pair, by the approximation alone.
 // Classes per lane: x >= 17 -> x; -inf < x <= -89 -> -0; -86 < x < 17 -> the approximation, accepted
-// when it passes the rounding test; anything else (NaN, +-inf, (-89, -86], a failed test) sends the
-// pair through silu_bf16_value.
-REAX_DEVI uint64_t silu2_bf16(float x0, float x1) {
+// when it passes the rounding test.  Bit i of `miss` is set when lane i is in none of these classes
+// (NaN, +-inf, (-89, -86], a failed test): its value must then come from silu_bf16_value.  No branch
+// and no call, so a caller can run many pairs side by side.
+REAX_DEVI uint64_t silu2_fast(float x0, float x1, uint32_t& miss) {
     constexpr float kNegLog2eHi = -1.44269502162933349609375f;
     constexpr float kNegLog2eLo = -1.925963033500011079e-08f;
     constexpr float kLn2 = 0.693147180559945309f;
@@ -364,21 +373,54 @@ REAX_DEVI uint64_t silu2_bf16(float x0, float x1) {
     const bool hi0 = x0 >= 17.0f, hi1 = x1 >= 17.0f;
     const bool lo0 = x0 <= -89.0f && x0 > -INFINITY, lo1 = x1 <= -89.0f && x1 > -INFINITY;
     const bool mid0 = x0 > -86.0f && x0 < 17.0f && !near0, mid1 = x1 > -86.0f && x1 < 17.0f && !near1;
-    float s0 = hi0 ? x0 : (lo0 ? -0.0f : __uint_as_float(b0));
-    float s1 = hi1 ? x1 : (lo1 ? -0.0f : __uint_as_float(b1));
-    uint32_t w = bf16x2_rn(f2(s0, s1));
-    if (!((hi0 || lo0 || mid0) && (hi1 || lo1 || mid1))) {
-        w = bf16x2_rn(f2(silu_bf16_value_slow(x0), silu_bf16_value_slow(x1)));
-    }
-    return bf16x2_to_f2(w);
+    const float s0 = hi0 ? x0 : (lo0 ? -0.0f : __uint_as_float(b0));
+    const float s1 = hi1 ? x1 : (lo1 ? -0.0f : __uint_as_float(b1));
+    miss = ((hi0 || lo0 || mid0) ? 0u : 1u) | ((hi1 || lo1 || mid1) ? 0u : 2u);
+    return bf16x2_to_f2(bf16x2_rn(f2(s0, s1)));
 }
 
-// SwiGLU of two (gate, up) float32 pairs: bf16x2 of bf16(bf16(silu(bf16(g))) * bf16(u)).
-REAX_DEVI uint32_t swiglu2(uint64_t vg2, uint64_t vu2) {
-    const uint64_t g2 = bf16x2_to_f2(bf16x2_rn(vg2));
-    const uint64_t u2 = bf16x2_to_f2(bf16x2_rn(vu2));
-    const uint64_t s2 = silu2_bf16(f2_lo(g2), f2_hi(g2));
-    return bf16x2_rn(mul2_rn(s2, u2));
+// silu_bf16_value out of line: the exact path, reached only for the values silu2_fast does not settle.
+__device__ __noinline__ float silu_bf16_exact(float x) { return silu_bf16_value(x); }
+
+// SwiGLU of PAIRS (gate, up) pairs whose gate and up values are already bf16-rounded (gb, ub):
+// o[i] = bf16x2 of bf16(silu(g) * u), lane-wise.  The approximation runs first for every pair; bit
+// 2i + l of the returned mask marks lane l of pair i as not settled.
+template <int PAIRS>
+REAX_DEVI uint32_t swiglu_fast_pairs(const uint64_t (&gb)[PAIRS], const uint64_t (&ub)[PAIRS], uint32_t (&o)[PAIRS]) {
+    uint32_t miss = 0;
+#pragma unroll
+    for (int i = 0; i < PAIRS; ++i) {
+        uint32_t m2;
+        o[i] = bf16x2_rn(mul2_rn(silu2_fast(f2_lo(gb[i]), f2_hi(gb[i]), m2), ub[i]));
+        miss |= m2 << (2 * i);
+    }
+    return miss;
+}
+
+// Redo the values marked in `miss` through the exact formula, warp-wide: in every round each lane takes
+// its lowest marked value and the whole warp evaluates silu_bf16_exact once, converged, so a warp pays
+// one exact evaluation per round (rounds = the most marked values of any one lane) instead of one per
+// marked value index.  All 32 lanes of the warp must call it together.
+template <int PAIRS>
+REAX_DEVI void swiglu_redo_warp(uint32_t miss, const uint64_t (&gb)[PAIRS], const uint64_t (&ub)[PAIRS],
+                                uint32_t (&o)[PAIRS]) {
+    static_assert(PAIRS <= 16, "one 32-bit mask");
+    while (__any_sync(0xFFFFFFFFu, miss != 0u)) {
+        const int v = miss ? __ffs(static_cast<int>(miss)) - 1 : -1;
+        float x = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 2 * PAIRS; ++i)
+            if (v == i) x = (i & 1) ? f2_hi(gb[i >> 1]) : f2_lo(gb[i >> 1]);
+        const float s = silu_bf16_exact(x);
+#pragma unroll
+        for (int i = 0; i < 2 * PAIRS; ++i)
+            if (v == i) {
+                const float uu = (i & 1) ? f2_hi(ub[i >> 1]) : f2_lo(ub[i >> 1]);
+                const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn(s, uu)));
+                o[i >> 1] = (i & 1) ? ((o[i >> 1] & 0xFFFFu) | (h << 16)) : ((o[i >> 1] & 0xFFFF0000u) | h);
+            }
+        miss &= miss - 1u;
+    }
 }
 
 // The same value through the accurate formula only (the domain reference for the test above).

@@ -36,6 +36,19 @@ constexpr int kStageBytes = kAStage + kBStage;  // 48 KiB
 constexpr int kTmemCols = 512;
 constexpr int kSlotInts = kBM * kBN;            // one split-tile partial: 128 x 256 int32 (128 KiB)
 constexpr int kSwapMaxTok = 64;                 // weight-major tiles: at most 64 token columns per accumulator
+constexpr int kOutStageBytes = kSwapMaxTok * (kBN / 2) * 2;   // weight-major output block staged for the stores
+
+// Thread layout: warp 0 issues the TMA copies, warp 1 the MMAs (it also owns TMEM), warps 2-3 only hand
+// their registers over, and warps kCtlWarps.. run the epilogue.  Warp w runs on SM sub-partition w % 4,
+// so every sub-partition holds one control warp and EPI_WARPS / 4 epilogue warps.
+constexpr int kCtlWarps = 4;
+constexpr int kCtlThreads = 32 * kCtlWarps;
+// Registers per thread after the split (setmaxnreg): the control warps shrink to kCtlRegs and the
+// epilogue warps grow to kEpiRegs.  The host launches a variant only when its compiled register count
+// R satisfies R * (kCtlWarps + EPI_WARPS) >= kCtlRegs * kCtlWarps + kEpiRegs * EPI_WARPS (with
+// 8 epilogue warps R = 168 gives exactly 56 + 2 * 224 per sub-partition), so the growth never waits.
+constexpr int kCtlRegs = 64;
+constexpr int kEpiRegs = 216;
 
 enum EpilogueKind : int { kEpiSwiglu = 0, kEpiPlain = 1 };
 
@@ -70,6 +83,7 @@ struct TcParams {
     unsigned long long timeout_ns;
     int evict_first_b;   // stream B with an evict-first L2 policy (weights read once)
     int n_tok;           // weight-major (swap) kernels: token columns per accumulator, a multiple of 16 >= M
+    int out_vec16;       // out is 16-byte aligned and ldo a multiple of 8: rows can be stored in 16-byte pieces
     // Mixed-origin slicing (BF16 partials): parts = P0 + P1 and part z < P0 is slice z of plan 0 (rows
     // < *split), part z >= P0 is slice z - P0 of plan 1 (rows >= *split).  Slice s of a plan covers K
     // blocks [s * chunk_kb, (s + 1) * chunk_kb) clipped to the K extent; its output part is s.
@@ -218,7 +232,7 @@ template <int EPI_WARPS, int W>
 REAX_DEVI bool publish_partial(const TcParams& p, const Segment& seg, int st, uint32_t t_acc, int c_lo, int c_hi,
                                int pair_off, int lane_row, bool lane_ok, int* last_flag) {
     const int KB = p.kb_int + p.kb_f16;
-    if (threadIdx.x == 64) *last_flag = (ld_acquire_gpu(p.ws_counters + st) + (seg.k1 - seg.k0) == KB) ? 1 : 0;
+    if (threadIdx.x == kCtlThreads) *last_flag = (ld_acquire_gpu(p.ws_counters + st) + (seg.k1 - seg.k0) == KB) ? 1 : 0;
     named_bar_sync(1, EPI_WARPS * 32);
     if (*reinterpret_cast<volatile int*>(last_flag) != 0) {
         __threadfence();
@@ -243,7 +257,7 @@ REAX_DEVI bool publish_partial(const TcParams& p, const Segment& seg, int st, ui
     }
     __threadfence();
     named_bar_sync(1, EPI_WARPS * 32);
-    if (threadIdx.x == 64) {
+    if (threadIdx.x == kCtlThreads) {
         const int n = seg.k1 - seg.k0;
         const int old = atomicAdd(p.ws_counters + st, n);
         *last_flag = (old + n == KB) ? 1 : 0;
@@ -293,7 +307,7 @@ REAX_DEVI void add_partials(const int4* const (&contrib)[kMaxContrib], int n, in
 // [n_tok, 2 n_tok) up, one column per token.  Every TMEM lane quarter then holds real rows even when
 // only a few tokens exist, so all four SM sub-partitions share the epilogue.
 template <int EPI_WARPS, int STAGES, int EPI, int MODE, bool ADD_F, bool SWAP>
-__global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+__global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     static_assert(!SWAP || (EPI == kEpiSwiglu && !ADD_F), "weight-major tiles: SwiGLU without BF16 columns");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -301,7 +315,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
     uint8_t* stage_b = smem + STAGES * kAStage;
     // per accumulator buffer: the tile's per-column scale and bias (token-major) or per-token scale
     // (weight-major), staged before the accumulator is ready
-    float* stage_sw = reinterpret_cast<float*>(stage_b + STAGES * kBStage);   // [2][kBN]
+    uint8_t* out_stage = stage_b + STAGES * kBStage;                           // [kSwapMaxTok][kBN / 2] bf16
+    float* stage_sw = reinterpret_cast<float*>(out_stage + kOutStageBytes);    // [2][kBN]
     float* stage_bias = stage_sw + 2 * kBN;                                    // [2][kBN]
     uint64_t* full = reinterpret_cast<uint64_t*>(stage_bias + 2 * kBN);
     uint64_t* empty = full + STAGES;
@@ -351,6 +366,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
     // bytes a stage receives: weight-major tiles load n_tok activation rows instead of 128
     const uint32_t stage_tx = SWAP ? static_cast<uint32_t>(kBStage + p.n_tok * kRowBytes) : kStageBytes;
 
+    if (warp < kCtlWarps) {
+    regs_shrink<kCtlRegs>();
     if (warp == 0) {
         // ------------------------------------------------------------------------------ TMA producer
         if (lane == 0) {
@@ -480,11 +497,24 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
             if (!mbar_wait_bounded(drain, 0, p.timeout_ns, nullptr)) atomicOr(p.status, kStatusTimeoutDrain);
         }
         __syncwarp();
-    } else {
+    }
+    // Teardown of the control warps; every role ends in its own copy, so no code runs under both
+    // register counts.
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+    return;
+    }
+
+    regs_grow<kEpiRegs>();
+    {
         // --------------------------------------------------------------------------------- epilogue
         // Epilogue warps only ever stop at the accumulator wait, and only on its own timeout (no abort
         // flag), so either all of them pass a segment or none does: the named barriers stay matched.
-        const int e = warp - 2;
+        const int e = warp - kCtlWarps;
         const int q = warp & 3;                      // TMEM lane quarter this warp may access
         const int r_tile = q * 32 + lane;            // accumulator row (= TMEM lane) of this thread
         constexpr int kSplit = EPI_WARPS / 4;        // warps sharing one lane quarter split the columns
@@ -509,20 +539,26 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
 
             if constexpr (SWAP) {
                 // ---------------------------------------------- weight-major tile: lanes are weight rows
+                constexpr int kTokW = kSwapMaxTok / 2;         // most tokens one warp finishes
                 const int n_tok = p.n_tok;
                 const int n0 = nt * (kBN / 2);                 // gate row (= output column) of lane 0
                 const int j = n0 + r_tile;                     // this thread's output column
-                const int tok_lo = (e / 4) * (n_tok / kSplit), tok_hi = tok_lo + n_tok / kSplit;
+                const int per_warp = n_tok / kSplit;
+                const int tok_lo = (e / 4) * per_warp, tok_hi = tok_lo + per_warp;
+                const int n_w = min(per_warp, p.M - tok_lo);   // real tokens of this warp (<= 0: none)
                 float swg = 0.f, swu = 0.f, bg = 0.f, bu = 0.f;
                 if constexpr (MODE == 0) {
                     swg = __ldg(p.sw + j);
                     swu = __ldg(p.sw + p.H + j);
                     bg = __ldg(p.bias + j);
                     bu = __ldg(p.bias + p.H + j);
-                    for (int t = threadIdx.x - 64; t < n_tok; t += EPI_WARPS * 32)
+                    for (int t = threadIdx.x - kCtlThreads; t < n_tok; t += EPI_WARPS * 32)
                         s_sw[t] = t < p.M ? __ldg(p.sa + t) : 0.f;
                     named_bar_sync(1, EPI_WARPS * 32);
                 }
+                // split tile: the other contributors' partial slots, resolved while the MMAs still run
+                const int4* contrib[kMaxContrib];
+                const int n_contrib = whole ? 0 : contributors(p, st, contrib);
                 if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
                     raise_error(p, abort_flag, kStatusTimeoutAccFull);
                     break;
@@ -535,64 +571,83 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
                                                            last_flag);
                 }
                 if (finish) {
-                    const int4* contrib[kMaxContrib];
-                    const int n_contrib = whole ? 0 : contributors(p, st, contrib);
-                    const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
-                    // this warp's tokens: up to 4 chunks of 8; all TMEM loads, then all partial loads, are
-                    // issued before any use, so the L2 round trips of the chunks overlap
-                    constexpr int kChunks = kSwapMaxTok / 2 / 8;
-                    const int tok_end = min(tok_hi, p.M);
-                    uint32_t g[kChunks][8], u[kChunks][8];
-#pragma unroll
-                    for (int c = 0; c < kChunks; ++c)
-                        if (tok_lo + 8 * c < tok_end)
-                            tmem_ld_x8_pair_sync(t_acc + tok_lo + 8 * c, t_acc + n_tok + tok_lo + 8 * c, g[c], u[c]);
+                    // this warp's gate and up accumulators (token columns tok_lo..), one TMEM round trip
+                    uint32_t g[kTokW], u[kTokW];
+                    if (per_warp > 8) tmem_ld2_x32_sync(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
+                    else tmem_ld_x8_pair_sync(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
                     for (int ci = 0; ci < n_contrib; ++ci) {
-                        int4 pg[kChunks][2], pu[kChunks][2];
+                        int4 pg[kTokW / 4], pu[kTokW / 4];
 #pragma unroll
-                        for (int c = 0; c < kChunks; ++c)
-                            if (tok_lo + 8 * c < tok_end) {
-#pragma unroll
-                                for (int h = 0; h < 2; ++h) {
-                                    pg[c][h] = __ldcg(contrib[ci] + ((tok_lo + 8 * c + 4 * h) / 4) * kBM + r_tile);
-                                    pu[c][h] = __ldcg(contrib[ci] + ((n_tok + tok_lo + 8 * c + 4 * h) / 4) * kBM + r_tile);
-                                }
+                        for (int c = 0; c < kTokW / 4; ++c)
+                            if (4 * c < n_w) {
+                                pg[c] = __ldcg(contrib[ci] + ((tok_lo + 4 * c) / 4) * kBM + r_tile);
+                                pu[c] = __ldcg(contrib[ci] + ((n_tok + tok_lo + 4 * c) / 4) * kBM + r_tile);
                             }
 #pragma unroll
-                        for (int c = 0; c < kChunks; ++c)
-                            if (tok_lo + 8 * c < tok_end) {
-#pragma unroll
-                                for (int h = 0; h < 2; ++h) {
-                                    g[c][4 * h] += pg[c][h].x; g[c][4 * h + 1] += pg[c][h].y;
-                                    g[c][4 * h + 2] += pg[c][h].z; g[c][4 * h + 3] += pg[c][h].w;
-                                    u[c][4 * h] += pu[c][h].x; u[c][4 * h + 1] += pu[c][h].y;
-                                    u[c][4 * h + 2] += pu[c][h].z; u[c][4 * h + 3] += pu[c][h].w;
-                                }
+                        for (int c = 0; c < kTokW / 4; ++c)
+                            if (4 * c < n_w) {
+                                g[4 * c] += pg[c].x; g[4 * c + 1] += pg[c].y; g[4 * c + 2] += pg[c].z; g[4 * c + 3] += pg[c].w;
+                                u[4 * c] += pu[c].x; u[4 * c + 1] += pu[c].y; u[4 * c + 2] += pu[c].z; u[4 * c + 3] += pu[c].w;
                             }
                     }
+                    // SwiGLU of every token pair by the approximation (no branch: the pairs' chains overlap),
+                    // then the values it does not settle, warp-wide through the exact formula
+                    const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
+                    uint64_t gb[kTokW / 2], ub[kTokW / 2];
+                    uint32_t o[kTokW / 2];
+                    uint32_t miss = 0;
 #pragma unroll
-                    for (int c = 0; c < kChunks; ++c) {
-                        if (tok_lo + 8 * c >= tok_end) continue;
-#pragma unroll
-                        for (int i = 0; i < 8; i += 2) {
-                            const int t = tok_lo + 8 * c + i;
-                            uint32_t o;
-                            if constexpr (MODE == 0) {
-                                const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sw + t);
-                                o = swiglu2(dequant2(g[c][i], g[c][i + 1], sa2, swg2, bg2),
-                                            dequant2(u[c][i], u[c][i + 1], sa2, swu2, bu2));
-                            } else {
-                                o = swiglu2(f2(__uint_as_float(g[c][i]), __uint_as_float(g[c][i + 1])),
-                                            f2(__uint_as_float(u[c][i]), __uint_as_float(u[c][i + 1])));
-                            }
-                            if (t < p.M) p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o & 0xFFFFu);
-                            if (t + 1 < p.M)
-                                p.out[static_cast<size_t>(t + 1) * p.ldo + j] = __ushort_as_bfloat16(o >> 16);
+                    for (int i = 0; i < kTokW / 2; ++i) {
+                        gb[i] = 0;
+                        ub[i] = 0;
+                        o[i] = 0;
+                        if (2 * i >= n_w) continue;
+                        uint64_t vg, vu;
+                        if constexpr (MODE == 0) {
+                            const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sw + tok_lo + 2 * i);
+                            vg = dequant2(g[2 * i], g[2 * i + 1], sa2, swg2, bg2);
+                            vu = dequant2(u[2 * i], u[2 * i + 1], sa2, swu2, bu2);
+                        } else {
+                            vg = f2(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
+                            vu = f2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
                         }
+                        gb[i] = bf16x2_to_f2(bf16x2_rn(vg));
+                        ub[i] = bf16x2_to_f2(bf16x2_rn(vu));
+                        uint32_t m2;
+                        o[i] = bf16x2_rn(mul2_rn(silu2_fast(f2_lo(gb[i]), f2_hi(gb[i]), m2), ub[i]));
+                        miss |= m2 << (2 * i);
                     }
-                    if (!whole) {
+                    swiglu_redo_warp(miss, gb, ub, o);
+                    if (p.out_vec16) {
+                        // the tile's [tokens x 128 columns] block goes through shared memory so that every
+                        // global store writes a whole 16-byte piece of a token row
+                        uint16_t* ot = reinterpret_cast<uint16_t*>(out_stage);
+#pragma unroll
+                        for (int i = 0; i < kTokW / 2; ++i)
+                            if (2 * i < n_w) {
+                                ot[(tok_lo + 2 * i) * (kBN / 2) + r_tile] = static_cast<uint16_t>(o[i] & 0xFFFFu);
+                                ot[(tok_lo + 2 * i + 1) * (kBN / 2) + r_tile] = static_cast<uint16_t>(o[i] >> 16);
+                            }
                         named_bar_sync(1, EPI_WARPS * 32);
-                        if (threadIdx.x == 64) p.ws_counters[st] = 0;
+                        if (!whole && threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
+                        for (int idx = threadIdx.x - kCtlThreads; idx < p.M * 16; idx += EPI_WARPS * 32) {
+                            const int t = idx >> 4, k = idx & 15;
+                            const uint4 v = *reinterpret_cast<const uint4*>(ot + t * (kBN / 2) + 8 * k);
+                            *reinterpret_cast<uint4*>(p.out + static_cast<size_t>(t) * p.ldo + n0 + 8 * k) = v;
+                        }
+                        named_bar_sync(1, EPI_WARPS * 32);   // the staging block is free again
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < kTokW / 2; ++i) {
+                            const int t = tok_lo + 2 * i;
+                            if (2 * i < n_w) p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o[i] & 0xFFFFu);
+                            if (2 * i + 1 < n_w)
+                                p.out[static_cast<size_t>(t + 1) * p.ldo + j] = __ushort_as_bfloat16(o[i] >> 16);
+                        }
+                        if (!whole) {
+                            named_bar_sync(1, EPI_WARPS * 32);
+                            if (threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
+                        }
                     }
                 }
             } else {
@@ -605,7 +660,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
                 // Stage this tile's column scales / biases and this row's scale while the MMAs still run.
                 float sa_row = 0.f;
                 if constexpr (MODE == 0) {
-                    for (int t = threadIdx.x - 64; t < kBN; t += EPI_WARPS * 32) {
+                    for (int t = threadIdx.x - kCtlThreads; t < kBN; t += EPI_WARPS * 32) {
                         int col;
                         if constexpr (EPI == kEpiSwiglu)
                             col = part * p.n_part_stride + nt * (kBN / 2) + (t < kBN / 2 ? t : p.H + t - kBN / 2);
@@ -645,14 +700,18 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
                             tmem_ld_x32_sync(t_acc + cc, g);
                             if constexpr (add_f) tmem_ld_x32_sync(t_f32 + cc, fg);
                         }
-                        if (!row_ok) continue;
-                        if (!whole) {
+                        if (__all_sync(0xFFFFFFFFu, !row_ok)) continue;   // warp-uniform: no row of this warp
+                        if (row_ok && !whole) {
                             add_partials<32>(contrib, n_contrib, cc, r_tile, g);
                             if constexpr (EPI == kEpiSwiglu) add_partials<32>(contrib, n_contrib, kBN / 2 + cc, r_tile, u);
                         }
                         uint32_t packed[16];
                         __nv_bfloat16* dst;
                         if constexpr (EPI == kEpiSwiglu) {
+                            // bf16 gate/up values of the 16 pairs, the approximation for all of them, then the
+                            // values it does not settle warp-wide through the exact formula (rows outside the
+                            // tile's range compute along and are never stored)
+                            uint64_t gb[16], ub[16];
 #pragma unroll
                             for (int i = 0; i < 32; i += 2) {
                                 uint64_t vg, vu;
@@ -671,8 +730,12 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
                                     vg = f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1]));
                                     vu = f2(__uint_as_float(u[i]), __uint_as_float(u[i + 1]));
                                 }
-                                packed[i / 2] = swiglu2(vg, vu);
+                                gb[i / 2] = bf16x2_to_f2(bf16x2_rn(vg));
+                                ub[i / 2] = bf16x2_to_f2(bf16x2_rn(vu));
                             }
+                            uint32_t miss = swiglu_fast_pairs(gb, ub, packed);
+                            if (!row_ok) miss = 0;
+                            swiglu_redo_warp(miss, gb, ub, packed);
                             dst = p.out + static_cast<size_t>(grow) * p.ldo + nt * (kBN / 2) + cc;
                         } else {
 #pragma unroll
@@ -690,14 +753,16 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
                             }
                             dst = p.out + out_part * p.out_part_stride + static_cast<size_t>(grow) * p.ldo + nt * kBN + cc;
                         }
+                        if (row_ok) {
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            reinterpret_cast<uint4*>(dst)[i] =
-                                make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                            for (int i = 0; i < 4; ++i)
+                                reinterpret_cast<uint4*>(dst)[i] =
+                                    make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                        }
                     }
                     if (!whole) {
                         named_bar_sync(1, EPI_WARPS * 32);
-                        if (threadIdx.x == 64) p.ws_counters[st] = 0;
+                        if (threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
                     }
                 }
             }
@@ -715,10 +780,6 @@ __global__ void __launch_bounds__(64 + 32 * EPI_WARPS, 1) tc_gemm_kernel(const _
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
-    }
 }
 
 }  // namespace reax
