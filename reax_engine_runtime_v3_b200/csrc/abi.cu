@@ -85,10 +85,11 @@ int variant_of(int epi, const reax::TcParams& p) {
     return p.mode == 1 ? kPlainBf16 : (p.kb_f16 > 0 ? kPlainI8F : kPlainI8);
 }
 
-// pipeline stages + weight-major output staging + 1 KiB alignment slack + staged column scales/biases
-// (2 x 2 x 256 floats) + barriers
+// pipeline stages + weight-major output staging + SiLU table + 1 KiB alignment slack + staged column
+// scales/biases (2 x 2 x 256 floats) + barriers
 constexpr size_t tc_smem_bytes() {
-    return static_cast<size_t>(kStages) * reax::kStageBytes + reax::kOutStageBytes + 1024 + 4096 + 256;
+    return static_cast<size_t>(kStages) * reax::kStageBytes + reax::kOutStageBytes + reax::kSiluTabBytes + 1024 +
+           4096 + 256;
 }
 
 // Current device, its SM count, and a check that it is sm_100; sets kernel attributes once.

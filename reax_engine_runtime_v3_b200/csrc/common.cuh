@@ -258,46 +258,56 @@ REAX_DEVI float bf16_round(float v) { return __bfloat162float(__float2bfloat16_r
 // float32: the arithmetic of the reference's silu_f32 (hybrid8_tiles.cuh:675).
 REAX_DEVI float silu_f32(float x) { return __fdiv_rn(x, 1.0f + expf(-x)); }
 
-// bf16(silu_f32(x)), bit-identical to rounding the accurate formula above, at a fraction of its cost.
-//
-// Ziv's rounding test.  A cheap approximation s ~ x * rcp(1 + 2^(-x log2 e)) is formed with the
-// hardware ex2 / rcp approximations; -x log2 e is carried as an unevaluated pair t_hi + t_lo (FMA-exact
-// product plus the constant's residual), so the approximation error is essentially that of ex2, rcp
-// and three roundings: about 2^-21 relative, i.e. <= 16 float32 ulps of s.  The accurate formula (CUDA
-// expf <= 2 ulp, two IEEE-rounded ops) is within about 2^-21.4 of silu(x) too, so both round to the
-// same bf16 value unless s lies within kSiluMargin ulps of a bf16 rounding midpoint (low 16 bits
-// 0x8000).  Then, and outside the fast domain, the accurate formula is evaluated.  Two saturated ends
-// are exact without evaluating it: for x >= 17, expf(-x) < 2^-24 so 1 + expf(-x) rounds to 1 and the
-// quotient is x; for x <= -89, expf(-x) overflows to +inf and x / inf = -0.
-// Only bf16 inputs reach this function; the 65536-pattern domain test checks every one of them.
-constexpr uint32_t kSiluMargin = 32;   // float32 ulps, about twice the error bound above
+// bf16(silu_f32(x)): the value the reference's SwiGLU multiplies by (hybrid8_tiles.cuh:676-678).
+REAX_DEVI float silu_bf16_value(float x) { return bf16_round(silu_f32(x)); }
 
-REAX_DEVI float silu_bf16_value(float x) {
-    constexpr float kNegLog2eHi = -1.44269502162933349609375f;          // float32(-log2 e)
-    constexpr float kNegLog2eLo = -1.925963033500011079e-08f;           // -log2 e - kNegLog2eHi
-    constexpr float kLn2 = 0.693147180559945309f;
-    if (x >= 17.0f && x <= 3.402823466e38f) return x;
-    if (x > -86.0f && x < 17.0f) {
-        const float t_hi = __fmul_rn(x, kNegLog2eHi);
-        const float t_lo = __fmaf_rn(x, kNegLog2eHi, -t_hi) + x * kNegLog2eLo;   // exact product residual
-        float e, r;
-        asm("ex2.approx.f32 %0, %1;" : "=f"(e) : "f"(t_hi));
-        e = __fmaf_rn(e, t_lo * kLn2, e);                                     // 2^t_lo ~ 1 + t_lo ln 2
-        const float d = __fadd_rn(1.0f, e);
-        asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(d));
-        const float s = __fmul_rn(x, r);
-        const uint32_t low = __float_as_uint(s) & 0xFFFFu;
-        const uint32_t dist = low > 0x8000u ? low - 0x8000u : 0x8000u - low;
-        if (dist > kSiluMargin) return bf16_round(s);
-    } else if (x <= -89.0f && x >= -3.402823466e38f) {
-        return -0.0f;
+// ------------------------------------------------------------------------------------------ SiLU table
+// For a bf16-valued x, bf16(silu_f32(x)) depends only on the 16-bit pattern of x, and outside the
+// exponent fields [kSiluTabElo, kSiluTabEhi] (|x| in [2^-10, 128)) it needs no table:
+//   |x| < 2^-10   -> bf16(x * 0.5): 1 + expf(-x) lies within 2^-10 of 2 - x, so the quotient is within
+//                    a relative 2^-11 of x / 2, which is a bf16 value (or rounds to the same bf16
+//                    subnormal as x * 0.5 does);
+//   x >= 128      -> x: expf(-x) < 2^-24, so 1 + expf(-x) rounds to 1;
+//   x <= -128     -> -0: expf(-x) overflows to +inf and x / inf = -0;
+//   +-inf, NaN    -> not settled here (exponent field 255): the caller evaluates silu_bf16_value.
+// The 2 x 17 x 128 patterns in between are tabulated by the exact formula (8.5 KiB of shared memory).
+// The test over all 65536 bf16 patterns compares this path with silu_bf16_value.
+constexpr uint32_t kSiluTabElo = 117;                                   // 2^-10
+constexpr uint32_t kSiluTabEhi = 133;                                   // [64, 128)
+constexpr uint32_t kSiluTabHalf = (kSiluTabEhi - kSiluTabElo + 1) * 128;  // patterns of one sign
+constexpr int kSiluTabBytes = static_cast<int>(2 * kSiluTabHalf * 2);
+
+// Fill the table: entry i < kSiluTabHalf is the positive pattern (kSiluTabElo << 7) + i, the rest the
+// negative ones in the same order.
+REAX_DEVI void silu_table_fill(uint16_t* tab, int tid, int nthreads) {
+    for (int i = tid; i < static_cast<int>(2 * kSiluTabHalf); i += nthreads) {
+        const uint32_t sign = static_cast<uint32_t>(i) >= kSiluTabHalf ? 0x8000u : 0u;
+        const uint32_t mag = static_cast<uint32_t>(i) % kSiluTabHalf + (kSiluTabElo << 7);
+        tab[i] = __bfloat16_as_ushort(__float2bfloat16_rn(silu_f32(__uint_as_float((sign | mag) << 16))));
     }
-    return bf16_round(silu_f32(x));
+}
+
+// bf16(silu_f32(x)) for a bf16-valued x through the table; `miss` is set for +-inf and NaN.
+REAX_DEVI float silu_tab(float x, const uint16_t* tab, bool& miss) {
+    const uint32_t b = __float_as_uint(x) >> 16;
+    const uint32_t mag = b & 0x7FFFu;
+    const uint32_t rel = mag - (kSiluTabElo << 7);        // wraps for |x| < 2^-10
+    const bool in_tab = rel < kSiluTabHalf;
+    const uint32_t idx = (in_tab ? rel : 0u) + ((b & 0x8000u) ? kSiluTabHalf : 0u);
+    const float t = __uint_as_float(static_cast<uint32_t>(tab[idx]) << 16);
+    const bool tiny = mag < (kSiluTabElo << 7);
+    const float small = bf16_round(__fmul_rn(x, 0.5f));
+    const float big = (b & 0x8000u) ? -0.0f : x;
+    miss = (mag & 0x7F80u) == 0x7F80u;
+    return in_tab ? t : (tiny ? small : big);
 }
 
 // out = bf16(float(bf16(silu_f32(g))) * u) for bf16-valued g and u (hybrid8_tiles.cuh:676-679).
-REAX_DEVI __nv_bfloat16 swiglu_bf16(float g_bf16_value, float u_bf16_value) {
-    return __float2bfloat16_rn(silu_bf16_value(g_bf16_value) * u_bf16_value);
+REAX_DEVI __nv_bfloat16 swiglu_bf16(float g_bf16_value, float u_bf16_value, const uint16_t* tab) {
+    bool miss;
+    float s = silu_tab(g_bf16_value, tab, miss);
+    if (miss) s = silu_bf16_value(g_bf16_value);
+    return __float2bfloat16_rn(__fmul_rn(s, u_bf16_value));
 }
 
 // ------------------------------------------------------------------------------------- packed float32 pairs
@@ -343,55 +353,29 @@ REAX_DEVI uint64_t dequant2(uint32_t a0, uint32_t a1, uint64_t sa2, uint64_t sw2
     return f2(v0, v1);
 }
 
-// bf16(silu_f32(x)) for two bf16-valued inputs, as a float32 pair, by the approximation alone.
-// Classes per lane: x >= 17 -> x; -inf < x <= -89 -> -0; -86 < x < 17 -> the approximation, accepted
-// when it passes the rounding test.  Bit i of `miss` is set when lane i is in none of these classes
-// (NaN, +-inf, (-89, -86], a failed test): its value must then come from silu_bf16_value.  No branch
-// and no call, so a caller can run many pairs side by side.
-REAX_DEVI uint64_t silu2_fast(float x0, float x1, uint32_t& miss) {
-    constexpr float kNegLog2eHi = -1.44269502162933349609375f;
-    constexpr float kNegLog2eLo = -1.925963033500011079e-08f;
-    constexpr float kLn2 = 0.693147180559945309f;
-    const uint64_t x2 = f2(fminf(fmaxf(x0, -86.0f), 17.0f), fminf(fmaxf(x1, -86.0f), 17.0f));
-    const uint64_t c_hi = f2(kNegLog2eHi, kNegLog2eHi);
-    const uint64_t t_hi = mul2_rn(x2, c_hi);
-    const uint64_t resid = fma2_rn(x2, c_hi, t_hi ^ 0x8000000080000000ull);       // x*C - t_hi, exact
-    const uint64_t t_lo = fma2_rn(x2, f2(kNegLog2eLo, kNegLog2eLo), resid);
-    float e0, e1, r0, r1;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(f2_lo(t_hi)));
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(f2_hi(t_hi)));
-    uint64_t e2 = f2(e0, e1);
-    e2 = fma2_rn(e2, mul2_rn(t_lo, f2(kLn2, kLn2)), e2);
-    const uint64_t d2 = add2_rn(f2(1.0f, 1.0f), e2);
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(f2_lo(d2)));
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(f2_hi(d2)));
-    const uint64_t s2 = mul2_rn(x2, f2(r0, r1));
-    const uint32_t b0 = static_cast<uint32_t>(s2), b1 = static_cast<uint32_t>(s2 >> 32);
-    // rounding test: |low 16 bits - 0x8000| > margin  <=>  ((bits - (0x8000 - margin)) & 0xFFFF) > 2 margin
-    const bool near0 = ((b0 - (0x8000u - kSiluMargin)) & 0xFFFFu) <= 2 * kSiluMargin;
-    const bool near1 = ((b1 - (0x8000u - kSiluMargin)) & 0xFFFFu) <= 2 * kSiluMargin;
-    const bool hi0 = x0 >= 17.0f, hi1 = x1 >= 17.0f;
-    const bool lo0 = x0 <= -89.0f && x0 > -INFINITY, lo1 = x1 <= -89.0f && x1 > -INFINITY;
-    const bool mid0 = x0 > -86.0f && x0 < 17.0f && !near0, mid1 = x1 > -86.0f && x1 < 17.0f && !near1;
-    const float s0 = hi0 ? x0 : (lo0 ? -0.0f : __uint_as_float(b0));
-    const float s1 = hi1 ? x1 : (lo1 ? -0.0f : __uint_as_float(b1));
-    miss = ((hi0 || lo0 || mid0) ? 0u : 1u) | ((hi1 || lo1 || mid1) ? 0u : 2u);
-    return bf16x2_to_f2(bf16x2_rn(f2(s0, s1)));
+// silu_tab of a pair; bit l of `miss` marks lane l as not settled (+-inf or NaN).
+REAX_DEVI uint64_t silu2_tab(uint64_t g2, const uint16_t* tab, uint32_t& miss) {
+    bool m0, m1;
+    const float s0 = silu_tab(f2_lo(g2), tab, m0);
+    const float s1 = silu_tab(f2_hi(g2), tab, m1);
+    miss = (m0 ? 1u : 0u) | (m1 ? 2u : 0u);
+    return f2(s0, s1);
 }
 
-// silu_bf16_value out of line: the exact path, reached only for the values silu2_fast does not settle.
+// silu_bf16_value out of line: the exact path, reached only for the values the table does not settle.
 __device__ __noinline__ float silu_bf16_exact(float x) { return silu_bf16_value(x); }
 
 // SwiGLU of PAIRS (gate, up) pairs whose gate and up values are already bf16-rounded (gb, ub):
-// o[i] = bf16x2 of bf16(silu(g) * u), lane-wise.  The approximation runs first for every pair; bit
-// 2i + l of the returned mask marks lane l of pair i as not settled.
+// o[i] = bf16x2 of bf16(silu(g) * u), lane-wise, through the table; bit 2i + l of the returned mask
+// marks lane l of pair i as not settled.
 template <int PAIRS>
-REAX_DEVI uint32_t swiglu_fast_pairs(const uint64_t (&gb)[PAIRS], const uint64_t (&ub)[PAIRS], uint32_t (&o)[PAIRS]) {
+REAX_DEVI uint32_t swiglu_tab_pairs(const uint64_t (&gb)[PAIRS], const uint64_t (&ub)[PAIRS], uint32_t (&o)[PAIRS],
+                                    const uint16_t* tab) {
     uint32_t miss = 0;
 #pragma unroll
     for (int i = 0; i < PAIRS; ++i) {
         uint32_t m2;
-        o[i] = bf16x2_rn(mul2_rn(silu2_fast(f2_lo(gb[i]), f2_hi(gb[i]), m2), ub[i]));
+        o[i] = bf16x2_rn(mul2_rn(silu2_tab(gb[i], tab, m2), ub[i]));
         miss |= m2 << (2 * i);
     }
     return miss;
@@ -421,12 +405,6 @@ REAX_DEVI void swiglu_redo_warp(uint32_t miss, const uint64_t (&gb)[PAIRS], cons
             }
         miss &= miss - 1u;
     }
-}
-
-// The same value through the accurate formula only (the domain reference for the test above).
-REAX_DEVI __nv_bfloat16 swiglu_bf16_accurate(float g_bf16_value, float u_bf16_value) {
-    const float s = bf16_round(silu_f32(g_bf16_value));
-    return __float2bfloat16_rn(s * u_bf16_value);
 }
 
 REAX_DEVI uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {

@@ -316,7 +316,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     // per accumulator buffer: the tile's per-column scale and bias (token-major) or per-token scale
     // (weight-major), staged before the accumulator is ready
     uint8_t* out_stage = stage_b + STAGES * kBStage;                           // [kSwapMaxTok][kBN / 2] bf16
-    float* stage_sw = reinterpret_cast<float*>(out_stage + kOutStageBytes);    // [2][kBN]
+    uint16_t* silu_tab_s = reinterpret_cast<uint16_t*>(out_stage + kOutStageBytes);   // SiLU table
+    float* stage_sw = reinterpret_cast<float*>(out_stage + kOutStageBytes + kSiluTabBytes);   // [2][kBN]
     float* stage_bias = stage_sw + 2 * kBN;                                    // [2][kBN]
     uint64_t* full = reinterpret_cast<uint64_t*>(stage_bias + 2 * kBN);
     uint64_t* empty = full + STAGES;
@@ -510,6 +511,11 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     }
 
     regs_grow<kEpiRegs>();
+    if constexpr (EPI == kEpiSwiglu) {
+        // the SiLU table, built while the first accumulator is still being computed
+        silu_table_fill(silu_tab_s, threadIdx.x - kCtlThreads, EPI_WARPS * 32);
+        named_bar_sync(1, EPI_WARPS * 32);
+    }
     {
         // --------------------------------------------------------------------------------- epilogue
         // Epilogue warps only ever stop at the accumulator wait, and only on its own timeout (no abort
@@ -590,8 +596,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                                 u[4 * c] += pu[c].x; u[4 * c + 1] += pu[c].y; u[4 * c + 2] += pu[c].z; u[4 * c + 3] += pu[c].w;
                             }
                     }
-                    // SwiGLU of every token pair by the approximation (no branch: the pairs' chains overlap),
-                    // then the values it does not settle, warp-wide through the exact formula
+                    // SwiGLU of every token pair through the SiLU table, then the values it does not settle
+                    // (+-inf, NaN) warp-wide through the exact formula
                     const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
                     uint64_t gb[kTokW / 2], ub[kTokW / 2];
                     uint32_t o[kTokW / 2];
@@ -614,7 +620,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         gb[i] = bf16x2_to_f2(bf16x2_rn(vg));
                         ub[i] = bf16x2_to_f2(bf16x2_rn(vu));
                         uint32_t m2;
-                        o[i] = bf16x2_rn(mul2_rn(silu2_fast(f2_lo(gb[i]), f2_hi(gb[i]), m2), ub[i]));
+                        o[i] = bf16x2_rn(mul2_rn(silu2_tab(gb[i], silu_tab_s, m2), ub[i]));
                         miss |= m2 << (2 * i);
                     }
                     swiglu_redo_warp(miss, gb, ub, o);
@@ -708,8 +714,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         uint32_t packed[16];
                         __nv_bfloat16* dst;
                         if constexpr (EPI == kEpiSwiglu) {
-                            // bf16 gate/up values of the 16 pairs, the approximation for all of them, then the
-                            // values it does not settle warp-wide through the exact formula (rows outside the
+                            // bf16 gate/up values of the 16 pairs, SiLU through the table, then the values it
+                            // does not settle (+-inf, NaN) warp-wide through the exact formula (rows outside the
                             // tile's range compute along and are never stored)
                             uint64_t gb[16], ub[16];
 #pragma unroll
@@ -733,7 +739,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                                 gb[i / 2] = bf16x2_to_f2(bf16x2_rn(vg));
                                 ub[i / 2] = bf16x2_to_f2(bf16x2_rn(vu));
                             }
-                            uint32_t miss = swiglu_fast_pairs(gb, ub, packed);
+                            uint32_t miss = swiglu_tab_pairs(gb, ub, packed, silu_tab_s);
                             if (!row_ok) miss = 0;
                             swiglu_redo_warp(miss, gb, ub, packed);
                             dst = p.out + static_cast<size_t>(grow) * p.ldo + nt * (kBN / 2) + cc;

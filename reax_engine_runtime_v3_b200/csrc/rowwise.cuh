@@ -256,6 +256,9 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __re
                                                        const __nv_bfloat16* __restrict__ u,
                                                        __nv_bfloat16* __restrict__ out, int rows, int cols,
                                                        long long gs, long long us) {
+    __shared__ uint16_t tab[kSiluTabBytes / 2];
+    silu_table_fill(tab, threadIdx.x, blockDim.x);
+    __syncthreads();
     grid_dependency_wait();
     const long long total = static_cast<long long>(rows) * cols;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -263,7 +266,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __re
         const long long r = i / cols, c = i % cols;
         const float gv = __bfloat162float(g[r * gs + c]);
         const float uv = __bfloat162float(u[r * us + c]);
-        out[i] = swiglu_bf16(gv, uv);
+        out[i] = swiglu_bf16(gv, uv, tab);
     }
 }
 
