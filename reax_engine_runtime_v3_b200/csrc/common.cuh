@@ -238,6 +238,37 @@ REAX_DEVI void tmem_ld2_x32_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[32], ui
         : "memory");
 }
 
+// Two 16-column loads and one wait.
+REAX_DEVI void tmem_ld2_x16_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[16], uint32_t (&b)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]),
+          "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15]),
+          "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]),
+          "=r"(b[8]), "=r"(b[9]), "=r"(b[10]), "=r"(b[11]), "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15])
+        : "r"(ta), "r"(tb)
+        : "memory");
+}
+
+// Gate and up accumulators of 2 * PAIRS token columns (8, 16 or 32) with one wait.
+template <int PAIRS>
+REAX_DEVI void tmem_ld_pairs_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[2 * PAIRS], uint32_t (&b)[2 * PAIRS]) {
+    static_assert(PAIRS == 4 || PAIRS == 8 || PAIRS == 16, "8, 16 or 32 columns");
+    if constexpr (PAIRS == 4) tmem_ld_x8_pair_sync(ta, tb, a, b);
+    else if constexpr (PAIRS == 8) tmem_ld2_x16_sync(ta, tb, a, b);
+    else tmem_ld2_x32_sync(ta, tb, a, b);
+}
+
+// Compile-time integer for generic lambdas.
+template <int N>
+struct IntC {
+    static constexpr int value = N;
+};
+
 // Named barrier over `count` threads (a multiple of 32).
 REAX_DEVI void named_bar_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
 
@@ -269,7 +300,10 @@ REAX_DEVI float silu_bf16_value(float x) { return bf16_round(silu_f32(x)); }
 //                    subnormal as x * 0.5 does);
 //   x >= 128      -> x: expf(-x) < 2^-24, so 1 + expf(-x) rounds to 1;
 //   x <= -128     -> -0: expf(-x) overflows to +inf and x / inf = -0;
-//   +-inf, NaN    -> not settled here (exponent field 255): the caller evaluates silu_bf16_value.
+//   +inf          -> +inf (+inf / (1 + 0));
+//   -inf, NaN     -> NaN (-inf / +inf, or a NaN operand).  Every NaN the reference can produce here is
+//                    multiplied by u next, which gives the canonical NaN whatever the payload, so
+//                    one NaN serves for all of them.
 // The 2 x 17 x 128 patterns in between are tabulated by the exact formula (8.5 KiB of shared memory).
 // The test over all 65536 bf16 patterns compares this path with silu_bf16_value.
 constexpr uint32_t kSiluTabElo = 117;                                   // 2^-10
@@ -287,8 +321,8 @@ REAX_DEVI void silu_table_fill(uint16_t* tab, int tid, int nthreads) {
     }
 }
 
-// bf16(silu_f32(x)) for a bf16-valued x through the table; `miss` is set for +-inf and NaN.
-REAX_DEVI float silu_tab(float x, const uint16_t* tab, bool& miss) {
+// bf16(silu_f32(x)) for a bf16-valued x through the table.
+REAX_DEVI float silu_tab(float x, const uint16_t* tab) {
     const uint32_t b = __float_as_uint(x) >> 16;
     const uint32_t mag = b & 0x7FFFu;
     const uint32_t rel = mag - (kSiluTabElo << 7);        // wraps for |x| < 2^-10
@@ -297,17 +331,14 @@ REAX_DEVI float silu_tab(float x, const uint16_t* tab, bool& miss) {
     const float t = __uint_as_float(static_cast<uint32_t>(tab[idx]) << 16);
     const bool tiny = mag < (kSiluTabElo << 7);
     const float small = bf16_round(__fmul_rn(x, 0.5f));
-    const float big = (b & 0x8000u) ? -0.0f : x;
-    miss = (mag & 0x7F80u) == 0x7F80u;
+    const bool special = (mag & 0x7F80u) == 0x7F80u;      // +-inf, NaN
+    const float big = special ? (x > 0.0f ? x : __uint_as_float(0x7FFFFFFFu)) : ((b & 0x8000u) ? -0.0f : x);
     return in_tab ? t : (tiny ? small : big);
 }
 
 // out = bf16(float(bf16(silu_f32(g))) * u) for bf16-valued g and u (hybrid8_tiles.cuh:676-679).
 REAX_DEVI __nv_bfloat16 swiglu_bf16(float g_bf16_value, float u_bf16_value, const uint16_t* tab) {
-    bool miss;
-    float s = silu_tab(g_bf16_value, tab, miss);
-    if (miss) s = silu_bf16_value(g_bf16_value);
-    return __float2bfloat16_rn(__fmul_rn(s, u_bf16_value));
+    return __float2bfloat16_rn(__fmul_rn(silu_tab(g_bf16_value, tab), u_bf16_value));
 }
 
 // ------------------------------------------------------------------------------------- packed float32 pairs
@@ -353,58 +384,12 @@ REAX_DEVI uint64_t dequant2(uint32_t a0, uint32_t a1, uint64_t sa2, uint64_t sw2
     return f2(v0, v1);
 }
 
-// silu_tab of a pair; bit l of `miss` marks lane l as not settled (+-inf or NaN).
-REAX_DEVI uint64_t silu2_tab(uint64_t g2, const uint16_t* tab, uint32_t& miss) {
-    bool m0, m1;
-    const float s0 = silu_tab(f2_lo(g2), tab, m0);
-    const float s1 = silu_tab(f2_hi(g2), tab, m1);
-    miss = (m0 ? 1u : 0u) | (m1 ? 2u : 0u);
-    return f2(s0, s1);
-}
+// silu_tab of a pair.
+REAX_DEVI uint64_t silu2_tab(uint64_t g2, const uint16_t* tab) { return f2(silu_tab(f2_lo(g2), tab), silu_tab(f2_hi(g2), tab)); }
 
-// silu_bf16_value out of line: the exact path, reached only for the values the table does not settle.
-__device__ __noinline__ float silu_bf16_exact(float x) { return silu_bf16_value(x); }
-
-// SwiGLU of PAIRS (gate, up) pairs whose gate and up values are already bf16-rounded (gb, ub):
-// o[i] = bf16x2 of bf16(silu(g) * u), lane-wise, through the table; bit 2i + l of the returned mask
-// marks lane l of pair i as not settled.
-template <int PAIRS>
-REAX_DEVI uint32_t swiglu_tab_pairs(const uint64_t (&gb)[PAIRS], const uint64_t (&ub)[PAIRS], uint32_t (&o)[PAIRS],
-                                    const uint16_t* tab) {
-    uint32_t miss = 0;
-#pragma unroll
-    for (int i = 0; i < PAIRS; ++i) {
-        uint32_t m2;
-        o[i] = bf16x2_rn(mul2_rn(silu2_tab(gb[i], tab, m2), ub[i]));
-        miss |= m2 << (2 * i);
-    }
-    return miss;
-}
-
-// Redo the values marked in `miss` through the exact formula, warp-wide: in every round each lane takes
-// its lowest marked value and the whole warp evaluates silu_bf16_exact once, converged, so a warp pays
-// one exact evaluation per round (rounds = the most marked values of any one lane) instead of one per
-// marked value index.  All 32 lanes of the warp must call it together.
-template <int PAIRS>
-REAX_DEVI void swiglu_redo_warp(uint32_t miss, const uint64_t (&gb)[PAIRS], const uint64_t (&ub)[PAIRS],
-                                uint32_t (&o)[PAIRS]) {
-    static_assert(PAIRS <= 16, "one 32-bit mask");
-    while (__any_sync(0xFFFFFFFFu, miss != 0u)) {
-        const int v = miss ? __ffs(static_cast<int>(miss)) - 1 : -1;
-        float x = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 2 * PAIRS; ++i)
-            if (v == i) x = (i & 1) ? f2_hi(gb[i >> 1]) : f2_lo(gb[i >> 1]);
-        const float s = silu_bf16_exact(x);
-#pragma unroll
-        for (int i = 0; i < 2 * PAIRS; ++i)
-            if (v == i) {
-                const float uu = (i & 1) ? f2_hi(ub[i >> 1]) : f2_lo(ub[i >> 1]);
-                const uint32_t h = __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn(s, uu)));
-                o[i >> 1] = (i & 1) ? ((o[i >> 1] & 0xFFFFu) | (h << 16)) : ((o[i >> 1] & 0xFFFF0000u) | h);
-            }
-        miss &= miss - 1u;
-    }
+// SwiGLU of a (gate, up) pair whose values are already bf16-rounded: bf16x2 of bf16(silu(g) * u).
+REAX_DEVI uint32_t swiglu2_tab(uint64_t gb, uint64_t ub, const uint16_t* tab) {
+    return bf16x2_rn(mul2_rn(silu2_tab(gb, tab), ub));
 }
 
 REAX_DEVI uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {

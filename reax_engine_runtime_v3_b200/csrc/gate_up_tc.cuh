@@ -37,6 +37,9 @@ constexpr int kTmemCols = 512;
 constexpr int kSlotInts = kBM * kBN;            // one split-tile partial: 128 x 256 int32 (128 KiB)
 constexpr int kSwapMaxTok = 64;                 // weight-major tiles: at most 64 token columns per accumulator
 constexpr int kOutStageBytes = kSwapMaxTok * (kBN / 2) * 2;   // weight-major output block staged for the stores
+// How long the contributor holding a split tile's first K blocks waits for the others to publish
+// before it publishes itself (a performance choice; both paths give the same result).
+constexpr unsigned long long kFinisherWaitNs = 10000;
 
 // Thread layout: warp 0 issues the TMA copies, warp 1 the MMAs (it also owns TMEM), warps 2-3 only hand
 // their registers over, and warps kCtlWarps.. run the epilogue.  Warp w runs on SM sub-partition w % 4,
@@ -266,6 +269,37 @@ REAX_DEVI bool publish_partial(const TcParams& p, const Segment& seg, int st, ui
     const bool finish = *reinterpret_cast<volatile int*>(last_flag) != 0;
     if (finish) __threadfence();
     return finish;
+}
+
+// Wait, for at most limit_ns, until every other contributor of split tile st has counted its K blocks;
+// then this CTA completes the tile without publishing (nobody else can reach KB any more) and the
+// contributors' partials are visible to all its epilogue threads.  Only the contributor holding the
+// tile's first K blocks calls it: in stream-K order those are the last K blocks of its range, while
+// every other contributor reaches this tile earlier in its own range and publishes without waiting,
+// so no two CTAs ever wait on each other.  When the limit passes (a contributor not resident yet, say)
+// the caller publishes like any other contributor.  All epilogue threads call it.
+template <int EPI_WARPS>
+REAX_DEVI bool wait_others_counted(const TcParams& p, const Segment& seg, int st, int* last_flag, uint64_t limit_ns) {
+    const int KB = p.kb_int + p.kb_f16;
+    if (threadIdx.x == kCtlThreads) {
+        const int need = KB - (seg.k1 - seg.k0);
+        const uint64_t t0 = global_timer_ns();
+        int done = 0;
+        while (true) {
+            if (ld_acquire_gpu(p.ws_counters + st) == need) {
+                done = 1;
+                break;
+            }
+            if (global_timer_ns() - t0 > limit_ns) break;
+            __nanosleep(100);
+        }
+        *last_flag = done;
+    }
+    named_bar_sync(1, EPI_WARPS * 32);
+    const bool complete = *reinterpret_cast<volatile int*>(last_flag) != 0;
+    named_bar_sync(1, EPI_WARPS * 32);   // every thread has read the flag before it is reused
+    if (complete) __threadfence();
+    return complete;
 }
 
 // Slots of a split tile's other contributors (CTA order), resolved once per tile.
@@ -545,19 +579,20 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 
             if constexpr (SWAP) {
                 // ---------------------------------------------- weight-major tile: lanes are weight rows
-                constexpr int kTokW = kSwapMaxTok / 2;         // most tokens one warp finishes
                 const int n_tok = p.n_tok;
                 const int n0 = nt * (kBN / 2);                 // gate row (= output column) of lane 0
                 const int j = n0 + r_tile;                     // this thread's output column
-                const int per_warp = n_tok / kSplit;
+                const int per_warp = n_tok / kSplit;           // token columns each warp finishes
                 const int tok_lo = (e / 4) * per_warp, tok_hi = tok_lo + per_warp;
-                const int n_w = min(per_warp, p.M - tok_lo);   // real tokens of this warp (<= 0: none)
+                const int n_w = min(per_warp, p.M - tok_lo);   // real tokens among them (<= 0: none)
                 float swg = 0.f, swu = 0.f, bg = 0.f, bu = 0.f;
                 if constexpr (MODE == 0) {
                     swg = __ldg(p.sw + j);
                     swu = __ldg(p.sw + p.H + j);
                     bg = __ldg(p.bias + j);
                     bu = __ldg(p.bias + p.H + j);
+                    // land the loads now, while the MMAs run, not at their first use after the wait
+                    asm volatile("" ::"f"(swg), "f"(swu), "f"(bg), "f"(bu));
                     for (int t = threadIdx.x - kCtlThreads; t < n_tok; t += EPI_WARPS * 32)
                         s_sw[t] = t < p.M ? __ldg(p.sa + t) : 0.f;
                     named_bar_sync(1, EPI_WARPS * 32);
@@ -565,75 +600,93 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 // split tile: the other contributors' partial slots, resolved while the MMAs still run
                 const int4* contrib[kMaxContrib];
                 const int n_contrib = whole ? 0 : contributors(p, st, contrib);
-                if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
-                    raise_error(p, abort_flag, kStatusTimeoutAccFull);
-                    break;
-                }
-                tc_fence_after();
-                bool finish = whole;
-                if (!whole) {
-                    // the gate columns of this warp's token range and the matching up columns
-                    finish = publish_partial<EPI_WARPS, 8>(p, seg, st, t_acc, tok_lo, tok_hi, n_tok, r_tile, true,
-                                                           last_flag);
-                }
-                if (finish) {
-                    // this warp's gate and up accumulators (token columns tok_lo..), one TMEM round trip
-                    uint32_t g[kTokW], u[kTokW];
-                    if (per_warp > 8) tmem_ld2_x32_sync(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
-                    else tmem_ld_x8_pair_sync(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
-                    for (int ci = 0; ci < n_contrib; ++ci) {
-                        int4 pg[kTokW / 4], pu[kTokW / 4];
+
+                // The segment, specialised on the pairs of token columns a warp finishes (per_warp
+                // rounded up to 8, 16 or 32): no branch separates the pairs, so their chains overlap;
+                // columns past the warp's real tokens compute on padding and are never stored.
+                auto segment = [&](auto pairs_c) -> bool {
+                    constexpr int PAIRS = decltype(pairs_c)::value;
+                    int4 qg[PAIRS / 2], qu[PAIRS / 2];   // the first contributor's partial of these columns
+                    auto fetch_first = [&]() {
 #pragma unroll
-                        for (int c = 0; c < kTokW / 4; ++c)
-                            if (4 * c < n_w) {
+                        for (int c = 0; c < PAIRS / 2; ++c) {
+                            qg[c] = __ldcg(contrib[0] + ((tok_lo + 4 * c) / 4) * kBM + r_tile);
+                            qu[c] = __ldcg(contrib[0] + ((n_tok + tok_lo + 4 * c) / 4) * kBM + r_tile);
+                        }
+                    };
+                    // The contributor holding the tile's first K blocks waits (bounded) for the others
+                    // instead of publishing, and fetches the first one's partial while its own last MMAs
+                    // still run.
+                    bool early = false;
+                    if (!whole && seg.k0 == 0) {
+                        early = wait_others_counted<EPI_WARPS>(p, seg, st, last_flag, kFinisherWaitNs);
+                        if (early && n_contrib > 0) fetch_first();
+                    }
+                    if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
+                        raise_error(p, abort_flag, kStatusTimeoutAccFull);
+                        return false;
+                    }
+                    tc_fence_after();
+                    bool finish = whole || early;
+                    if (!finish) {
+                        // the gate columns of this warp's token range and the matching up columns
+                        finish = publish_partial<EPI_WARPS, 8>(p, seg, st, t_acc, tok_lo, tok_hi, n_tok, r_tile, true,
+                                                               last_flag);
+                        if (finish && n_contrib > 0) fetch_first();
+                    }
+                    if (!finish) return true;
+                    uint32_t o[PAIRS];
+                    if (n_w > 0) {
+                        uint32_t g[2 * PAIRS], u[2 * PAIRS];
+                        tmem_ld_pairs_sync<PAIRS>(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
+                        if (n_contrib > 0) {
+#pragma unroll
+                            for (int c = 0; c < PAIRS / 2; ++c) {
+                                g[4 * c] += qg[c].x; g[4 * c + 1] += qg[c].y; g[4 * c + 2] += qg[c].z; g[4 * c + 3] += qg[c].w;
+                                u[4 * c] += qu[c].x; u[4 * c + 1] += qu[c].y; u[4 * c + 2] += qu[c].z; u[4 * c + 3] += qu[c].w;
+                            }
+                        }
+                        for (int ci = 1; ci < n_contrib; ++ci) {
+                            int4 pg[PAIRS / 2], pu[PAIRS / 2];
+#pragma unroll
+                            for (int c = 0; c < PAIRS / 2; ++c) {
                                 pg[c] = __ldcg(contrib[ci] + ((tok_lo + 4 * c) / 4) * kBM + r_tile);
                                 pu[c] = __ldcg(contrib[ci] + ((n_tok + tok_lo + 4 * c) / 4) * kBM + r_tile);
                             }
 #pragma unroll
-                        for (int c = 0; c < kTokW / 4; ++c)
-                            if (4 * c < n_w) {
+                            for (int c = 0; c < PAIRS / 2; ++c) {
                                 g[4 * c] += pg[c].x; g[4 * c + 1] += pg[c].y; g[4 * c + 2] += pg[c].z; g[4 * c + 3] += pg[c].w;
                                 u[4 * c] += pu[c].x; u[4 * c + 1] += pu[c].y; u[4 * c + 2] += pu[c].z; u[4 * c + 3] += pu[c].w;
                             }
-                    }
-                    // SwiGLU of every token pair through the SiLU table, then the values it does not settle
-                    // (+-inf, NaN) warp-wide through the exact formula
-                    const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
-                    uint64_t gb[kTokW / 2], ub[kTokW / 2];
-                    uint32_t o[kTokW / 2];
-                    uint32_t miss = 0;
-#pragma unroll
-                    for (int i = 0; i < kTokW / 2; ++i) {
-                        gb[i] = 0;
-                        ub[i] = 0;
-                        o[i] = 0;
-                        if (2 * i >= n_w) continue;
-                        uint64_t vg, vu;
-                        if constexpr (MODE == 0) {
-                            const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sw + tok_lo + 2 * i);
-                            vg = dequant2(g[2 * i], g[2 * i + 1], sa2, swg2, bg2);
-                            vu = dequant2(u[2 * i], u[2 * i + 1], sa2, swu2, bu2);
-                        } else {
-                            vg = f2(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
-                            vu = f2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
                         }
-                        gb[i] = bf16x2_to_f2(bf16x2_rn(vg));
-                        ub[i] = bf16x2_to_f2(bf16x2_rn(vu));
-                        uint32_t m2;
-                        o[i] = bf16x2_rn(mul2_rn(silu2_tab(gb[i], silu_tab_s, m2), ub[i]));
-                        miss |= m2 << (2 * i);
+                        // SwiGLU of every token pair through the SiLU table
+                        const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
+#pragma unroll
+                        for (int i = 0; i < PAIRS; ++i) {
+                            uint64_t vg, vu;
+                            if constexpr (MODE == 0) {
+                                const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sw + tok_lo + 2 * i);
+                                vg = dequant2(g[2 * i], g[2 * i + 1], sa2, swg2, bg2);
+                                vu = dequant2(u[2 * i], u[2 * i + 1], sa2, swu2, bu2);
+                            } else {
+                                vg = f2(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
+                                vu = f2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
+                            }
+                            o[i] = swiglu2_tab(bf16x2_to_f2(bf16x2_rn(vg)), bf16x2_to_f2(bf16x2_rn(vu)), silu_tab_s);
+                        }
                     }
-                    swiglu_redo_warp(miss, gb, ub, o);
                     if (p.out_vec16) {
                         // the tile's [tokens x 128 columns] block goes through shared memory so that every
                         // global store writes a whole 16-byte piece of a token row
                         uint16_t* ot = reinterpret_cast<uint16_t*>(out_stage);
+                        if (n_w > 0) {
 #pragma unroll
-                        for (int i = 0; i < kTokW / 2; ++i)
-                            if (2 * i < n_w) {
-                                ot[(tok_lo + 2 * i) * (kBN / 2) + r_tile] = static_cast<uint16_t>(o[i] & 0xFFFFu);
-                                ot[(tok_lo + 2 * i + 1) * (kBN / 2) + r_tile] = static_cast<uint16_t>(o[i] >> 16);
-                            }
+                            for (int i = 0; i < PAIRS; ++i)
+                                if (2 * PAIRS == per_warp || 2 * i < per_warp) {
+                                    ot[(tok_lo + 2 * i) * (kBN / 2) + r_tile] = static_cast<uint16_t>(o[i] & 0xFFFFu);
+                                    ot[(tok_lo + 2 * i + 1) * (kBN / 2) + r_tile] = static_cast<uint16_t>(o[i] >> 16);
+                                }
+                        }
                         named_bar_sync(1, EPI_WARPS * 32);
                         if (!whole && threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
                         for (int idx = threadIdx.x - kCtlThreads; idx < p.M * 16; idx += EPI_WARPS * 32) {
@@ -643,19 +696,27 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         }
                         named_bar_sync(1, EPI_WARPS * 32);   // the staging block is free again
                     } else {
+                        if (n_w > 0) {
 #pragma unroll
-                        for (int i = 0; i < kTokW / 2; ++i) {
-                            const int t = tok_lo + 2 * i;
-                            if (2 * i < n_w) p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o[i] & 0xFFFFu);
-                            if (2 * i + 1 < n_w)
-                                p.out[static_cast<size_t>(t + 1) * p.ldo + j] = __ushort_as_bfloat16(o[i] >> 16);
+                            for (int i = 0; i < PAIRS; ++i) {
+                                const int t = tok_lo + 2 * i;
+                                if (2 * i < n_w) p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o[i] & 0xFFFFu);
+                                if (2 * i + 1 < n_w)
+                                    p.out[static_cast<size_t>(t + 1) * p.ldo + j] = __ushort_as_bfloat16(o[i] >> 16);
+                            }
                         }
                         if (!whole) {
                             named_bar_sync(1, EPI_WARPS * 32);
                             if (threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
                         }
                     }
-                }
+                    return true;
+                };
+                bool ok;
+                if (per_warp <= 8) ok = segment(IntC<4>{});
+                else if (per_warp <= 16) ok = segment(IntC<8>{});
+                else ok = segment(IntC<16>{});
+                if (!ok) break;
             } else {
                 // ------------------------------------------------ token-major tile: lanes are token rows
                 constexpr int kCols = (EPI == kEpiSwiglu) ? kBN / 2 : kBN;   // output columns of a tile
@@ -706,18 +767,15 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             tmem_ld_x32_sync(t_acc + cc, g);
                             if constexpr (add_f) tmem_ld_x32_sync(t_f32 + cc, fg);
                         }
-                        if (__all_sync(0xFFFFFFFFu, !row_ok)) continue;   // warp-uniform: no row of this warp
-                        if (row_ok && !whole) {
+                        if (!row_ok) continue;
+                        if (!whole) {
                             add_partials<32>(contrib, n_contrib, cc, r_tile, g);
                             if constexpr (EPI == kEpiSwiglu) add_partials<32>(contrib, n_contrib, kBN / 2 + cc, r_tile, u);
                         }
                         uint32_t packed[16];
                         __nv_bfloat16* dst;
                         if constexpr (EPI == kEpiSwiglu) {
-                            // bf16 gate/up values of the 16 pairs, SiLU through the table, then the values it
-                            // does not settle (+-inf, NaN) warp-wide through the exact formula (rows outside the
-                            // tile's range compute along and are never stored)
-                            uint64_t gb[16], ub[16];
+                            // bf16 gate/up values of the 16 pairs, SiLU through the table
 #pragma unroll
                             for (int i = 0; i < 32; i += 2) {
                                 uint64_t vg, vu;
@@ -736,12 +794,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                                     vg = f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1]));
                                     vu = f2(__uint_as_float(u[i]), __uint_as_float(u[i + 1]));
                                 }
-                                gb[i / 2] = bf16x2_to_f2(bf16x2_rn(vg));
-                                ub[i / 2] = bf16x2_to_f2(bf16x2_rn(vu));
+                                packed[i / 2] = swiglu2_tab(bf16x2_to_f2(bf16x2_rn(vg)), bf16x2_to_f2(bf16x2_rn(vu)), silu_tab_s);
                             }
-                            uint32_t miss = swiglu_tab_pairs(gb, ub, packed, silu_tab_s);
-                            if (!row_ok) miss = 0;
-                            swiglu_redo_warp(miss, gb, ub, packed);
                             dst = p.out + static_cast<size_t>(grow) * p.ldo + nt * (kBN / 2) + cc;
                         } else {
 #pragma unroll
@@ -759,12 +813,10 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             }
                             dst = p.out + out_part * p.out_part_stride + static_cast<size_t>(grow) * p.ldo + nt * kBN + cc;
                         }
-                        if (row_ok) {
 #pragma unroll
-                            for (int i = 0; i < 4; ++i)
-                                reinterpret_cast<uint4*>(dst)[i] =
-                                    make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-                        }
+                        for (int i = 0; i < 4; ++i)
+                            reinterpret_cast<uint4*>(dst)[i] =
+                                make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
                     }
                     if (!whole) {
                         named_bar_sync(1, EPI_WARPS * 32);
