@@ -217,6 +217,13 @@ void plan_schedule(reax::TcParams& p, int sms, bool allow_split, int* grid) {
     }
     p.dp_tiles = T > sms ? (T / sms - 1) * sms : 0;
     p.sk_iters = static_cast<long long>(T - p.dp_tiles) * KB;
+    if (p.sk_iters * (sms + 1) >= (1LL << 31)) {
+        // the kernel's stream-K range arithmetic is 32-bit: deal every tile whole instead
+        p.dp_tiles = T;
+        p.sk_iters = 0;
+        *grid = T < sms ? T : sms;
+        return;
+    }
     long long g = sms;
     if (p.dp_tiles == 0) {
         // at least two K blocks per CTA
@@ -224,6 +231,17 @@ void plan_schedule(reax::TcParams& p, int sms, bool allow_split, int* grid) {
         if (cap < g) g = cap < 1 ? 1 : cap;
     }
     *grid = static_cast<int>(g);
+}
+
+// Weight-major tiles: gate rows per tile.  With 128 rows there are ceil(H / 128) tiles; when they leave a
+// partial wave of at least half the SMs, an even share R = ceil(H / (waves * SMs)) <= 128 rows per tile
+// fills whole waves instead, so no tile is split by K.  The TMA box then covers R weight rows, the MMA
+// still computes 128 (rows past R are never stored), and the weight bytes read stay the same.
+int swap_rows_for(int H, int sms) {
+    const int t128 = (H + 127) / 128;
+    if (t128 % sms == 0 || 2 * t128 < sms) return 128;
+    const int waves = (t128 + sms - 1) / sms;
+    return (H + waves * sms - 1) / (waves * sms);
 }
 
 int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
@@ -249,6 +267,7 @@ void init_params(reax::TcParams& p) {
     p.acc_bufs = 2;
     p.timeout_ns = g_timeout_ns;
     p.parts = 1;
+    p.swap_rows = 128;
 }
 
 // Plain launch (no attributes) whose error comes from the launch call itself, so no sticky error
@@ -452,11 +471,15 @@ int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, const void
     // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
     const bool swap = KH == 0 && M <= kSwapMaxRows;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
-    p.out_vec16 = 1;   // out 16-byte aligned and ldo % 8 == 0, checked above
+    p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
+    // out 16-byte aligned and ldo % 8 == 0 (checked above); weight-major rows are staged as 128-column blocks
+    p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
     if (KL) {
         if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
             return rc;
-        if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, swap ? p.swap_rows : 128)) !=
+            REAX_OK)
+            return rc;
     }
     if (KH) {
         if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH)) != REAX_OK) return rc;
@@ -480,7 +503,7 @@ int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, const void
     p.kb_int = KL / 128;
     p.kb_f16 = KH / 64;
     p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
-    p.n_tiles = (N2 / 2) / (reax::kBN / 2);
+    p.n_tiles = (N2 / 2 + p.swap_rows - 1) / p.swap_rows;
     p.tiles = p.m_tiles * p.n_tiles;
     p.mode = 0;
     p.acc_bufs = KH ? 1 : 2;
@@ -489,7 +512,7 @@ int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, const void
     p.status = ws.status;
     p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
     int grid = 0;
-    plan_schedule(p, info->sms, KH == 0, &grid);
+    plan_schedule(p, info->sms, KH == 0 && p.swap_rows == 128, &grid);
     return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
 }
 
@@ -513,10 +536,14 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     init_params(p);
     const bool swap = M <= kSwapMaxRows;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
-    p.out_vec16 = 1;   // out 16-byte aligned and ldo % 8 == 0, checked above
+    p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
+    // out 16-byte aligned and ldo % 8 == 0 (checked above); weight-major rows are staged as 128-column blocks
+    p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
     if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : 128)) != REAX_OK)
         return rc;
-    if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K)) != REAX_OK) return rc;
+    if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K, swap ? p.swap_rows : 128)) !=
+        REAX_OK)
+        return rc;
     p.tm_a = p.tm_ah;
     p.tm_b = p.tm_bh;
     p.out = static_cast<__nv_bfloat16*>(out);
@@ -526,7 +553,7 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     p.kb_int = 0;
     p.kb_f16 = K / 64;
     p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
-    p.n_tiles = (N2 / 2) / (reax::kBN / 2);
+    p.n_tiles = (N2 / 2 + p.swap_rows - 1) / p.swap_rows;
     p.tiles = p.m_tiles * p.n_tiles;
     p.mode = 1;
     p.acc_bufs = 2;
@@ -708,10 +735,13 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     init_params(p);
     const bool swap = KH == 0 && M <= kSwapMaxRows;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
-    p.out_vec16 = 1;   // out 16-byte aligned and ldo % 8 == 0, checked above
+    p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
+    // out 16-byte aligned and ldo % 8 == 0 (checked above); weight-major rows are staged as 128-column blocks
+    p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
     if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
         return rc;
-    if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL)) != REAX_OK) return rc;
+    if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, swap ? p.swap_rows : 128)) != REAX_OK)
+        return rc;
     if (KH) {
         if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH)) != REAX_OK) return rc;
         if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH)) != REAX_OK) return rc;
@@ -729,7 +759,7 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     p.kb_int = KL / 128;
     p.kb_f16 = KH / 64;
     p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
-    p.n_tiles = (N2 / 2) / (reax::kBN / 2);
+    p.n_tiles = (N2 / 2 + p.swap_rows - 1) / p.swap_rows;
     p.tiles = p.m_tiles * p.n_tiles;
     p.mode = 0;
     p.acc_bufs = KH ? 1 : 2;
@@ -737,7 +767,7 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     // Whole-tile plans need no partials; a plan that splits tiles is re-planned for at most
     // kNoAllocMaxCtas CTAs, whose partials the static scratch holds.
     int grid = 0;
-    plan_schedule(p, info->sms, KH == 0, &grid);
+    plan_schedule(p, info->sms, KH == 0 && p.swap_rows == 128, &grid);
     int ctas = grid;
     if (p.sk_iters > 0 && grid > kNoAllocMaxCtas) {
         plan_schedule(p, kNoAllocMaxCtas, true, &grid);

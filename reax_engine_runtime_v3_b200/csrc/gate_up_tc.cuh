@@ -37,7 +37,7 @@ constexpr int kTmemCols = 512;
 constexpr int kSlotInts = kBM * kBN;            // one split-tile partial: 128 x 256 int32 (128 KiB)
 constexpr int kSwapMaxTok = 64;                 // weight-major tiles: at most 64 token columns per accumulator
 constexpr int kOutStageBytes = kSwapMaxTok * (kBN / 2) * 2;   // weight-major output block staged for the stores
-// How long the contributor holding a split tile's first K blocks waits for the others to publish
+// How long the contributor holding a split tile's last K blocks waits for the others to publish
 // before it publishes itself (a performance choice; both paths give the same result).
 constexpr unsigned long long kFinisherWaitNs = 10000;
 
@@ -87,6 +87,7 @@ struct TcParams {
     int evict_first_b;   // stream B with an evict-first L2 policy (weights read once)
     int n_tok;           // weight-major (swap) kernels: token columns per accumulator, a multiple of 16 >= M
     int out_vec16;       // out is 16-byte aligned and ldo a multiple of 8: rows can be stored in 16-byte pieces
+    int swap_rows;       // weight-major tiles: gate rows (and as many up rows) per tile, <= 128
     // Mixed-origin slicing (BF16 partials): parts = P0 + P1 and part z < P0 is slice z of plan 0 (rows
     // < *split), part z >= P0 is slice z - P0 of plan 1 (rows >= *split).  Slice s of a plan covers K
     // blocks [s * chunk_kb, (s + 1) * chunk_kb) clipped to the K extent; its output part is s.
@@ -109,7 +110,11 @@ struct Cursor {
     long long sk_end;
 };
 
-REAX_DEVI long long sk_begin(const TcParams& p, int c) { return p.sk_iters * c / gridDim.x; }
+// First stream-K iteration of CTA c: floor(c * S / G).  The host keeps S * (G + 1) below 2^31, so 32-bit
+// arithmetic is exact here and in sk_owner.
+REAX_DEVI long long sk_begin(const TcParams& p, int c) {
+    return static_cast<long long>(static_cast<unsigned>(p.sk_iters) * static_cast<unsigned>(c) / gridDim.x);
+}
 
 REAX_DEVI Cursor cursor_init(const TcParams& p) {
     Cursor c;
@@ -180,16 +185,19 @@ REAX_DEVI bool cursor_next(const TcParams& p, int split, Cursor& c, Segment& s) 
         }
     }
     if (c.sk < c.sk_end) {
-        const long long it = c.sk;
-        const int st = static_cast<int>(it / KB);
-        const int k0 = static_cast<int>(it % KB);
-        const long long left = c.sk_end - it;
-        const int k1 = static_cast<int>(left < KB - k0 ? k0 + left : KB);
+        // The range is walked from its last tile back to its first.  A split tile's first K blocks lie
+        // at the end of some CTA's range and are computed (and published) first there; its last K
+        // blocks lie at the start of the next CTA's range and are computed last there, by the CTA that
+        // completes the tile, long after the others have published.
+        const long long last = c.sk_end - 1;
+        const int st = static_cast<int>(last / KB);
+        const long long tb = static_cast<long long>(st) * KB;
+        const long long lo = c.sk > tb ? c.sk : tb;
         s.tile = p.dp_tiles + st;
-        s.k0 = k0;
-        s.k1 = k1;
-        s.whole = (k0 == 0 && k1 == KB);
-        c.sk += k1 - k0;
+        s.k0 = static_cast<int>(lo - tb);
+        s.k1 = static_cast<int>(c.sk_end - tb);
+        s.whole = (s.k0 == 0 && s.k1 == KB);
+        c.sk_end = lo;
         return true;
     }
     return false;
@@ -197,7 +205,7 @@ REAX_DEVI bool cursor_next(const TcParams& p, int split, Cursor& c, Segment& s) 
 
 // CTA whose stream-K range holds iteration i (ranges are floor(c * S / G) .. floor((c+1) * S / G)).
 REAX_DEVI int sk_owner(const TcParams& p, long long i) {
-    return static_cast<int>(((i + 1) * gridDim.x - 1) / p.sk_iters);
+    return static_cast<int>((static_cast<unsigned>(i + 1) * gridDim.x - 1u) / static_cast<unsigned>(p.sk_iters));
 }
 
 REAX_DEVI int sk_slot(const TcParams& p, int c, int st) {
@@ -274,10 +282,10 @@ REAX_DEVI bool publish_partial(const TcParams& p, const Segment& seg, int st, ui
 // Wait, for at most limit_ns, until every other contributor of split tile st has counted its K blocks;
 // then this CTA completes the tile without publishing (nobody else can reach KB any more) and the
 // contributors' partials are visible to all its epilogue threads.  Only the contributor holding the
-// tile's first K blocks calls it: in stream-K order those are the last K blocks of its range, while
-// every other contributor reaches this tile earlier in its own range and publishes without waiting,
-// so no two CTAs ever wait on each other.  When the limit passes (a contributor not resident yet, say)
-// the caller publishes like any other contributor.  All epilogue threads call it.
+// tile's last K blocks calls it: those start its range, which it walks backwards, so it reaches them
+// last, while every other contributor reaches this tile first in its own range and publishes without
+// waiting; no two CTAs ever wait on each other.  When the limit passes (a contributor not resident
+// yet, say) the caller publishes like any other contributor.  All epilogue threads call it.
 template <int EPI_WARPS>
 REAX_DEVI bool wait_others_counted(const TcParams& p, const Segment& seg, int st, int* last_flag, uint64_t limit_ns) {
     const int KB = p.kb_int + p.kb_f16;
@@ -300,6 +308,34 @@ REAX_DEVI bool wait_others_counted(const TcParams& p, const Segment& seg, int st
     named_bar_sync(1, EPI_WARPS * 32);   // every thread has read the flag before it is reused
     if (complete) __threadfence();
     return complete;
+}
+
+// After every epilogue thread has stored its share of this CTA's partial of split tile st: count the
+// CTA's K blocks (one thread, after a release fence that covers the whole CTA's stores) and learn
+// whether that count completed the tile.  All epilogue threads call it.
+template <int EPI_WARPS>
+REAX_DEVI bool count_published(const TcParams& p, const Segment& seg, int st, int* last_flag) {
+    const int KB = p.kb_int + p.kb_f16;
+    named_bar_sync(1, EPI_WARPS * 32);
+    if (threadIdx.x == kCtlThreads) {
+        __threadfence();
+        const int n = seg.k1 - seg.k0;
+        *last_flag = (atomicAdd(p.ws_counters + st, n) + n == KB) ? 1 : 0;
+    }
+    named_bar_sync(1, EPI_WARPS * 32);
+    const bool finish = *reinterpret_cast<volatile int*>(last_flag) != 0;
+    named_bar_sync(1, EPI_WARPS * 32);   // every thread has read the flag before it is reused
+    if (finish) __threadfence();
+    return finish;
+}
+
+// Weight-major tile of segment s: (sw, sw, bias, bias) of this thread's gate and up rows (weight row
+// `row` of the tile).
+REAX_DEVI float4 swap_column_scales(const TcParams& p, const Segment& s, int row) {
+    int part, mt, nt;
+    tile_coords(p, s.tile, part, mt, nt);
+    const int j = min(nt * p.swap_rows + row, p.H - 1);   // lanes past the tile's rows load a valid column
+    return make_float4(__ldg(p.sw + j), __ldg(p.sw + p.H + j), __ldg(p.bias + j), __ldg(p.bias + p.H + j));
 }
 
 // Slots of a split tile's other contributors (CTA order), resolved once per tile.
@@ -399,7 +435,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     grid_dependency_wait();
     const int split = p.slice_mode ? min(max(__ldg(p.split), 0), p.M) : 0;
     // bytes a stage receives: weight-major tiles load n_tok activation rows instead of 128
-    const uint32_t stage_tx = SWAP ? static_cast<uint32_t>(kBStage + p.n_tok * kRowBytes) : kStageBytes;
+    const uint32_t stage_tx =
+        SWAP ? static_cast<uint32_t>((2 * p.swap_rows + p.n_tok) * kRowBytes) : static_cast<uint32_t>(kStageBytes);
 
     if (warp < kCtlWarps) {
     regs_shrink<kCtlRegs>();
@@ -419,8 +456,9 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 int part, mt, nt;
                 tile_coords(p, seg.tile, part, mt, nt);
                 const int m0 = mt * kBM;
-                const int b0 = (EPI == kEpiSwiglu) ? nt * (kBN / 2) : nt * kBN;
-                const int b1 = (EPI == kEpiSwiglu) ? p.H + nt * (kBN / 2) : nt * kBN + kBN / 2;
+                const int rows = SWAP ? p.swap_rows : kBN / 2;   // gate rows of the tile
+                const int b0 = (EPI == kEpiSwiglu) ? nt * rows : nt * kBN;
+                const int b1 = (EPI == kEpiSwiglu) ? p.H + nt * rows : nt * kBN + kBN / 2;
                 for (int kb = seg.k0; kb < seg.k1; ++kb) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns, vabort)) {
                         if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutEmpty);
@@ -563,6 +601,18 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         uint32_t acc_phase = 0;
         Cursor cur = cursor_init(p);
         Segment seg;
+        // Weight-major tiles: every tile covers all tokens, so the token scales are staged once, and each
+        // segment's column scales and biases are loaded one segment ahead (a cursor kept one step in
+        // front), so that they have landed when the segment starts.
+        Cursor ahead = cur;
+        Segment aseg;
+        float4 next_cs = make_float4(0.f, 0.f, 0.f, 0.f);   // (sw gate, sw up, bias gate, bias up)
+        if constexpr (SWAP && MODE == 0) {
+            for (int t = threadIdx.x - kCtlThreads; t < p.n_tok; t += EPI_WARPS * 32)
+                stage_sw[t] = t < p.M ? __ldg(p.sa + t) : 0.f;
+            named_bar_sync(1, EPI_WARPS * 32);
+            if (cursor_next(p, split, ahead, aseg)) next_cs = swap_column_scales(p, aseg, q * 32 + lane);
+        }
         while (cursor_next(p, split, cur, seg)) {
             int part, mt, nt;
             tile_coords(p, seg.tile, part, mt, nt);
@@ -580,23 +630,18 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             if constexpr (SWAP) {
                 // ---------------------------------------------- weight-major tile: lanes are weight rows
                 const int n_tok = p.n_tok;
-                const int n0 = nt * (kBN / 2);                 // gate row (= output column) of lane 0
+                const int n0 = nt * p.swap_rows;               // gate row (= output column) of lane 0
                 const int j = n0 + r_tile;                     // this thread's output column
+                // lanes past the tile's rows (or past H in the last tile) hold rows of no output column
+                const bool col_ok = r_tile < p.swap_rows && j < p.H;
                 const int per_warp = n_tok / kSplit;           // token columns each warp finishes
-                const int tok_lo = (e / 4) * per_warp, tok_hi = tok_lo + per_warp;
+                const int tok_lo = (e / 4) * per_warp;
                 const int n_w = min(per_warp, p.M - tok_lo);   // real tokens among them (<= 0: none)
-                float swg = 0.f, swu = 0.f, bg = 0.f, bu = 0.f;
+                const float swg = next_cs.x, swu = next_cs.y, bg = next_cs.z, bu = next_cs.w;
                 if constexpr (MODE == 0) {
-                    swg = __ldg(p.sw + j);
-                    swu = __ldg(p.sw + p.H + j);
-                    bg = __ldg(p.bias + j);
-                    bu = __ldg(p.bias + p.H + j);
-                    // land the loads now, while the MMAs run, not at their first use after the wait
-                    asm volatile("" ::"f"(swg), "f"(swu), "f"(bg), "f"(bu));
-                    for (int t = threadIdx.x - kCtlThreads; t < n_tok; t += EPI_WARPS * 32)
-                        s_sw[t] = t < p.M ? __ldg(p.sa + t) : 0.f;
-                    named_bar_sync(1, EPI_WARPS * 32);
+                    if (cursor_next(p, split, ahead, aseg)) next_cs = swap_column_scales(p, aseg, r_tile);
                 }
+                const float* s_sa = stage_sw;   // token scales, staged once
                 // split tile: the other contributors' partial slots, resolved while the MMAs still run
                 const int4* contrib[kMaxContrib];
                 const int n_contrib = whole ? 0 : contributors(p, st, contrib);
@@ -614,11 +659,11 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             qu[c] = __ldcg(contrib[0] + ((n_tok + tok_lo + 4 * c) / 4) * kBM + r_tile);
                         }
                     };
-                    // The contributor holding the tile's first K blocks waits (bounded) for the others
+                    // The contributor holding the tile's last K blocks waits (bounded) for the others
                     // instead of publishing, and fetches the first one's partial while its own last MMAs
                     // still run.
                     bool early = false;
-                    if (!whole && seg.k0 == 0) {
+                    if (!whole && seg.k1 == p.kb_int + p.kb_f16) {
                         early = wait_others_counted<EPI_WARPS>(p, seg, st, last_flag, kFinisherWaitNs);
                         if (early && n_contrib > 0) fetch_first();
                     }
@@ -629,9 +674,22 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     tc_fence_after();
                     bool finish = whole || early;
                     if (!finish) {
-                        // the gate columns of this warp's token range and the matching up columns
-                        finish = publish_partial<EPI_WARPS, 8>(p, seg, st, t_acc, tok_lo, tok_hi, n_tok, r_tile, true,
-                                                               last_flag);
+                        // Publish this warp's gate columns and the matching up columns (one TMEM round trip),
+                        // then count this CTA's K blocks; the contributor whose count completes the tile
+                        // finishes it.  One thread fences for the CTA after the barrier.
+                        uint32_t g[2 * PAIRS], u[2 * PAIRS];
+                        tmem_ld_pairs_sync<PAIRS>(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
+                        int4* slot = reinterpret_cast<int4*>(
+                            p.ws_partials + (static_cast<size_t>(blockIdx.x) * 2 + sk_slot(p, blockIdx.x, st)) * kSlotInts);
+#pragma unroll
+                        for (int c = 0; c < PAIRS / 2; ++c)
+                            if (2 * PAIRS == per_warp || 4 * c < per_warp) {
+                                __stcg(slot + ((tok_lo + 4 * c) / 4) * kBM + r_tile,
+                                       make_int4(g[4 * c], g[4 * c + 1], g[4 * c + 2], g[4 * c + 3]));
+                                __stcg(slot + ((n_tok + tok_lo + 4 * c) / 4) * kBM + r_tile,
+                                       make_int4(u[4 * c], u[4 * c + 1], u[4 * c + 2], u[4 * c + 3]));
+                            }
+                        finish = count_published<EPI_WARPS>(p, seg, st, last_flag);
                         if (finish && n_contrib > 0) fetch_first();
                     }
                     if (!finish) return true;
@@ -665,7 +723,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         for (int i = 0; i < PAIRS; ++i) {
                             uint64_t vg, vu;
                             if constexpr (MODE == 0) {
-                                const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sw + tok_lo + 2 * i);
+                                const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sa + tok_lo + 2 * i);
                                 vg = dequant2(g[2 * i], g[2 * i + 1], sa2, swg2, bg2);
                                 vu = dequant2(u[2 * i], u[2 * i + 1], sa2, swu2, bu2);
                             } else {
@@ -700,8 +758,9 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 #pragma unroll
                             for (int i = 0; i < PAIRS; ++i) {
                                 const int t = tok_lo + 2 * i;
-                                if (2 * i < n_w) p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o[i] & 0xFFFFu);
-                                if (2 * i + 1 < n_w)
+                                if (col_ok && 2 * i < n_w)
+                                    p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o[i] & 0xFFFFu);
+                                if (col_ok && 2 * i + 1 < n_w)
                                     p.out[static_cast<size_t>(t + 1) * p.ldo + j] = __ushort_as_bfloat16(o[i] >> 16);
                             }
                         }

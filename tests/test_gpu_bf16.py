@@ -45,7 +45,8 @@ def gpu_table():
     return H.bits(t)
 
 
-@pytest.mark.parametrize("M,K,H2", [(1, 1024, 512), (64, 4096, 2048), (128, 4096, 14336), (333, 1024, 4096)])
+@pytest.mark.parametrize("M,K,H2", [(1, 1024, 512), (64, 4096, 2048), (8, 512, 10240), (128, 4096, 14336),
+                                    (333, 1024, 4096)])
 def test_gate_up_bf16_unsplit(M, K, H2):
     from reax_engine_runtime_v3_b200.runtime.mixed_origin_bf16 import Native
     g = H.gen(M + K)
