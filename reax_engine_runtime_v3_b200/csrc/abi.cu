@@ -472,7 +472,8 @@ int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, const void
     const bool swap = KH == 0 && M <= kSwapMaxRows;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
     p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
-    // out 16-byte aligned and ldo % 8 == 0 (checked above); weight-major rows are staged as 128-column blocks
+    // out 16-byte aligned and ldo % 8 == 0 (checked above): 128-row weight-major tiles store through
+    // shared memory in 16-byte pieces; balanced tiles store their columns directly
     p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
     if (KL) {
         if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
@@ -537,7 +538,8 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     const bool swap = M <= kSwapMaxRows;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
     p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
-    // out 16-byte aligned and ldo % 8 == 0 (checked above); weight-major rows are staged as 128-column blocks
+    // out 16-byte aligned and ldo % 8 == 0 (checked above): 128-row weight-major tiles store through
+    // shared memory in 16-byte pieces; balanced tiles store their columns directly
     p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
     if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : 128)) != REAX_OK)
         return rc;
@@ -736,7 +738,8 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     const bool swap = KH == 0 && M <= kSwapMaxRows;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
     p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
-    // out 16-byte aligned and ldo % 8 == 0 (checked above); weight-major rows are staged as 128-column blocks
+    // out 16-byte aligned and ldo % 8 == 0 (checked above): 128-row weight-major tiles store through
+    // shared memory in 16-byte pieces; balanced tiles store their columns directly
     p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
     if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
         return rc;

@@ -387,9 +387,23 @@ REAX_DEVI uint64_t dequant2(uint32_t a0, uint32_t a1, uint64_t sa2, uint64_t sw2
 // silu_tab of a pair.
 REAX_DEVI uint64_t silu2_tab(uint64_t g2, const uint16_t* tab) { return f2(silu_tab(f2_lo(g2), tab), silu_tab(f2_hi(g2), tab)); }
 
-// SwiGLU of a (gate, up) pair whose values are already bf16-rounded: bf16x2 of bf16(silu(g) * u).
-REAX_DEVI uint32_t swiglu2_tab(uint64_t gb, uint64_t ub, const uint16_t* tab) {
-    return bf16x2_rn(mul2_rn(silu2_tab(gb, tab), ub));
+// SwiGLU of a (gate, up) pair given as packed bf16x2 words: bf16x2 of bf16(silu(g) * u), lane-wise.
+// When every lane of the warp has both gate values inside the table's range (the usual case) the
+// SiLU is one shared-memory load per value; otherwise the warp takes silu_tab's full case analysis.
+// All 32 lanes of the warp must call it together.
+REAX_DEVI uint32_t swiglu2_bits(uint32_t gw, uint32_t uw, const uint16_t* tab) {
+    const uint32_t b0 = gw & 0xFFFFu, b1 = gw >> 16;
+    const uint32_t r0 = (b0 & 0x7FFFu) - (kSiluTabElo << 7), r1 = (b1 & 0x7FFFu) - (kSiluTabElo << 7);
+    uint32_t s0, s1;   // bf16(silu) as float32 bit patterns
+    if (__all_sync(0xFFFFFFFFu, r0 < kSiluTabHalf && r1 < kSiluTabHalf)) {
+        s0 = static_cast<uint32_t>(tab[r0 + (b0 >> 15) * kSiluTabHalf]) << 16;
+        s1 = static_cast<uint32_t>(tab[r1 + (b1 >> 15) * kSiluTabHalf]) << 16;
+    } else {
+        s0 = __float_as_uint(silu_tab(__uint_as_float(b0 << 16), tab));
+        s1 = __float_as_uint(silu_tab(__uint_as_float(b1 << 16), tab));
+    }
+    const uint64_t s2 = (static_cast<uint64_t>(s1) << 32) | s0;
+    return bf16x2_rn(mul2_rn(s2, bf16x2_to_f2(uw)));
 }
 
 REAX_DEVI uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {

@@ -36,7 +36,10 @@ constexpr int kStageBytes = kAStage + kBStage;  // 48 KiB
 constexpr int kTmemCols = 512;
 constexpr int kSlotInts = kBM * kBN;            // one split-tile partial: 128 x 256 int32 (128 KiB)
 constexpr int kSwapMaxTok = 64;                 // weight-major tiles: at most 64 token columns per accumulator
-constexpr int kOutStageBytes = kSwapMaxTok * (kBN / 2) * 2;   // weight-major output block staged for the stores
+// Weight-major output block staged for the stores: per token, the tile's (<= 128) columns placed at
+// their 16-byte phase in the output row, so rows of 136 halfwords.
+constexpr int kOutStagePitch = kBN / 2 + 8;
+constexpr int kOutStageBytes = kSwapMaxTok * kOutStagePitch * 2;
 // How long the contributor holding a split tile's last K blocks waits for the others to publish
 // before it publishes itself (a performance choice; both paths give the same result).
 constexpr unsigned long long kFinisherWaitNs = 10000;
@@ -730,27 +733,44 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                                 vg = f2(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
                                 vu = f2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
                             }
-                            o[i] = swiglu2_tab(bf16x2_to_f2(bf16x2_rn(vg)), bf16x2_to_f2(bf16x2_rn(vu)), silu_tab_s);
+                            o[i] = swiglu2_bits(bf16x2_rn(vg), bf16x2_rn(vu), silu_tab_s);
                         }
                     }
                     if (p.out_vec16) {
-                        // the tile's [tokens x 128 columns] block goes through shared memory so that every
-                        // global store writes a whole 16-byte piece of a token row
+                        // The tile's [tokens x columns] block goes through shared memory, each token row placed
+                        // at the 16-byte phase of its destination (ph = n0 % 8 halfwords; out is 16-byte
+                        // aligned and ldo a multiple of 8), so the copy writes whole aligned 16-byte pieces and
+                        // 2-byte stores only where a piece sticks out of [n0, n_end).
                         uint16_t* ot = reinterpret_cast<uint16_t*>(out_stage);
-                        if (n_w > 0) {
+                        const int ph = n0 & 7;
+                        if (n_w > 0 && col_ok) {
 #pragma unroll
                             for (int i = 0; i < PAIRS; ++i)
                                 if (2 * PAIRS == per_warp || 2 * i < per_warp) {
-                                    ot[(tok_lo + 2 * i) * (kBN / 2) + r_tile] = static_cast<uint16_t>(o[i] & 0xFFFFu);
-                                    ot[(tok_lo + 2 * i + 1) * (kBN / 2) + r_tile] = static_cast<uint16_t>(o[i] >> 16);
+                                    ot[(tok_lo + 2 * i) * kOutStagePitch + ph + r_tile] = static_cast<uint16_t>(o[i] & 0xFFFFu);
+                                    ot[(tok_lo + 2 * i + 1) * kOutStagePitch + ph + r_tile] = static_cast<uint16_t>(o[i] >> 16);
                                 }
                         }
                         named_bar_sync(1, EPI_WARPS * 32);
                         if (!whole && threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
-                        for (int idx = threadIdx.x - kCtlThreads; idx < p.M * 16; idx += EPI_WARPS * 32) {
-                            const int t = idx >> 4, k = idx & 15;
-                            const uint4 v = *reinterpret_cast<const uint4*>(ot + t * (kBN / 2) + 8 * k);
-                            *reinterpret_cast<uint4*>(p.out + static_cast<size_t>(t) * p.ldo + n0 + 8 * k) = v;
+                        // one token row per warp and iteration, one 16-byte piece per lane (at most 17 pieces)
+                        const int n_end = min(n0 + p.swap_rows, p.H);       // one past the tile's last column
+                        const int pieces = (ph + (n_end - n0) + 7) >> 3;
+                        const int c0 = n0 - ph + 8 * lane;                 // first column of this lane's piece
+                        const bool full = c0 >= n0 && c0 + 8 <= n_end;
+                        for (int t = e; t < p.M; t += EPI_WARPS) {
+                            if (lane >= pieces) continue;
+                            const uint4 v = *reinterpret_cast<const uint4*>(ot + t * kOutStagePitch + 8 * lane);
+                            __nv_bfloat16* dst = p.out + static_cast<size_t>(t) * p.ldo + c0;
+                            if (full) {
+                                *reinterpret_cast<uint4*>(dst) = v;
+                            } else {
+                                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                                for (int h = 0; h < 8; ++h)
+                                    if (c0 + h >= n0 && c0 + h < n_end)
+                                        dst[h] = __ushort_as_bfloat16(static_cast<uint16_t>(w[h >> 1] >> (16 * (h & 1))));
+                            }
                         }
                         named_bar_sync(1, EPI_WARPS * 32);   // the staging block is free again
                     } else {
@@ -826,8 +846,10 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             tmem_ld_x32_sync(t_acc + cc, g);
                             if constexpr (add_f) tmem_ld_x32_sync(t_f32 + cc, fg);
                         }
-                        if (!row_ok) continue;
-                        if (!whole) {
+                        // whole warps outside the tile's rows skip; the others stay converged for the SiLU's
+                        // warp vote, and only their stores and partial sums are per row
+                        if (__all_sync(0xFFFFFFFFu, !row_ok)) continue;
+                        if (row_ok && !whole) {
                             add_partials<32>(contrib, n_contrib, cc, r_tile, g);
                             if constexpr (EPI == kEpiSwiglu) add_partials<32>(contrib, n_contrib, kBN / 2 + cc, r_tile, u);
                         }
@@ -853,7 +875,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                                     vg = f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1]));
                                     vu = f2(__uint_as_float(u[i]), __uint_as_float(u[i + 1]));
                                 }
-                                packed[i / 2] = swiglu2_tab(bf16x2_to_f2(bf16x2_rn(vg)), bf16x2_to_f2(bf16x2_rn(vu)), silu_tab_s);
+                                packed[i / 2] = swiglu2_bits(bf16x2_rn(vg), bf16x2_rn(vu), silu_tab_s);
                             }
                             dst = p.out + static_cast<size_t>(grow) * p.ldo + nt * (kBN / 2) + cc;
                         } else {
@@ -872,10 +894,12 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             }
                             dst = p.out + out_part * p.out_part_stride + static_cast<size_t>(grow) * p.ldo + nt * kBN + cc;
                         }
+                        if (row_ok) {
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            reinterpret_cast<uint4*>(dst)[i] =
-                                make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                            for (int i = 0; i < 4; ++i)
+                                reinterpret_cast<uint4*>(dst)[i] =
+                                    make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                        }
                     }
                     if (!whole) {
                         named_bar_sync(1, EPI_WARPS * 32);

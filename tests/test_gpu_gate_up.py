@@ -105,6 +105,17 @@ def test_weight_major_plans(M, K, Hh):
     compare_int8(H.activations(g, M, K), H.int8_bank(g, K, Hh))
 
 
+@pytest.mark.parametrize("M", [8, 200])
+def test_silu_range_edges(M):
+    """Gate values on both sides of every edge of the epilogue's SiLU table: column scales log-uniform
+    over 1e-9 .. 1e-1 with zero bias put gates below 2^-10, inside [2^-10, 128) and at or above 128,
+    mixed within warps, in weight-major (M = 8) and token-major (M = 200) tiles."""
+    g = H.gen(77 + M)
+    bank = H.int8_bank(g, 1024, 2816, bias=False)
+    bank.scales = (10.0 ** (-9.0 + 8.0 * torch.rand(bank.scales.shape, generator=g))).float().contiguous()
+    compare_int8(H.activations(g, M, 1024), bank)
+
+
 def test_cfg3_prefill_rows_sample():
     """BASELINE config 3 (M=4096, K=4096, H=14336): full GPU run, oracle on a sample of rows."""
     g = H.gen(3)
