@@ -108,6 +108,18 @@ REAX_API int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, c
                     const float* sw, const float* bias, void* out, int M, int N2, int KL, int KH, int ldo,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- a1 + a4-a9: quantize, then the fused INT8 gate/up --------------------------------------------
+ * Replaces reaxv2.gate_up.Native.project (reaxv2/gate_up.py:29-37): reax_quant_rows on x bf16 [M, K]
+ * into low int8 [M, KL], high bf16 [M, KH] and scales float32 [M], then reax_gate_up_i8 on them with W,
+ * WH, sw and bias (the bank) into out.  Because the GEMM follows this library's quantizer on the
+ * stream, it requests its first weight tiles while the quantizer still runs.  Same requirements as the
+ * two calls it makes. */
+REAX_API int reax_project_i8(const void* x, const int32_t* low_columns, const int32_t* high_columns,
+                             const float* smoothing, const float* centers, int center, const int8_t* W,
+                             const void* WH, const float* sw, const float* bias, int8_t* low, void* high,
+                             float* scales, void* out, int M, int K, int KL, int KH, int N2, int ldo, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* ---- a5-a9 without a caller workspace ----------------------------------------------------------------
  * No counterpart in the reference: the same INT8 gate/up + dequant + SwiGLU as reax_gate_up_i8, for
  * callers that cannot allocate device memory for a workspace - e.g. a serving process that has handed

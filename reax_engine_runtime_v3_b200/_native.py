@@ -41,6 +41,8 @@ SIGNATURES = {
     "reax_silu_table": ([_P, _P], _I),
     "reax_gate_up_i8": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_gate_up_i8_noalloc": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
+    "reax_project_i8": ([_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _SZ, _P],
+                        _I),
     "reax_gate_up_bf16": ([_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_bf16_partials": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_sliced_i8": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),

@@ -27,7 +27,7 @@ constexpr size_t kStatusBytes = 256;
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;   // 2 s
 
 // Quantizer division for the plain '/' of reaxv2/quantize.py:18-19,42 (see rowwise.cuh).
-constexpr int kQuantDivision = reax::kDivFull;
+constexpr int kQuantDivision = reax::kQuantDiv;
 
 thread_local std::string g_last_error;
 unsigned long long g_timeout_ns = kDefaultTimeoutNs;
@@ -287,6 +287,27 @@ int launch_plain(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 blo
     return REAX_OK;
 }
 
+// Launch with programmatic stream serialization: the kernel may be scheduled while its predecessor on
+// the stream still runs, once that predecessor signals griddepcontrol.launch_dependents.  Only for
+// kernels that execute griddepcontrol.wait before their first memory access.
+template <typename... KArgs, typename... Args>
+int launch_dependent(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return REAX_OK;
+}
+
 int elementwise_grid(long long work, int sms) {
     long long g = (work + 255) / 256;
     const long long cap = static_cast<long long>(sms) * 16;
@@ -324,6 +345,82 @@ int noalloc_scratch(int dev, void** out) {
     return REAX_OK;
 }
 
+// reax_gate_up_i8 with the option of requesting the first weight tiles before the dependency wait.
+int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa, const float* sw,
+                      const float* bias, void* out, int M, int N2, int KL, int KH, int ldo, void* workspace,
+                      size_t workspace_bytes, void* stream, int early_b) {
+    if (M < 0 || N2 <= 0 || KL < 0 || KH < 0 || KL + KH == 0)
+        return fail(REAX_ERR_INVALID, "gate_up_i8: bad sizes M=%d N2=%d KL=%d KH=%d", M, N2, KL, KH);
+    if (KL % 128 != 0 || KH % 64 != 0 || N2 % 256 != 0)
+        return fail(REAX_ERR_INVALID, "gate_up_i8: needs KL %% 128 == 0, KH %% 64 == 0, N2 %% 256 == 0 (KL=%d KH=%d N2=%d)",
+                    KL, KH, N2);
+    if (ldo < N2 / 2 || ldo % 8 != 0) return fail(REAX_ERR_INVALID, "gate_up_i8: ldo=%d (needs >= N2/2, %% 8 == 0)", ldo);
+    if (KL == 0) return fail(REAX_ERR_INVALID, "gate_up_i8: KL must be > 0 (the INT8 part of the bank is empty)");
+    if (M == 0) return REAX_OK;
+    if (!out || !sw || !bias || (KL && (!A || !W || !sa)) || (KH && (!AH || !WH)))
+        return fail(REAX_ERR_INVALID, "gate_up_i8: NULL pointer argument");
+    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(AH, 16) || !aligned(WH, 16) || !aligned(sw, 16) ||
+        !aligned(bias, 16) || !aligned(out, 16))
+        return fail(REAX_ERR_ALIGN, "gate_up_i8: operands, sw, bias and out must be 16-byte aligned");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    Workspace ws;
+    if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
+
+    reax::TcParams p;
+    init_params(p);
+    // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
+    const bool swap = KH == 0 && M <= kSwapMaxRows;
+    p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
+    p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
+    // out 16-byte aligned and ldo % 8 == 0 (checked above): 128-row weight-major tiles store through
+    // shared memory in 16-byte pieces; balanced tiles store their columns directly
+    p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
+    if (KL) {
+        if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
+            return rc;
+        if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, swap ? p.swap_rows : 128)) !=
+            REAX_OK)
+            return rc;
+    }
+    if (KH) {
+        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH)) != REAX_OK) return rc;
+    }
+    if (!KL) {
+        p.tm_a = p.tm_ah;
+        p.tm_b = p.tm_bh;
+    }
+    if (!KH) {
+        p.tm_ah = p.tm_a;
+        p.tm_bh = p.tm_b;
+    }
+    p.sa = sa;
+    p.sw = sw;
+    p.bias = bias;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.M = M;
+    p.H = N2 / 2;
+    p.ldo = ldo;
+    p.kb_int = KL / 128;
+    p.kb_f16 = KH / 64;
+    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
+    p.n_tiles = (N2 / 2 + p.swap_rows - 1) / p.swap_rows;
+    p.tiles = p.m_tiles * p.n_tiles;
+    p.mode = 0;
+    p.acc_bufs = KH ? 1 : 2;
+    p.ws_partials = ws.partials;
+    p.ws_counters = ws.counters;
+    p.status = ws.status;
+    p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
+    p.early_b = early_b;
+    int grid = 0;
+    plan_schedule(p, info->sms, KH == 0 && p.swap_rows == 128, &grid);
+    return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
+}
+
 }  // namespace
 
 extern "C" {
@@ -359,7 +456,7 @@ int reax_quant_rows(const void* x, const int32_t* low_columns, const int32_t* hi
     if (rc != REAX_OK) return rc;
     const int aligned_x = (aligned(x, 16) && K % 8 == 0) ? 1 : 0;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return launch_plain("quant_rows launch", reax::quant_rows_kernel<kQuantDivision>, dim3(M), dim3(256), s,
+    return launch_dependent("quant_rows launch", reax::quant_rows_kernel<kQuantDivision>, dim3(M), dim3(reax::kQuantThreads), s,
                         static_cast<const __nv_bfloat16*>(x), static_cast<const int*>(low_columns),
                         static_cast<const int*>(high_columns), smoothing, centers, low,
                         static_cast<__nv_bfloat16*>(high), scales, K, KL, KH, center ? 1 : 0, aligned_x);
@@ -377,7 +474,7 @@ int reax_quant_groups(const void* x, const int32_t* low_columns, const int32_t* 
     DeviceInfo* info;
     int rc = current_device(&dev, &info);
     if (rc != REAX_OK) return rc;
-    return launch_plain("quant_groups launch", reax::quant_groups_kernel<kQuantDivision>, dim3(M, P), dim3(256),
+    return launch_dependent("quant_groups launch", reax::quant_groups_kernel<kQuantDivision>, dim3(M, P), dim3(256),
                         static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
                         static_cast<const int*>(low_columns), static_cast<const int*>(high_columns), centers,
                         smoothing, low, static_cast<__nv_bfloat16*>(high), scales, M, K, G, HP, P);
@@ -446,75 +543,20 @@ int reax_silu_table(void* table, void* stream) {
 int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa, const float* sw,
                     const float* bias, void* out, int M, int N2, int KL, int KH, int ldo, void* workspace,
                     size_t workspace_bytes, void* stream) {
-    if (M < 0 || N2 <= 0 || KL < 0 || KH < 0 || KL + KH == 0)
-        return fail(REAX_ERR_INVALID, "gate_up_i8: bad sizes M=%d N2=%d KL=%d KH=%d", M, N2, KL, KH);
-    if (KL % 128 != 0 || KH % 64 != 0 || N2 % 256 != 0)
-        return fail(REAX_ERR_INVALID, "gate_up_i8: needs KL %% 128 == 0, KH %% 64 == 0, N2 %% 256 == 0 (KL=%d KH=%d N2=%d)",
-                    KL, KH, N2);
-    if (ldo < N2 / 2 || ldo % 8 != 0) return fail(REAX_ERR_INVALID, "gate_up_i8: ldo=%d (needs >= N2/2, %% 8 == 0)", ldo);
-    if (KL == 0) return fail(REAX_ERR_INVALID, "gate_up_i8: KL must be > 0 (the INT8 part of the bank is empty)");
-    if (M == 0) return REAX_OK;
-    if (!out || !sw || !bias || (KL && (!A || !W || !sa)) || (KH && (!AH || !WH)))
-        return fail(REAX_ERR_INVALID, "gate_up_i8: NULL pointer argument");
-    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(AH, 16) || !aligned(WH, 16) || !aligned(sw, 16) ||
-        !aligned(bias, 16) || !aligned(out, 16))
-        return fail(REAX_ERR_ALIGN, "gate_up_i8: operands, sw, bias and out must be 16-byte aligned");
-    int dev;
-    DeviceInfo* info;
-    int rc = current_device(&dev, &info);
-    if (rc != REAX_OK) return rc;
-    Workspace ws;
-    if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
+    return gate_up_i8_launch(A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, workspace, workspace_bytes, stream, 0);
+}
 
-    reax::TcParams p;
-    init_params(p);
-    // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
-    const bool swap = KH == 0 && M <= kSwapMaxRows;
-    p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
-    p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
-    // out 16-byte aligned and ldo % 8 == 0 (checked above): 128-row weight-major tiles store through
-    // shared memory in 16-byte pieces; balanced tiles store their columns directly
-    p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
-    if (KL) {
-        if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
-            return rc;
-        if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, swap ? p.swap_rows : 128)) !=
-            REAX_OK)
-            return rc;
-    }
-    if (KH) {
-        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH)) != REAX_OK) return rc;
-        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH)) != REAX_OK) return rc;
-    }
-    if (!KL) {
-        p.tm_a = p.tm_ah;
-        p.tm_b = p.tm_bh;
-    }
-    if (!KH) {
-        p.tm_ah = p.tm_a;
-        p.tm_bh = p.tm_b;
-    }
-    p.sa = sa;
-    p.sw = sw;
-    p.bias = bias;
-    p.out = static_cast<__nv_bfloat16*>(out);
-    p.M = M;
-    p.H = N2 / 2;
-    p.ldo = ldo;
-    p.kb_int = KL / 128;
-    p.kb_f16 = KH / 64;
-    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
-    p.n_tiles = (N2 / 2 + p.swap_rows - 1) / p.swap_rows;
-    p.tiles = p.m_tiles * p.n_tiles;
-    p.mode = 0;
-    p.acc_bufs = KH ? 1 : 2;
-    p.ws_partials = ws.partials;
-    p.ws_counters = ws.counters;
-    p.status = ws.status;
-    p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
-    int grid = 0;
-    plan_schedule(p, info->sms, KH == 0 && p.swap_rows == 128, &grid);
-    return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
+int reax_project_i8(const void* x, const int32_t* low_columns, const int32_t* high_columns, const float* smoothing,
+                    const float* centers, int center, const int8_t* W, const void* WH, const float* sw,
+                    const float* bias, int8_t* low, void* high, float* scales, void* out, int M, int K, int KL, int KH,
+                    int N2, int ldo, void* workspace, size_t workspace_bytes, void* stream) {
+    int rc = reax_quant_rows(x, low_columns, high_columns, smoothing, centers, low, high, scales, M, K, KL, KH, center,
+                             stream);
+    if (rc != REAX_OK) return rc;
+    // The GEMM follows the quantizer on the stream, so it may request its first weight tiles before its
+    // dependency wait (early_b).
+    return gate_up_i8_launch(low, W, KH ? high : nullptr, KH ? WH : nullptr, scales, sw, bias, out, M, N2, KL, KH, ldo,
+                             workspace, workspace_bytes, stream, 1);
 }
 
 int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, int K, int ldo, void* workspace,

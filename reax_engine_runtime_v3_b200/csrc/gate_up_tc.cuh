@@ -91,6 +91,10 @@ struct TcParams {
     int n_tok;           // weight-major (swap) kernels: token columns per accumulator, a multiple of 16 >= M
     int out_vec16;       // out is 16-byte aligned and ldo a multiple of 8: rows can be stored in 16-byte pieces
     int swap_rows;       // weight-major tiles: gate rows (and as many up rows) per tile, <= 128
+    // The kernel before this one on the stream is this library's quantizer, which signals its dependents
+    // only after its own dependency wait: the first weight tiles may be requested before this kernel's
+    // wait, since nothing in flight then can still be writing them (not with slice_mode).
+    int early_b;
     // Mixed-origin slicing (BF16 partials): parts = P0 + P1 and part z < P0 is slice z of plan 0 (rows
     // < *split), part z >= P0 is slice z - P0 of plan 1 (rows >= *split).  Slice s of a plan covers K
     // blocks [s * chunk_kb, (s + 1) * chunk_kb) clipped to the K extent; its output part is s.
@@ -434,9 +438,16 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     volatile int* vabort = abort_flag;
 
     // Inputs of this kernel may be written by the kernel launched just before it on the stream
-    // (programmatic dependent launch): everything above overlapped that kernel's tail.
-    grid_dependency_wait();
-    const int split = p.slice_mode ? min(max(__ldg(p.split), 0), p.M) : 0;
+    // (programmatic dependent launch): everything above overlapped that kernel's tail, and each role
+    // waits for that kernel before its first global access (the producer may first load weight tiles,
+    // see early_b).  From then on the next kernel may be scheduled: every kernel this library launches
+    // with programmatic serialization waits for this grid's completion before it touches memory, and
+    // other launches on the stream keep full serialization.
+    auto dependency_wait = [&]() -> int {
+        grid_dependency_wait();
+        grid_dependents_launch();
+        return p.slice_mode ? min(max(__ldg(p.split), 0), p.M) : 0;
+    };
     // bytes a stage receives: weight-major tiles load n_tok activation rows instead of 128
     const uint32_t stage_tx =
         SWAP ? static_cast<uint32_t>((2 * p.swap_rows + p.n_tok) * kRowBytes) : static_cast<uint32_t>(kStageBytes);
@@ -452,36 +463,69 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             uint32_t phase = 0;
             uint32_t armed = 0;        // bit s: stage s has been armed at least once
             uint32_t armed_parity = 0; // bit s: parity of the last arming of stage s
+            // B (weight) boxes of K block kb of a tile into stage st
+            auto load_b = [&](int st, int kb, int part, int b0, int b1) {
+                uint8_t* sb_ = stage_b + st * kBStage;
+                if (kb < p.kb_int) {
+                    const int x = (part * p.kb_int_part + kb) * kRowBytes;
+                    tma_load_2d(sb_, &p.tm_b, &full[st], x, b0, pol_b);
+                    tma_load_2d(sb_ + kBStage / 2, &p.tm_b, &full[st], x, b1, pol_b);
+                } else {
+                    const int x = (part * p.kb_f16_part + kb - p.kb_int) * (kRowBytes / 2);
+                    tma_load_2d(sb_, &p.tm_bh, &full[st], x, b0, pol_b);
+                    tma_load_2d(sb_ + kBStage / 2, &p.tm_bh, &full[st], x, b1, pol_b);
+                }
+            };
+            auto tile_rows = [&](const Segment& sg, int& part, int& m0, int& b0, int& b1) {
+                int mt, nt;
+                tile_coords(p, sg.tile, part, mt, nt);
+                m0 = mt * kBM;
+                const int rows = SWAP ? p.swap_rows : kBN / 2;   // gate rows of the tile
+                b0 = (EPI == kEpiSwiglu) ? nt * rows : nt * kBN;
+                b1 = (EPI == kEpiSwiglu) ? p.H + nt * rows : nt * kBN + kBN / 2;
+            };
+            // early_b: the weight boxes of the first segment's first STAGES K blocks are requested before
+            // the dependency wait (the weights are not produced by the kernel this one waits for).
+            int pre = 0;
+            if (p.early_b && !p.slice_mode) {
+                Cursor c0 = cursor_init(p);
+                Segment s0;
+                if (cursor_next(p, 0, c0, s0)) {
+                    int part, m0, b0, b1;
+                    tile_rows(s0, part, m0, b0, b1);
+                    pre = min(STAGES, s0.k1 - s0.k0);
+                    for (int i = 0; i < pre; ++i) {
+                        mbar_arrive_expect_tx(&full[i], stage_tx);
+                        load_b(i, s0.k0 + i, part, b0, b1);
+                        armed |= 1u << i;
+                    }
+                }
+            }
+            const int split = dependency_wait();
+            bool ok = true;
             Cursor cur = cursor_init(p);
             Segment seg;
-            bool ok = true;
+            bool first = true;
             while (ok && cursor_next(p, split, cur, seg)) {
-                int part, mt, nt;
-                tile_coords(p, seg.tile, part, mt, nt);
-                const int m0 = mt * kBM;
-                const int rows = SWAP ? p.swap_rows : kBN / 2;   // gate rows of the tile
-                const int b0 = (EPI == kEpiSwiglu) ? nt * rows : nt * kBN;
-                const int b1 = (EPI == kEpiSwiglu) ? p.H + nt * rows : nt * kBN + kBN / 2;
+                int part, m0, b0, b1;
+                tile_rows(seg, part, m0, b0, b1);
                 for (int kb = seg.k0; kb < seg.k1; ++kb) {
                     if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns, vabort)) {
                         if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutEmpty);
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[stage], stage_tx);
+                    const bool prefetched = first && kb - seg.k0 < pre;   // armed, B boxes requested
+                    if (!prefetched) mbar_arrive_expect_tx(&full[stage], stage_tx);
                     uint8_t* sa_ = stage_a + stage * kAStage;
-                    uint8_t* sb_ = stage_b + stage * kBStage;
                     if (kb < p.kb_int) {
                         const int x = (part * p.kb_int_part + kb) * kRowBytes;
                         tma_load_2d(sa_, &p.tm_a, &full[stage], x, m0, pol_a);
-                        tma_load_2d(sb_, &p.tm_b, &full[stage], x, b0, pol_b);
-                        tma_load_2d(sb_ + kBStage / 2, &p.tm_b, &full[stage], x, b1, pol_b);
                     } else {
                         const int x = (part * p.kb_f16_part + kb - p.kb_int) * (kRowBytes / 2);
                         tma_load_2d(sa_, &p.tm_ah, &full[stage], x, m0, pol_a);
-                        tma_load_2d(sb_, &p.tm_bh, &full[stage], x, b0, pol_b);
-                        tma_load_2d(sb_ + kBStage / 2, &p.tm_bh, &full[stage], x, b1, pol_b);
                     }
+                    if (!prefetched) load_b(stage, kb, part, b0, b1);
                     armed |= 1u << stage;
                     armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
@@ -489,6 +533,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         phase ^= 1;
                     }
                 }
+                first = false;
             }
             // Drain: every copy this thread started must have landed before the CTA can exit.
             for (int s = 0; s < STAGES; ++s) {
@@ -502,6 +547,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     } else if (warp == 1) {
         // ------------------------------------------------------------------------------- MMA issuer
         if (lane == 0) {
+            const int split = dependency_wait();
             const uint32_t idesc_i8 = SWAP ? idesc_i8_s32(kBM, p.n_tok) : idesc_i8_s32(kBM, kBN);
             const uint32_t idesc_f16 = SWAP ? idesc_bf16_f32(kBM, p.n_tok) : idesc_bf16_f32(kBM, kBN);
             int stage = 0;
@@ -591,6 +637,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         silu_table_fill(silu_tab_s, threadIdx.x - kCtlThreads, EPI_WARPS * 32);
         named_bar_sync(1, EPI_WARPS * 32);
     }
+    const int split = dependency_wait();
     {
         // --------------------------------------------------------------------------------- epilogue
         // Epilogue warps only ever stop at the accumulator wait, and only on its own timeout (no abort

@@ -10,6 +10,8 @@ namespace reax {
 // Division used by the quantizer where the reference writes a plain '/' in Triton
 // (reaxv2/quantize.py:18-19,42): kDivIeee = IEEE round-to-nearest, kDivFull = PTX div.full.f32.
 enum QuantDivision : int { kDivIeee = 0, kDivFull = 1 };
+// The division the library's quantizers use: Triton lowers the reference's fp32 '/' to div.full.f32.
+constexpr int kQuantDiv = kDivFull;
 
 template <int DIV>
 REAX_DEVI float quant_div(float a, float b) {
@@ -22,37 +24,42 @@ REAX_DEVI float quant_div(float a, float b) {
     }
 }
 
-// Block-wide max of non-negative floats (warp shuffles, then one value per warp in shared memory).
+// Max over `nthreads` threads (tid in [0, nthreads), whole warps) of non-negative, non-NaN floats (each
+// thread's fmaxf-accumulated absmax).  For such floats the order of the bit patterns as unsigned
+// integers is the order of the values, so one redux.sync per warp finds the warp's max; every thread
+// then reads the warps' maxima.  bar() synchronizes the nthreads threads.
+template <class Bar>
+REAX_DEVI float group_max_nonneg(float v, float* red, int tid, int nthreads, Bar bar) {
+    const unsigned m = __reduce_max_sync(0xffffffffu, __float_as_uint(v));
+    bar();   // red may still be read by a previous call
+    if ((tid & 31) == 0) red[tid / 32] = __uint_as_float(m);
+    bar();
+    float r = red[0];
+    for (int i = 1; i < nthreads / 32; ++i) r = fmaxf(r, red[i]);
+    return r;
+}
+
 REAX_DEVI float block_max_nonneg(float v, float* red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-        const int nw = blockDim.x / 32;
-        v = lane < nw ? red[lane] : 0.f;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0) red[32] = v;
-    }
-    __syncthreads();
-    return red[32];
+    return group_max_nonneg(v, red, threadIdx.x, blockDim.x, [] { __syncthreads(); });
 }
 
 // Eight consecutive quantizer inputs of one row: x[row, src[c]] for c in [c0, c0 + 8), as float.
-// One 16-byte load when the eight sources are consecutive and 16-byte aligned, gathers otherwise.
-REAX_DEVI void load8_columns(const __nv_bfloat16* xr, const int* src, bool aligned_x, float (&v)[8], int (&idx)[8]) {
-    const int4 i0 = __ldg(reinterpret_cast<const int4*>(src));
-    const int4 i1 = __ldg(reinterpret_cast<const int4*>(src) + 1);
+// With aligned_x the eight columns c0.. of x are requested together with the source indices (the usual
+// bank maps low column c to column c); when the indices confirm it, no further load is needed, else the
+// sources are loaded as one 16-byte run when consecutive and aligned, or gathered.
+REAX_DEVI void load8_columns(const __nv_bfloat16* xr, const int* src, int c0, bool aligned_x, float (&v)[8],
+                             int (&idx)[8]) {
+    const int4 i0 = __ldg(reinterpret_cast<const int4*>(src + c0));
+    const int4 i1 = __ldg(reinterpret_cast<const int4*>(src + c0) + 1);
+    uint4 guess = make_uint4(0u, 0u, 0u, 0u);
+    if (aligned_x) guess = __ldg(reinterpret_cast<const uint4*>(xr + c0));
     idx[0] = i0.x; idx[1] = i0.y; idx[2] = i0.z; idx[3] = i0.w;
     idx[4] = i1.x; idx[5] = i1.y; idx[6] = i1.z; idx[7] = i1.w;
     bool run = aligned_x && (idx[0] & 7) == 0;
 #pragma unroll
     for (int i = 1; i < 8; ++i) run = run && idx[i] == idx[0] + i;
     if (run) {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(xr + idx[0]));
+        const uint4 raw = idx[0] == c0 ? guess : __ldg(reinterpret_cast<const uint4*>(xr + idx[0]));
         const __nv_bfloat16* b = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(b[i]);
@@ -64,92 +71,119 @@ REAX_DEVI void load8_columns(const __nv_bfloat16* xr, const int* src, bool align
 
 // ------------------------------------------------------------------------------ a1: per-token quantization
 // One CTA per row (reaxv2/quantize.py:5-29).  Pass 1: v = (x - centre) / smoothing, absmax over the
-// row; scale = max(absmax, 1e-12) / 127.  Pass 2 recomputes v (same float ops, same result) and
-// stores nearbyint(div_rn(v, scale)) clamped to [-127, 127].  The row is re-read from L1/L2.
+// row; scale = max(absmax, 1e-12) / 127.  Pass 2 stores nearbyint(div_rn(v, scale)) clamped to
+// [-127, 127].  The first kQuantHeld chunks of 8 columns of each thread (rows up to 16384 columns with
+// kQuantThreads threads) keep v in registers between the passes; columns past them are recomputed from
+// a re-read of the row (same float ops, same result).
+constexpr int kQuantHeld = 4;
+constexpr int kQuantThreads = 512;
+
+// v for 8 consecutive low columns starting at c0.
 template <int DIV>
-__global__ void __launch_bounds__(256) quant_rows_kernel(const __nv_bfloat16* __restrict__ x,
+REAX_DEVI void quant_prep8(const __nv_bfloat16* xr, const int* low_columns, const float* smoothing,
+                           const float* centers, int c0, int center, bool aligned_x, float (&t)[8]) {
+    int idx[8];
+    load8_columns(xr, low_columns, c0, aligned_x, t, idx);
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(smoothing + c0));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(smoothing + c0) + 1);
+    const float sm[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float ce[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (center) {
+        const float4 c0v = __ldg(reinterpret_cast<const float4*>(centers + c0));
+        const float4 c1v = __ldg(reinterpret_cast<const float4*>(centers + c0) + 1);
+        ce[0] = c0v.x; ce[1] = c0v.y; ce[2] = c0v.z; ce[3] = c0v.w;
+        ce[4] = c1v.x; ce[5] = c1v.y; ce[6] = c1v.z; ce[7] = c1v.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t[i] = quant_div<DIV>(center ? __fsub_rn(t[i], ce[i]) : t[i], sm[i]);
+}
+
+// Codes of 8 values, stored at lr[c0..c0+8).
+REAX_DEVI void quant_store8(int8_t* lr, int c0, const float (&t)[8], float scale, bool vec_store) {
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float r = fminf(fmaxf(rintf(__fdiv_rn(t[i], scale)), -127.f), 127.f);
+        packed[i / 4] |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * (i % 4));
+    }
+    if (vec_store) {
+        *reinterpret_cast<uint2*>(lr + c0) = make_uint2(packed[0], packed[1]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) lr[c0 + i] = static_cast<int8_t>((packed[i / 4] >> (8 * (i % 4))) & 0xFFu);
+    }
+}
+
+// The low columns of one row, quantized by nthreads threads (tid in [0, nthreads)): codes into lr and
+// the scale into *scale_out; bar() synchronizes the nthreads threads, red holds nthreads / 32 floats.
+template <int DIV, class Bar>
+REAX_DEVI void quant_row(const __nv_bfloat16* xr, const int* low_columns, const float* smoothing,
+                         const float* centers, int center, bool aligned_x, int KL, int tid, int nthreads, float* red,
+                         Bar bar, int8_t* lr, float* scale_out) {
+    const int KL8 = KL & ~7;
+    const int step = nthreads * 8;
+    float held[kQuantHeld][8];
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < kQuantHeld; ++j) {
+        const int c0 = tid * 8 + j * step;
+        if (c0 < KL8) {
+            quant_prep8<DIV>(xr, low_columns, smoothing, centers, c0, center, aligned_x, held[j]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(held[j][i]));
+        }
+    }
+    for (int c0 = tid * 8 + kQuantHeld * step; c0 < KL8; c0 += step) {
+        float t[8];
+        quant_prep8<DIV>(xr, low_columns, smoothing, centers, c0, center, aligned_x, t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(t[i]));
+    }
+    for (int c = KL8 + tid; c < KL; c += nthreads) {
+        float t = __bfloat162float(xr[__ldg(low_columns + c)]);
+        if (center) t = __fsub_rn(t, __ldg(centers + c));
+        t = quant_div<DIV>(t, __ldg(smoothing + c));
+        amax = fmaxf(amax, fabsf(t));
+    }
+    amax = group_max_nonneg(amax, red, tid, nthreads, bar);
+    const float scale = quant_div<DIV>(fmaxf(amax, 1.0e-12f), 127.0f);
+    if (tid == 0) *scale_out = scale;
+    const bool vec_store = (KL & 7) == 0;
+#pragma unroll
+    for (int j = 0; j < kQuantHeld; ++j) {
+        const int c0 = tid * 8 + j * step;
+        if (c0 < KL8) quant_store8(lr, c0, held[j], scale, vec_store);
+    }
+    for (int c0 = tid * 8 + kQuantHeld * step; c0 < KL8; c0 += step) {
+        float t[8];
+        quant_prep8<DIV>(xr, low_columns, smoothing, centers, c0, center, aligned_x, t);
+        quant_store8(lr, c0, t, scale, vec_store);
+    }
+    for (int c = KL8 + tid; c < KL; c += nthreads) {
+        float t = __bfloat162float(xr[__ldg(low_columns + c)]);
+        if (center) t = __fsub_rn(t, __ldg(centers + c));
+        t = quant_div<DIV>(t, __ldg(smoothing + c));
+        const float r = fminf(fmaxf(rintf(__fdiv_rn(t, scale)), -127.f), 127.f);
+        lr[c] = static_cast<int8_t>(static_cast<int>(r));
+    }
+}
+
+template <int DIV>
+__global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const __nv_bfloat16* __restrict__ x,
                                                          const int* __restrict__ low_columns,
                                                          const int* __restrict__ high_columns,
                                                          const float* __restrict__ smoothing,
                                                          const float* __restrict__ centers, int8_t* __restrict__ low,
                                                          __nv_bfloat16* __restrict__ high, float* __restrict__ scales,
                                                          int K, int KL, int KH, int center, int aligned_x) {
-    __shared__ float red[33];
+    __shared__ float red[32];
     grid_dependency_wait();
     grid_dependents_launch();
     const int row = blockIdx.x;
     const __nv_bfloat16* xr = x + static_cast<size_t>(row) * K;
-    const int KL8 = KL & ~7;
     if (KL > 0) {
-        float amax = 0.f;
-        for (int c0 = threadIdx.x * 8; c0 < KL8; c0 += blockDim.x * 8) {
-            float v[8];
-            int idx[8];
-            load8_columns(xr, low_columns + c0, aligned_x != 0, v, idx);
-            const float4 s0 = __ldg(reinterpret_cast<const float4*>(smoothing + c0));
-            const float4 s1 = __ldg(reinterpret_cast<const float4*>(smoothing + c0) + 1);
-            const float sm[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-            float ce[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if (center) {
-                const float4 c0v = __ldg(reinterpret_cast<const float4*>(centers + c0));
-                const float4 c1v = __ldg(reinterpret_cast<const float4*>(centers + c0) + 1);
-                ce[0] = c0v.x; ce[1] = c0v.y; ce[2] = c0v.z; ce[3] = c0v.w;
-                ce[4] = c1v.x; ce[5] = c1v.y; ce[6] = c1v.z; ce[7] = c1v.w;
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                float t = center ? __fsub_rn(v[i], ce[i]) : v[i];
-                t = quant_div<DIV>(t, sm[i]);
-                amax = fmaxf(amax, fabsf(t));
-            }
-        }
-        for (int c = KL8 + threadIdx.x; c < KL; c += blockDim.x) {
-            float t = __bfloat162float(xr[__ldg(low_columns + c)]);
-            if (center) t = __fsub_rn(t, __ldg(centers + c));
-            t = quant_div<DIV>(t, __ldg(smoothing + c));
-            amax = fmaxf(amax, fabsf(t));
-        }
-        amax = block_max_nonneg(amax, red);
-        const float scale = quant_div<DIV>(fmaxf(amax, 1.0e-12f), 127.0f);
-        if (threadIdx.x == 0) scales[row] = scale;
-        int8_t* lr = low + static_cast<size_t>(row) * KL;
-        const bool vec_store = (KL & 7) == 0;
-        for (int c0 = threadIdx.x * 8; c0 < KL8; c0 += blockDim.x * 8) {
-            float v[8];
-            int idx[8];
-            load8_columns(xr, low_columns + c0, aligned_x != 0, v, idx);
-            const float4 s0 = __ldg(reinterpret_cast<const float4*>(smoothing + c0));
-            const float4 s1 = __ldg(reinterpret_cast<const float4*>(smoothing + c0) + 1);
-            const float sm[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-            float ce[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if (center) {
-                const float4 c0v = __ldg(reinterpret_cast<const float4*>(centers + c0));
-                const float4 c1v = __ldg(reinterpret_cast<const float4*>(centers + c0) + 1);
-                ce[0] = c0v.x; ce[1] = c0v.y; ce[2] = c0v.z; ce[3] = c0v.w;
-                ce[4] = c1v.x; ce[5] = c1v.y; ce[6] = c1v.z; ce[7] = c1v.w;
-            }
-            uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                float t = center ? __fsub_rn(v[i], ce[i]) : v[i];
-                t = quant_div<DIV>(t, sm[i]);
-                const float r = fminf(fmaxf(rintf(__fdiv_rn(t, scale)), -127.f), 127.f);
-                packed[i / 4] |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * (i % 4));
-            }
-            if (vec_store) {
-                *reinterpret_cast<uint2*>(lr + c0) = make_uint2(packed[0], packed[1]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) lr[c0 + i] = static_cast<int8_t>((packed[i / 4] >> (8 * (i % 4))) & 0xFFu);
-            }
-        }
-        for (int c = KL8 + threadIdx.x; c < KL; c += blockDim.x) {
-            float t = __bfloat162float(xr[__ldg(low_columns + c)]);
-            if (center) t = __fsub_rn(t, __ldg(centers + c));
-            t = quant_div<DIV>(t, __ldg(smoothing + c));
-            const float r = fminf(fmaxf(rintf(__fdiv_rn(t, scale)), -127.f), 127.f);
-            lr[c] = static_cast<int8_t>(static_cast<int>(r));
-        }
+        quant_row<DIV>(xr, low_columns, smoothing, centers, center, aligned_x != 0, KL, threadIdx.x, blockDim.x, red,
+                       [] { __syncthreads(); }, low + static_cast<size_t>(row) * KL, scales + row);
     } else if (threadIdx.x == 0) {
         scales[row] = 1.0f;
     }

@@ -1,7 +1,7 @@
 """Drop-in for ``reaxv2/gate_up.py``: the hybrid INT8/BF16 gate/up + SwiGLU operator.
 
-``Native.project(x, p, name, drop)`` quantizes the activations and calls ``product``; ``product``
-launches one tcgen05 kernel (``reax_gate_up_i8``) that computes the int32 INT8 GEMM of the gate and
+``Native.project(x, p, name, drop)`` quantizes the activations and runs the product in one library call
+(``reax_project_i8``); ``product`` launches one tcgen05 kernel (``reax_gate_up_i8``) that computes the int32 INT8 GEMM of the gate and
 up rows, dequantizes ``((acc * sa[row]) * sw[col]) + bias[col]``, adds the BF16 outlier columns and
 writes ``bf16(silu(g)) * u`` as bf16 (reference: reaxv2/gate_up.py:11-37 and
 kernel-source/legacy-v2/src/native_hybrid8.cu:4-28).
@@ -85,5 +85,29 @@ class Native(NativeInt8):
         return gate_up_i8(x, w, xh, wh, sa, sw, bias)
 
     def project(self, x, p, name, drop=0):
-        low, high, scales = quantize_rows(x, p)
-        return self.product(low, p.low_weight, high, p.high_weight, scales, p.scales, p.bias, name, drop)
+        """quantize_rows + product in one library call (``reax_project_i8``), which lets the GEMM start
+        loading weights while the quantizer runs; same results as the two calls."""
+        m = len(x)
+        kl, kh = len(p.low_columns), len(p.high_columns)
+        n2 = len(p.low_weight)
+        assert kl % 128 == 0 and kh % 64 == 0 and n2 % self.tile_n(name) == 0
+        _native.require_cuda(x, p.low_weight, p.scales, p.bias)
+        if x.dtype != torch.bfloat16:
+            raise RuntimeError("project: x must be a bfloat16 tensor")
+        for t in (x, p.low_columns, p.high_columns, p.smoothing, p.centers, p.low_weight, p.high_weight, p.scales,
+                  p.bias):
+            if t is not None and not t.is_contiguous():
+                raise RuntimeError("project: operands must be contiguous")
+        low = torch.empty((m, kl), device=x.device, dtype=torch.int8)
+        high = torch.empty((m, kh), device=x.device, dtype=torch.bfloat16)
+        scales = torch.empty(m, device=x.device)
+        out = torch.empty((m, n2 // 2), device=x.device, dtype=torch.bfloat16)
+        with torch.cuda.device(x.device):
+            ws = _native.workspace(x.device)
+            _native.check(_native.load().reax_project_i8(
+                x.data_ptr(), p.low_columns.data_ptr(), _native.ptr(p.high_columns) if kh else None,
+                p.smoothing.data_ptr(), _native.ptr(p.centers), 1 if p.centered else 0, p.low_weight.data_ptr(),
+                _native.ptr(p.high_weight) if kh else None, p.scales.data_ptr(), p.bias.data_ptr(), low.data_ptr(),
+                _native.ptr(high) if kh else None, scales.data_ptr(), out.data_ptr(), m, p.width, kl, kh, n2,
+                out.stride(0), ws.data_ptr(), ws.numel(), _native.stream_handle(x.device)))
+        return out

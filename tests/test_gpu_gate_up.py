@@ -116,6 +116,22 @@ def test_silu_range_edges(M):
     compare_int8(H.activations(g, M, 1024), bank)
 
 
+@pytest.mark.parametrize("M,K,Hh,KH", [(1, 4096, 14336, 0), (64, 4096, 14336, 0), (300, 1024, 4096, 0),
+                                       (200, 2560, 1024, 128)])
+def test_project_entry_matches_two_calls(M, K, Hh, KH):
+    """reax_project_i8 (the quantizer, then the GEMM requesting its first weight tiles while the quantizer
+    runs) gives the bits of quantize_rows followed by gate_up_i8."""
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native, gate_up_i8, quantize_rows
+    g = H.gen(31 * M + K + Hh + KH)
+    x = H.activations(g, M, K).cuda()
+    bank = H.bank_to(H.int8_bank(g, K, Hh, KH=KH, centered=KH > 0), "cuda")
+    fused = Native(None).project(x, bank, "hybrid8_b128n256_s64n256")
+    low, high, sc = quantize_rows(x, bank)
+    two = gate_up_i8(low, bank.low_weight, high, bank.high_weight, sc, bank.scales, bank.bias)
+    torch.cuda.synchronize()
+    assert torch.equal(fused.view(torch.int16), two.view(torch.int16))
+
+
 def test_cfg3_prefill_rows_sample():
     """BASELINE config 3 (M=4096, K=4096, H=14336): full GPU run, oracle on a sample of rows."""
     g = H.gen(3)
