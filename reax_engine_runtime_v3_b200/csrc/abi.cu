@@ -89,7 +89,7 @@ int variant_of(int epi, const reax::TcParams& p) {
 // scales/biases (2 x 2 x 256 floats) + barriers
 constexpr size_t tc_smem_bytes() {
     return static_cast<size_t>(kStages) * reax::kStageBytes + reax::kOutStageBytes + reax::kSiluTabBytes + 1024 +
-           4096 + 256;
+           4096 + 512;
 }
 
 // Current device, its SM count, and a check that it is sm_100; sets kernel attributes once.
@@ -237,11 +237,45 @@ void plan_schedule(reax::TcParams& p, int sms, bool allow_split, int* grid) {
 // partial wave of at least half the SMs, an even share R = ceil(H / (waves * SMs)) <= 128 rows per tile
 // fills whole waves instead, so no tile is split by K.  The TMA box then covers R weight rows, the MMA
 // still computes 128 (rows past R are never stored), and the weight bytes read stay the same.
-int swap_rows_for(int H, int sms) {
+// Weight-major pipeline: stages of [gate box | up box | activation box] (each 128 bytes wide, the weight
+// boxes rounded up to whole 8-row swizzle atoms), as many as fit the kStages x kStageBytes pool (at most
+// kMaxStages).  The M = 128 MMAs read 128 rows from each weight box, so the last stage's up box keeps
+// 16 KiB of the pool behind it.
+void set_swap_pipeline(reax::TcParams& p) {
+    const int r8 = (p.tile_rows + 7) & ~7;
+    const int bytes = (((2 * r8 + p.n_tok) * reax::kRowBytes) + 1023) & ~1023;
+    const int pool = kStages * reax::kStageBytes;
+    int stages = (pool - r8 * reax::kRowBytes - reax::kBM * reax::kRowBytes) / bytes + 1;
+    if (stages > reax::kMaxStages) stages = reax::kMaxStages;
+    p.tile_rows8 = r8;
+    p.stage_bytes = bytes;
+    p.stages = stages;
+}
+
+int tile_rows_for(int H, int sms) {
     const int t128 = (H + 127) / 128;
     if (t128 % sms == 0 || 2 * t128 < sms) return 128;
     const int waves = (t128 + sms - 1) / sms;
     return (H + waves * sms - 1) / (waves * sms);
+}
+
+// Tile plan of a SwiGLU gate/up launch: orientation, gate rows per tile, activation box rows.  Few
+// tokens take weight-major tiles (the weights as the MMA's A operand; measured faster on B200 than
+// token-major tiles of the same rows) unless BF16 outlier columns need token-major tiles; either way
+// with balanced gate rows and an activation box of round16(M) rows.  Returns whether the tiles are
+// weight-major.
+bool plan_gate_up_tiles(reax::TcParams& p, int M, int H, bool weight_major_ok, int sms) {
+    const bool few = M <= kSwapMaxRows;
+    const bool swap = weight_major_ok && few;
+    p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
+    p.tile_rows = few ? tile_rows_for(H, sms) : 128;
+    p.tile_rows8 = (p.tile_rows + 7) & ~7;
+    p.a_rows = M < reax::kBM ? ((M + 15) / 16) * 16 : reax::kBM;
+    if (swap) set_swap_pipeline(p);
+    // out 16-byte aligned and ldo % 8 == 0 (checked by the callers): 128-row weight-major tiles store
+    // through shared memory in 16-byte pieces; balanced weight-major tiles store their columns directly
+    p.out_vec16 = p.tile_rows == 128 ? 1 : 0;
+    return swap;
 }
 
 int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
@@ -267,7 +301,9 @@ void init_params(reax::TcParams& p) {
     p.acc_bufs = 2;
     p.timeout_ns = g_timeout_ns;
     p.parts = 1;
-    p.swap_rows = 128;
+    p.tile_rows = 128;
+    p.tile_rows8 = 128;
+    p.a_rows = 128;
 }
 
 // Plain launch (no attributes) whose error comes from the launch call itself, so no sticky error
@@ -372,22 +408,17 @@ int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const vo
     reax::TcParams p;
     init_params(p);
     // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
-    const bool swap = KH == 0 && M <= kSwapMaxRows;
-    p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
-    p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
-    // out 16-byte aligned and ldo % 8 == 0 (checked above): 128-row weight-major tiles store through
-    // shared memory in 16-byte pieces; balanced tiles store their columns directly
-    p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
+    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KH == 0, info->sms);
     if (KL) {
-        if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
+        if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
             return rc;
-        if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, swap ? p.swap_rows : 128)) !=
+        if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, p.tile_rows)) !=
             REAX_OK)
             return rc;
     }
     if (KH) {
-        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH)) != REAX_OK) return rc;
-        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH, p.a_rows)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH, p.tile_rows)) != REAX_OK) return rc;
     }
     if (!KL) {
         p.tm_a = p.tm_ah;
@@ -407,7 +438,7 @@ int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const vo
     p.kb_int = KL / 128;
     p.kb_f16 = KH / 64;
     p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
-    p.n_tiles = (N2 / 2 + p.swap_rows - 1) / p.swap_rows;
+    p.n_tiles = (N2 / 2 + p.tile_rows - 1) / p.tile_rows;
     p.tiles = p.m_tiles * p.n_tiles;
     p.mode = 0;
     p.acc_bufs = KH ? 1 : 2;
@@ -417,7 +448,7 @@ int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const vo
     p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
     p.early_b = early_b;
     int grid = 0;
-    plan_schedule(p, info->sms, KH == 0 && p.swap_rows == 128, &grid);
+    plan_schedule(p, info->sms, KH == 0 && p.tile_rows == 128, &grid);
     return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
 }
 
@@ -577,15 +608,10 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
     reax::TcParams p;
     init_params(p);
-    const bool swap = M <= kSwapMaxRows;
-    p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
-    p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
-    // out 16-byte aligned and ldo % 8 == 0 (checked above): 128-row weight-major tiles store through
-    // shared memory in 16-byte pieces; balanced tiles store their columns directly
-    p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
-    if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : 128)) != REAX_OK)
+    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, true, info->sms);
+    if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : p.a_rows)) != REAX_OK)
         return rc;
-    if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K, swap ? p.swap_rows : 128)) !=
+    if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K, p.tile_rows)) !=
         REAX_OK)
         return rc;
     p.tm_a = p.tm_ah;
@@ -597,7 +623,7 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     p.kb_int = 0;
     p.kb_f16 = K / 64;
     p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
-    p.n_tiles = (N2 / 2 + p.swap_rows - 1) / p.swap_rows;
+    p.n_tiles = (N2 / 2 + p.tile_rows - 1) / p.tile_rows;
     p.tiles = p.m_tiles * p.n_tiles;
     p.mode = 1;
     p.acc_bufs = 2;
@@ -777,19 +803,14 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
 
     reax::TcParams p;
     init_params(p);
-    const bool swap = KH == 0 && M <= kSwapMaxRows;
-    p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
-    p.swap_rows = swap ? swap_rows_for(N2 / 2, info->sms) : 128;
-    // out 16-byte aligned and ldo % 8 == 0 (checked above): 128-row weight-major tiles store through
-    // shared memory in 16-byte pieces; balanced tiles store their columns directly
-    p.out_vec16 = p.swap_rows == 128 ? 1 : 0;
-    if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : 128)) != REAX_OK)
+    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KH == 0, info->sms);
+    if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
         return rc;
-    if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, swap ? p.swap_rows : 128)) != REAX_OK)
+    if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, p.tile_rows)) != REAX_OK)
         return rc;
     if (KH) {
-        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH)) != REAX_OK) return rc;
-        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH, p.a_rows)) != REAX_OK) return rc;
+        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH, p.tile_rows)) != REAX_OK) return rc;
     } else {
         p.tm_ah = p.tm_a;
         p.tm_bh = p.tm_b;
@@ -804,7 +825,7 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     p.kb_int = KL / 128;
     p.kb_f16 = KH / 64;
     p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
-    p.n_tiles = (N2 / 2 + p.swap_rows - 1) / p.swap_rows;
+    p.n_tiles = (N2 / 2 + p.tile_rows - 1) / p.tile_rows;
     p.tiles = p.m_tiles * p.n_tiles;
     p.mode = 0;
     p.acc_bufs = KH ? 1 : 2;
@@ -812,7 +833,7 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     // Whole-tile plans need no partials; a plan that splits tiles is re-planned for at most
     // kNoAllocMaxCtas CTAs, whose partials the static scratch holds.
     int grid = 0;
-    plan_schedule(p, info->sms, KH == 0 && p.swap_rows == 128, &grid);
+    plan_schedule(p, info->sms, KH == 0 && p.tile_rows == 128, &grid);
     int ctas = grid;
     if (p.sk_iters > 0 && grid > kNoAllocMaxCtas) {
         plan_schedule(p, kNoAllocMaxCtas, true, &grid);

@@ -33,6 +33,10 @@ constexpr int kRowBytes = 128;                  // K bytes per stage row: one 12
 constexpr int kAStage = kBM * kRowBytes;        // 16 KiB
 constexpr int kBStage = kBN * kRowBytes;        // 32 KiB
 constexpr int kStageBytes = kAStage + kBStage;  // 48 KiB
+// Weight-major plans carve the same pool (STAGES x kStageBytes) into up to kMaxStages smaller stages:
+// [gate box | up box | activation box], sized by the plan, so more K blocks are in flight when tiles
+// have few rows.
+constexpr int kMaxStages = 16;
 constexpr int kTmemCols = 512;
 constexpr int kSlotInts = kBM * kBN;            // one split-tile partial: 128 x 256 int32 (128 KiB)
 constexpr int kSwapMaxTok = 64;                 // weight-major tiles: at most 64 token columns per accumulator
@@ -90,7 +94,14 @@ struct TcParams {
     int evict_first_b;   // stream B with an evict-first L2 policy (weights read once)
     int n_tok;           // weight-major (swap) kernels: token columns per accumulator, a multiple of 16 >= M
     int out_vec16;       // out is 16-byte aligned and ldo a multiple of 8: rows can be stored in 16-byte pieces
-    int swap_rows;       // weight-major tiles: gate rows (and as many up rows) per tile, <= 128
+    // SwiGLU tiles: gate rows (and as many up rows) per tile, <= 128 (128 unless the plan balances
+    // R = ceil(H / SMs) rows per tile).  The up rows follow the gate rows tile_rows8 rows further on
+    // in the B stage (and in TMEM for token-major tiles).
+    int tile_rows;
+    int tile_rows8;      // tile_rows rounded up to whole 8-row swizzle atoms
+    int a_rows;          // token-major: activation rows per A box (128, or n_tok rounded to 16 for few tokens)
+    int stages;          // weight-major pipeline stages (<= kMaxStages)
+    int stage_bytes;     // weight-major stage size (a multiple of 1024)
     // The kernel before this one on the stream is this library's quantizer, which signals its dependents
     // only after its own dependency wait: the first weight tiles may be requested before this kernel's
     // wait, since nothing in flight then can still be writing them (not with slice_mode).
@@ -341,7 +352,7 @@ REAX_DEVI bool count_published(const TcParams& p, const Segment& seg, int st, in
 REAX_DEVI float4 swap_column_scales(const TcParams& p, const Segment& s, int row) {
     int part, mt, nt;
     tile_coords(p, s.tile, part, mt, nt);
-    const int j = min(nt * p.swap_rows + row, p.H - 1);   // lanes past the tile's rows load a valid column
+    const int j = min(nt * p.tile_rows + row, p.H - 1);   // lanes past the tile's rows load a valid column
     return make_float4(__ldg(p.sw + j), __ldg(p.sw + p.H + j), __ldg(p.bias + j), __ldg(p.bias + p.H + j));
 }
 
@@ -397,18 +408,30 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     float* stage_sw = reinterpret_cast<float*>(out_stage + kOutStageBytes + kSiluTabBytes);   // [2][kBN]
     float* stage_bias = stage_sw + 2 * kBN;                                    // [2][kBN]
     uint64_t* full = reinterpret_cast<uint64_t*>(stage_bias + 2 * kBN);
-    uint64_t* empty = full + STAGES;
-    uint64_t* acc_full = empty + STAGES;
+    uint64_t* empty = full + kMaxStages;
+    uint64_t* acc_full = empty + kMaxStages;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     int* last_flag = abort_flag + 1;
+    // pipeline stages and the boxes inside them
+    const int ns = SWAP ? p.stages : STAGES;
+    auto box_a = [&](int st) -> uint8_t* {   // activation box (weight-major) or A tile
+        return SWAP ? smem + st * p.stage_bytes + 2 * p.tile_rows8 * kRowBytes : stage_a + st * kAStage;
+    };
+    auto box_b = [&](int st) -> uint8_t* {   // gate rows (weight-major) or the first half of B
+        return SWAP ? smem + st * p.stage_bytes : stage_b + st * kBStage;
+    };
+    auto box_bu = [&](int st) -> uint8_t* {  // up rows (weight-major) or the second half of B
+        return SWAP ? smem + st * p.stage_bytes + p.tile_rows8 * kRowBytes
+                    : stage_b + st * kBStage + (EPI == kEpiSwiglu ? p.tile_rows8 * kRowBytes : kBStage / 2);
+    };
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < ns; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -450,7 +473,9 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     };
     // bytes a stage receives: weight-major tiles load n_tok activation rows instead of 128
     const uint32_t stage_tx =
-        SWAP ? static_cast<uint32_t>((2 * p.swap_rows + p.n_tok) * kRowBytes) : static_cast<uint32_t>(kStageBytes);
+        SWAP ? static_cast<uint32_t>((2 * p.tile_rows + p.n_tok) * kRowBytes)
+             : (EPI == kEpiSwiglu ? static_cast<uint32_t>((p.a_rows + 2 * p.tile_rows) * kRowBytes)
+                                  : static_cast<uint32_t>(kStageBytes));
 
     if (warp < kCtlWarps) {
     regs_shrink<kCtlRegs>();
@@ -465,26 +490,25 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             uint32_t armed_parity = 0; // bit s: parity of the last arming of stage s
             // B (weight) boxes of K block kb of a tile into stage st
             auto load_b = [&](int st, int kb, int part, int b0, int b1) {
-                uint8_t* sb_ = stage_b + st * kBStage;
                 if (kb < p.kb_int) {
                     const int x = (part * p.kb_int_part + kb) * kRowBytes;
-                    tma_load_2d(sb_, &p.tm_b, &full[st], x, b0, pol_b);
-                    tma_load_2d(sb_ + kBStage / 2, &p.tm_b, &full[st], x, b1, pol_b);
+                    tma_load_2d(box_b(st), &p.tm_b, &full[st], x, b0, pol_b);
+                    tma_load_2d(box_bu(st), &p.tm_b, &full[st], x, b1, pol_b);
                 } else {
                     const int x = (part * p.kb_f16_part + kb - p.kb_int) * (kRowBytes / 2);
-                    tma_load_2d(sb_, &p.tm_bh, &full[st], x, b0, pol_b);
-                    tma_load_2d(sb_ + kBStage / 2, &p.tm_bh, &full[st], x, b1, pol_b);
+                    tma_load_2d(box_b(st), &p.tm_bh, &full[st], x, b0, pol_b);
+                    tma_load_2d(box_bu(st), &p.tm_bh, &full[st], x, b1, pol_b);
                 }
             };
             auto tile_rows = [&](const Segment& sg, int& part, int& m0, int& b0, int& b1) {
                 int mt, nt;
                 tile_coords(p, sg.tile, part, mt, nt);
                 m0 = mt * kBM;
-                const int rows = SWAP ? p.swap_rows : kBN / 2;   // gate rows of the tile
+                const int rows = p.tile_rows;   // gate rows of a SwiGLU tile
                 b0 = (EPI == kEpiSwiglu) ? nt * rows : nt * kBN;
                 b1 = (EPI == kEpiSwiglu) ? p.H + nt * rows : nt * kBN + kBN / 2;
             };
-            // early_b: the weight boxes of the first segment's first STAGES K blocks are requested before
+            // early_b: the weight boxes of the first segment's first ns K blocks are requested before
             // the dependency wait (the weights are not produced by the kernel this one waits for).
             int pre = 0;
             if (p.early_b && !p.slice_mode) {
@@ -493,7 +517,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 if (cursor_next(p, 0, c0, s0)) {
                     int part, m0, b0, b1;
                     tile_rows(s0, part, m0, b0, b1);
-                    pre = min(STAGES, s0.k1 - s0.k0);
+                    pre = min(ns, s0.k1 - s0.k0);
                     for (int i = 0; i < pre; ++i) {
                         mbar_arrive_expect_tx(&full[i], stage_tx);
                         load_b(i, s0.k0 + i, part, b0, b1);
@@ -517,7 +541,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     }
                     const bool prefetched = first && kb - seg.k0 < pre;   // armed, B boxes requested
                     if (!prefetched) mbar_arrive_expect_tx(&full[stage], stage_tx);
-                    uint8_t* sa_ = stage_a + stage * kAStage;
+                    uint8_t* sa_ = box_a(stage);
                     if (kb < p.kb_int) {
                         const int x = (part * p.kb_int_part + kb) * kRowBytes;
                         tma_load_2d(sa_, &p.tm_a, &full[stage], x, m0, pol_a);
@@ -528,7 +552,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     if (!prefetched) load_b(stage, kb, part, b0, b1);
                     armed |= 1u << stage;
                     armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
-                    if (++stage == STAGES) {
+                    if (++stage == ns) {
                         stage = 0;
                         phase ^= 1;
                     }
@@ -536,7 +560,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 first = false;
             }
             // Drain: every copy this thread started must have landed before the CTA can exit.
-            for (int s = 0; s < STAGES; ++s) {
+            for (int s = 0; s < ns; ++s) {
                 if (armed & (1u << s)) {
                     if (!mbar_wait_bounded(&full[s], (armed_parity >> s) & 1, p.timeout_ns, nullptr)) {
                         atomicOr(p.status, kStatusTimeoutDrain);
@@ -548,8 +572,10 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         // ------------------------------------------------------------------------------- MMA issuer
         if (lane == 0) {
             const int split = dependency_wait();
-            const uint32_t idesc_i8 = SWAP ? idesc_i8_s32(kBM, p.n_tok) : idesc_i8_s32(kBM, kBN);
-            const uint32_t idesc_f16 = SWAP ? idesc_bf16_f32(kBM, p.n_tok) : idesc_bf16_f32(kBM, kBN);
+            // token-major SwiGLU tiles: N = the gate rows and the up rows of the tile (2 x tile_rows8)
+            const int n_mma = SWAP ? p.n_tok : (EPI == kEpiSwiglu ? 2 * p.tile_rows8 : kBN);
+            const uint32_t idesc_i8 = idesc_i8_s32(kBM, n_mma);
+            const uint32_t idesc_f16 = idesc_bf16_f32(kBM, n_mma);
             int stage = 0;
             uint32_t phase = 0;
             int buf = 0;
@@ -573,9 +599,9 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ad = sw128_kmajor_desc(smem_u32(stage_a + stage * kAStage));
-                    const uint64_t bd = sw128_kmajor_desc(smem_u32(stage_b + stage * kBStage));
-                    const uint64_t bd_up = sw128_kmajor_desc(smem_u32(stage_b + stage * kBStage + kBStage / 2));
+                    const uint64_t ad = sw128_kmajor_desc(smem_u32(box_a(stage)));
+                    const uint64_t bd = sw128_kmajor_desc(smem_u32(box_b(stage)));
+                    const uint64_t bd_up = sw128_kmajor_desc(smem_u32(box_bu(stage)));
                     if (kb < p.kb_int) {
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
@@ -600,7 +626,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         }
                     }
                     umma_commit(&empty[stage]);
-                    if (++stage == STAGES) {
+                    if (++stage == ns) {
                         stage = 0;
                         phase ^= 1;
                     }
@@ -680,10 +706,10 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             if constexpr (SWAP) {
                 // ---------------------------------------------- weight-major tile: lanes are weight rows
                 const int n_tok = p.n_tok;
-                const int n0 = nt * p.swap_rows;               // gate row (= output column) of lane 0
+                const int n0 = nt * p.tile_rows;               // gate row (= output column) of lane 0
                 const int j = n0 + r_tile;                     // this thread's output column
                 // lanes past the tile's rows (or past H in the last tile) hold rows of no output column
-                const bool col_ok = r_tile < p.swap_rows && j < p.H;
+                const bool col_ok = r_tile < p.tile_rows && j < p.H;
                 const int per_warp = n_tok / kSplit;           // token columns each warp finishes
                 const int tok_lo = (e / 4) * per_warp;
                 const int n_w = min(per_warp, p.M - tok_lo);   // real tokens among them (<= 0: none)
@@ -701,6 +727,10 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 // columns past the warp's real tokens compute on padding and are never stored.
                 auto segment = [&](auto pairs_c) -> bool {
                     constexpr int PAIRS = decltype(pairs_c)::value;
+                    // this warp's gate and up accumulators of its token columns
+                    auto load_acc = [&](uint32_t (&g)[2 * PAIRS], uint32_t (&u)[2 * PAIRS]) {
+                        tmem_ld_pairs_sync<PAIRS>(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
+                    };
                     int4 qg[PAIRS / 2], qu[PAIRS / 2];   // the first contributor's partial of these columns
                     auto fetch_first = [&]() {
 #pragma unroll
@@ -728,7 +758,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         // then count this CTA's K blocks; the contributor whose count completes the tile
                         // finishes it.  One thread fences for the CTA after the barrier.
                         uint32_t g[2 * PAIRS], u[2 * PAIRS];
-                        tmem_ld_pairs_sync<PAIRS>(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
+                        load_acc(g, u);
                         int4* slot = reinterpret_cast<int4*>(
                             p.ws_partials + (static_cast<size_t>(blockIdx.x) * 2 + sk_slot(p, blockIdx.x, st)) * kSlotInts);
 #pragma unroll
@@ -746,7 +776,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     uint32_t o[PAIRS];
                     if (n_w > 0) {
                         uint32_t g[2 * PAIRS], u[2 * PAIRS];
-                        tmem_ld_pairs_sync<PAIRS>(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
+                        load_acc(g, u);
                         if (n_contrib > 0) {
 #pragma unroll
                             for (int c = 0; c < PAIRS / 2; ++c) {
@@ -801,7 +831,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         named_bar_sync(1, EPI_WARPS * 32);
                         if (!whole && threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
                         // one token row per warp and iteration, one 16-byte piece per lane (at most 17 pieces)
-                        const int n_end = min(n0 + p.swap_rows, p.H);       // one past the tile's last column
+                        const int n_end = min(n0 + p.tile_rows, p.H);       // one past the tile's last column
                         const int pieces = (ph + (n_end - n0) + 7) >> 3;
                         const int c0 = n0 - ph + 8 * lane;                 // first column of this lane's piece
                         const bool full = c0 >= n0 && c0 + 8 <= n_end;
@@ -845,9 +875,14 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 if (!ok) break;
             } else {
                 // ------------------------------------------------ token-major tile: lanes are token rows
-                constexpr int kCols = (EPI == kEpiSwiglu) ? kBN / 2 : kBN;   // output columns of a tile
+                constexpr int kCols = (EPI == kEpiSwiglu) ? kBN / 2 : kBN;   // output columns of a tile, at most
                 const int c_lo = (e / 4) * (kCols / kSplit);
                 const int c_hi = c_lo + kCols / kSplit;
+                // SwiGLU tiles hold tile_rows gate columns (the last tile of a row may hold fewer: c_end) and
+                // their up columns up_off TMEM columns further on
+                const int rows = (EPI == kEpiSwiglu) ? p.tile_rows : kBN;
+                const int up_off = (EPI == kEpiSwiglu) ? p.tile_rows8 : 0;
+                const int c_end = (EPI == kEpiSwiglu) ? min(rows, p.H - nt * rows) : kBN;
                 const int grow = m0 + r_tile;
                 const bool row_ok = grow >= row_lo && grow < row_hi;
                 // Stage this tile's column scales / biases and this row's scale while the MMAs still run.
@@ -855,8 +890,9 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 if constexpr (MODE == 0) {
                     for (int t = threadIdx.x - kCtlThreads; t < kBN; t += EPI_WARPS * 32) {
                         int col;
-                        if constexpr (EPI == kEpiSwiglu)
-                            col = part * p.n_part_stride + nt * (kBN / 2) + (t < kBN / 2 ? t : p.H + t - kBN / 2);
+                        if constexpr (EPI == kEpiSwiglu)   // columns past c_end repeat a valid one (never stored)
+                            col = part * p.n_part_stride + nt * rows +
+                                  (t < kBN / 2 ? min(t, c_end - 1) : p.H + min(t - kBN / 2, c_end - 1));
                         else
                             col = part * p.n_part_stride + nt * kBN + t;
                         s_sw[t] = __ldg(p.sw + col);
@@ -872,9 +908,9 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 tc_fence_after();
                 bool finish = whole;
                 if (!whole) {
-                    // SwiGLU tiles publish the gate columns [c_lo, c_hi) and the up columns 128 + [c_lo, c_hi)
-                    finish = publish_partial<EPI_WARPS, 32>(p, seg, st, t_int, c_lo, c_hi,
-                                                            EPI == kEpiSwiglu ? kBN / 2 : 0, r_tile, row_ok, last_flag);
+                    // SwiGLU tiles publish the gate columns [c_lo, c_hi) and the up columns up_off + [c_lo, c_hi)
+                    finish = publish_partial<EPI_WARPS, 32>(p, seg, st, t_int, c_lo, c_hi, up_off, r_tile, row_ok,
+                                                            last_flag);
                 }
                 if (finish) {
                     const int4* contrib[kMaxContrib];
@@ -882,13 +918,14 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     constexpr bool add_f = (MODE == 0 && ADD_F);
                     const uint64_t sa2 = f2(sa_row, sa_row);
                     for (int cc = c_lo; cc < c_hi; cc += 32) {
+                        if (cc >= c_end) break;   // the same for the whole CTA
                         uint32_t g[32];
                         uint32_t u[32];
                         uint32_t fg[32];
                         uint32_t fu[32];
                         if constexpr (EPI == kEpiSwiglu) {
-                            tmem_ld2_x32_sync(t_acc + cc, t_acc + kBN / 2 + cc, g, u);
-                            if constexpr (add_f) tmem_ld2_x32_sync(t_f32 + cc, t_f32 + kBN / 2 + cc, fg, fu);
+                            tmem_ld2_x32_sync(t_acc + cc, t_acc + up_off + cc, g, u);
+                            if constexpr (add_f) tmem_ld2_x32_sync(t_f32 + cc, t_f32 + up_off + cc, fg, fu);
                         } else {
                             tmem_ld_x32_sync(t_acc + cc, g);
                             if constexpr (add_f) tmem_ld_x32_sync(t_f32 + cc, fg);
@@ -898,7 +935,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         if (__all_sync(0xFFFFFFFFu, !row_ok)) continue;
                         if (row_ok && !whole) {
                             add_partials<32>(contrib, n_contrib, cc, r_tile, g);
-                            if constexpr (EPI == kEpiSwiglu) add_partials<32>(contrib, n_contrib, kBN / 2 + cc, r_tile, u);
+                            if constexpr (EPI == kEpiSwiglu) add_partials<32>(contrib, n_contrib, up_off + cc, r_tile, u);
                         }
                         uint32_t packed[16];
                         __nv_bfloat16* dst;
@@ -924,7 +961,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                                 }
                                 packed[i / 2] = swiglu2_bits(bf16x2_rn(vg), bf16x2_rn(vu), silu_tab_s);
                             }
-                            dst = p.out + static_cast<size_t>(grow) * p.ldo + nt * (kBN / 2) + cc;
+                            dst = p.out + static_cast<size_t>(grow) * p.ldo + nt * rows + cc;
                         } else {
 #pragma unroll
                             for (int i = 0; i < 32; i += 2) {
@@ -942,10 +979,18 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             dst = p.out + out_part * p.out_part_stride + static_cast<size_t>(grow) * p.ldo + nt * kBN + cc;
                         }
                         if (row_ok) {
+                            if (EPI != kEpiSwiglu || (rows & 7) == 0) {
+                                // 16-byte pieces: c_end is a multiple of 8, so a piece is wholly in or out
 #pragma unroll
-                            for (int i = 0; i < 4; ++i)
-                                reinterpret_cast<uint4*>(dst)[i] =
-                                    make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                                for (int i = 0; i < 4; ++i)
+                                    if (cc + 8 * i < c_end)
+                                        reinterpret_cast<uint4*>(dst)[i] =
+                                            make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                            } else {
+#pragma unroll
+                                for (int i = 0; i < 32; ++i)
+                                    if (cc + i < c_end) dst[i] = __ushort_as_bfloat16(static_cast<uint16_t>(packed[i / 2] >> (16 * (i & 1))));
+                            }
                         }
                     }
                     if (!whole) {

@@ -147,12 +147,15 @@ def test_cfg5_outliers():
         compare_int8(H.activations(g, M, 4096, "student"), bank, rows=np.arange(0, M, 3))
 
 
-def test_hybrid_bank_with_outlier_columns():
-    """Production-style bank: centred, power-of-two smoothing, bias, 128 BF16 outlier columns."""
+@pytest.mark.parametrize("M,K,Hh", [(200, 2560, 1024), (8, 2560, 10240), (40, 1280, 10240)])
+def test_hybrid_bank_with_outlier_columns(M, K, Hh):
+    """Production-style bank: centred, power-of-two smoothing, bias, 128 BF16 outlier columns.  Few
+    tokens with BF16 columns take token-major tiles with a short activation box, and at H = 10240
+    balanced tiles of ceil(H / SMs) gate rows (N = 2 x 72 per MMA)."""
     from reax_engine_runtime_v3_b200.reaxv2.gate_up import quantize_rows
-    g = H.gen(11)
-    x = H.activations(g, 200, 2560)
-    bank = H.int8_bank(g, 2560, 1024, KH=128, centered=True, pow2_smoothing=True, bias=True)
+    g = H.gen(11 + M)
+    x = H.activations(g, M, K)
+    bank = H.int8_bank(g, K, Hh, KH=128, centered=True, pow2_smoothing=True, bias=True)
     bd = H.bank_to(bank, "cuda")
     out = run_project(x.cuda(), bd)
     low, high, scales = quantize_rows(x.cuda(), bd)
