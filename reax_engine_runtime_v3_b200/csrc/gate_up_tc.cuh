@@ -1,22 +1,26 @@
 // tcgen05 GEMM kernels of the gate/up path (sm_100a).
 //
 // One warp-specialised persistent kernel computes C = A[M, K] x B[N, K]^T tile by tile with the
-// 5th-generation tensor cores and hands each accumulator tile to an epilogue:
-//   warp 0        TMA producer: 128x128-byte boxes of A and B into a STAGES-deep smem ring (128B swizzle)
-//   warp 1        TMEM allocator + MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=32 bytes)
-//   warps 2..     epilogue: tcgen05.ld of its 32 TMEM lanes, dequant / SwiGLU / bf16 store
+// 5th-generation tensor cores and hands each accumulator tile to an epilogue.  Twelve warps:
+//   warps 0, 2, 3  TMA producers, one box each per K block (B first half / gate rows, B second half /
+//                  up rows, A / activation rows), into a smem ring of stages (128B swizzle)
+//   warp 1         TMEM allocator + MMA issuer: one thread issues tcgen05.mma (M = 128, K = 32 bytes)
+//   warps 4..11    epilogue: tcgen05.ld of its TMEM lane quarter, dequant / SwiGLU / bf16 store
+// The control warps (0-3) give registers to the epilogue warps with setmaxnreg.
 //
-// Tile = 128 rows of A (tokens) x 256 rows of B.  For the gate/up SwiGLU epilogue the 256 B rows
-// are 128 gate rows W[n0 .. n0+127] followed by the matching up rows W[H+n0 ..] (the interleave of
-// the reference's loader, hybrid8_tiles.cuh:93-94), so TMEM columns j and 128+j of one lane hold
-// the gate and up accumulators of the same output element and the SwiGLU needs no data exchange.
+// Token-major tiles: 128 rows of A (tokens) x 256 rows of B.  For the gate/up SwiGLU epilogue the B
+// rows are R gate rows W[n0 .. n0+R) followed by the matching up rows W[H+n0 ..) (the interleave of
+// the reference's loader, hybrid8_tiles.cuh:93-94; R = 128 unless the plan balances rows per tile),
+// so TMEM columns j and R8+j of one lane hold the gate and up accumulators of one output element.
+// Weight-major tiles (few tokens): the R gate rows and the R up rows are the A operands of two MMAs
+// whose B operand is the activation tile; TMEM lanes are weight rows and columns are tokens.
 //
 // Work distribution ("stream-K hybrid"): the tile list (grouped GROUP_M x n_tiles order, for L2
 // reuse) is cut into data-parallel tiles, dealt round-robin to the CTAs, and a remainder (< 2 waves)
-// whose K-blocks are split evenly between all CTAs.  A CTA that computes only part of a tile writes
+// whose K blocks are split evenly between all CTAs.  A CTA that computes only part of a tile writes
 // its int32 partial to its own workspace slot and adds its K-block count to the tile's counter; the
-// CTA that completes the count sums every partial (integer addition: exact, order-free) with its own
-// TMEM accumulator and runs the epilogue, then clears the counter.  No CTA ever waits for another.
+// CTA that completes the tile sums every partial (integer addition: exact, order-free) with its own
+// TMEM accumulator and runs the epilogue, then clears the counter.
 //
 // Every mbarrier wait is bounded (timeout_ns of global time); on expiry the kernel ORs a bit into
 // the caller's status word, raises a shared abort flag so the other roles stop, drains its own
@@ -432,7 +436,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ns; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], 3);   // one arrival per producer (gate, up, activation boxes)
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -471,47 +475,48 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         grid_dependents_launch();
         return p.slice_mode ? min(max(__ldg(p.split), 0), p.M) : 0;
     };
-    // bytes a stage receives: weight-major tiles load n_tok activation rows instead of 128
-    const uint32_t stage_tx =
-        SWAP ? static_cast<uint32_t>((2 * p.tile_rows + p.n_tok) * kRowBytes)
-             : (EPI == kEpiSwiglu ? static_cast<uint32_t>((p.a_rows + 2 * p.tile_rows) * kRowBytes)
-                                  : static_cast<uint32_t>(kStageBytes));
 
     if (warp < kCtlWarps) {
     regs_shrink<kCtlRegs>();
-    if (warp == 0) {
-        // ------------------------------------------------------------------------------ TMA producer
+    if (warp == 0 || warp >= 2) {
+        // ----------------------------------------------------------------------------- TMA producers
+        // One box per producer and K block: warp 0 the gate rows (first half of B), warp 2 the up rows
+        // (second half of B), warp 3 the activation rows (A).  Each arms the stage's full barrier with
+        // its own bytes (three arrivals per phase), so the three copies are issued in parallel.
         if (lane == 0) {
-            const uint64_t pol_a = l2_policy_evict_last();
-            const uint64_t pol_b = p.evict_first_b ? l2_policy_evict_first() : l2_policy_evict_normal();
+            const int role = warp == 0 ? 0 : warp - 1;   // 0 gate, 1 up, 2 activation
+            const uint64_t policy = role == 2 ? l2_policy_evict_last()
+                                              : (p.evict_first_b ? l2_policy_evict_first() : l2_policy_evict_normal());
+            const int b_rows = (EPI == kEpiSwiglu) ? p.tile_rows : kBN / 2;
+            const int a_rows = SWAP ? p.n_tok : p.a_rows;
+            const uint32_t box_tx = static_cast<uint32_t>((role == 2 ? a_rows : b_rows) * kRowBytes);
             int stage = 0;
             uint32_t phase = 0;
             uint32_t armed = 0;        // bit s: stage s has been armed at least once
             uint32_t armed_parity = 0; // bit s: parity of the last arming of stage s
-            // B (weight) boxes of K block kb of a tile into stage st
-            auto load_b = [&](int st, int kb, int part, int b0, int b1) {
+            // this producer's box of K block kb of the tile (part, m0, b0, b1) into stage st
+            auto load_box = [&](int st, int kb, int part, int m0, int b0, int b1) {
+                uint8_t* dst = role == 0 ? box_b(st) : (role == 1 ? box_bu(st) : box_a(st));
+                const int y = role == 0 ? b0 : (role == 1 ? b1 : m0);
                 if (kb < p.kb_int) {
                     const int x = (part * p.kb_int_part + kb) * kRowBytes;
-                    tma_load_2d(box_b(st), &p.tm_b, &full[st], x, b0, pol_b);
-                    tma_load_2d(box_bu(st), &p.tm_b, &full[st], x, b1, pol_b);
+                    tma_load_2d(dst, role == 2 ? &p.tm_a : &p.tm_b, &full[st], x, y, policy);
                 } else {
                     const int x = (part * p.kb_f16_part + kb - p.kb_int) * (kRowBytes / 2);
-                    tma_load_2d(box_b(st), &p.tm_bh, &full[st], x, b0, pol_b);
-                    tma_load_2d(box_bu(st), &p.tm_bh, &full[st], x, b1, pol_b);
+                    tma_load_2d(dst, role == 2 ? &p.tm_ah : &p.tm_bh, &full[st], x, y, policy);
                 }
             };
             auto tile_rows = [&](const Segment& sg, int& part, int& m0, int& b0, int& b1) {
                 int mt, nt;
                 tile_coords(p, sg.tile, part, mt, nt);
                 m0 = mt * kBM;
-                const int rows = p.tile_rows;   // gate rows of a SwiGLU tile
-                b0 = (EPI == kEpiSwiglu) ? nt * rows : nt * kBN;
-                b1 = (EPI == kEpiSwiglu) ? p.H + nt * rows : nt * kBN + kBN / 2;
+                b0 = (EPI == kEpiSwiglu) ? nt * p.tile_rows : nt * kBN;
+                b1 = (EPI == kEpiSwiglu) ? p.H + nt * p.tile_rows : nt * kBN + kBN / 2;
             };
-            // early_b: the weight boxes of the first segment's first ns K blocks are requested before
-            // the dependency wait (the weights are not produced by the kernel this one waits for).
+            // early_b: the weight producers request the first segment's first ns K blocks before the
+            // dependency wait (the weights are not produced by the kernel this one waits for).
             int pre = 0;
-            if (p.early_b && !p.slice_mode) {
+            if (role != 2 && p.early_b && !p.slice_mode) {
                 Cursor c0 = cursor_init(p);
                 Segment s0;
                 if (cursor_next(p, 0, c0, s0)) {
@@ -519,8 +524,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     tile_rows(s0, part, m0, b0, b1);
                     pre = min(ns, s0.k1 - s0.k0);
                     for (int i = 0; i < pre; ++i) {
-                        mbar_arrive_expect_tx(&full[i], stage_tx);
-                        load_b(i, s0.k0 + i, part, b0, b1);
+                        mbar_arrive_expect_tx(&full[i], box_tx);
+                        load_box(i, s0.k0 + i, part, m0, b0, b1);
                         armed |= 1u << i;
                     }
                 }
@@ -534,22 +539,18 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 int part, m0, b0, b1;
                 tile_rows(seg, part, m0, b0, b1);
                 for (int kb = seg.k0; kb < seg.k1; ++kb) {
-                    if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns, vabort)) {
-                        if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutEmpty);
-                        ok = false;
-                        break;
+                    // A K block requested early already owns its (then fresh) stage: it must not wait on
+                    // the stage's empty barrier, whose first phase the other producers and the MMAs may
+                    // have completed by now.
+                    if (!(first && kb - seg.k0 < pre)) {
+                        if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns, vabort)) {
+                            if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutEmpty);
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[stage], box_tx);
+                        load_box(stage, kb, part, m0, b0, b1);
                     }
-                    const bool prefetched = first && kb - seg.k0 < pre;   // armed, B boxes requested
-                    if (!prefetched) mbar_arrive_expect_tx(&full[stage], stage_tx);
-                    uint8_t* sa_ = box_a(stage);
-                    if (kb < p.kb_int) {
-                        const int x = (part * p.kb_int_part + kb) * kRowBytes;
-                        tma_load_2d(sa_, &p.tm_a, &full[stage], x, m0, pol_a);
-                    } else {
-                        const int x = (part * p.kb_f16_part + kb - p.kb_int) * (kRowBytes / 2);
-                        tma_load_2d(sa_, &p.tm_ah, &full[stage], x, m0, pol_a);
-                    }
-                    if (!prefetched) load_b(stage, kb, part, b0, b1);
                     armed |= 1u << stage;
                     armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == ns) {

@@ -132,6 +132,26 @@ def test_project_entry_matches_two_calls(M, K, Hh, KH):
     assert torch.equal(fused.view(torch.int16), two.view(torch.int16))
 
 
+@pytest.mark.parametrize("M", [1, 8])
+def test_project_entry_repeated_status_clean(M):
+    """Back-to-back project calls (the GEMM's weight producers start before its dependency wait and may
+    lag the activation producer by whole stages) stay equal to the two-call path with no expired wait."""
+    from reax_engine_runtime_v3_b200 import _native
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native, gate_up_i8, quantize_rows
+    g = H.gen(77 * M)
+    bank = H.bank_to(H.int8_bank(g, 4096, 14336), "cuda")
+    ws = _native.workspace(torch.device("cuda"))
+    _native.clear_status(ws)
+    xs = [H.activations(g, M, 4096).cuda() for _ in range(12)]
+    outs = [Native(None).project(x, bank, "hybrid8_b128n256_s64n256") for x in xs]
+    torch.cuda.synchronize()
+    assert _native.read_status(ws) == 0
+    for x, out in zip(xs, outs):
+        low, high, sc = quantize_rows(x, bank)
+        two = gate_up_i8(low, bank.low_weight, high, bank.high_weight, sc, bank.scales, bank.bias)
+        assert torch.equal(out.view(torch.int16), two.view(torch.int16))
+
+
 def test_cfg3_prefill_rows_sample():
     """BASELINE config 3 (M=4096, K=4096, H=14336): full GPU run, oracle on a sample of rows."""
     g = H.gen(3)
