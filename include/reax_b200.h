@@ -41,6 +41,7 @@ extern "C" {
 #define REAX_STATUS_TIMEOUT_ACC_EMPTY 0x8u
 #define REAX_STATUS_TIMEOUT_DRAIN 0x10u
 #define REAX_STATUS_SELFTEST 0x20u
+#define REAX_STATUS_PLAN_LIMIT 0x40u
 
 /* Library version (major * 10000 + minor * 100 + patch). */
 REAX_API int reax_version(void);

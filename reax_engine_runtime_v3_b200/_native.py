@@ -20,7 +20,8 @@ ERRORS = {1: "invalid argument", 2: "misaligned argument", 3: "CUDA failure", 4:
           5: "workspace too small"}
 STATUS_BITS = {0x1: "timeout waiting for a TMA stage", 0x2: "timeout waiting for a free stage",
                0x4: "timeout waiting for an accumulator", 0x8: "timeout waiting for a free accumulator",
-               0x10: "timeout draining in-flight work", 0x20: "self-test wait expired"}
+               0x10: "timeout draining in-flight work", 0x20: "self-test wait expired",
+               0x40: "a split tile had more contributors than the finisher gathers (plan limit)"}
 
 _P = C.c_void_p
 _I = C.c_int

@@ -4,6 +4,7 @@
 // reaxv2/gate_up.py:14 and reaxv2/sliced.py:26, plus the alignment the kernels need), TMA tensor-map
 // encoding, the tile / stream-K plan of the tcgen05 kernels, and the launches.  Nothing here
 // allocates device memory or synchronizes, so every entry point is usable inside graph capture.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -224,19 +225,14 @@ void plan_schedule(reax::TcParams& p, int sms, bool allow_split, int* grid) {
         *grid = T < sms ? T : sms;
         return;
     }
+    // Every CTA's K range covers at least two K blocks and at least ceil(KB / kMaxContrib) of them, so a
+    // split tile has at most kMaxContrib + 1 contributors (the finisher gathers kMaxContrib partials).
     long long g = sms;
-    if (p.dp_tiles == 0) {
-        // at least two K blocks per CTA
-        const long long cap = p.sk_iters / 2;
-        if (cap < g) g = cap < 1 ? 1 : cap;
-    }
+    const long long min_len = std::max<long long>(2, (KB + reax::kMaxContrib - 1) / reax::kMaxContrib);
+    if (p.sk_iters / min_len < g) g = std::max<long long>(1, p.sk_iters / min_len);
     *grid = static_cast<int>(g);
 }
 
-// Weight-major tiles: gate rows per tile.  With 128 rows there are ceil(H / 128) tiles; when they leave a
-// partial wave of at least half the SMs, an even share R = ceil(H / (waves * SMs)) <= 128 rows per tile
-// fills whole waves instead, so no tile is split by K.  The TMA box then covers R weight rows, the MMA
-// still computes 128 (rows past R are never stored), and the weight bytes read stay the same.
 // Weight-major pipeline: stages of [gate box | up box | activation box] (each 128 bytes wide, the weight
 // boxes rounded up to whole 8-row swizzle atoms), as many as fit the kStages x kStageBytes pool (at most
 // kMaxStages).  The M = 128 MMAs read 128 rows from each weight box, so the last stage's up box keeps
@@ -252,23 +248,56 @@ void set_swap_pipeline(reax::TcParams& p) {
     p.stages = stages;
 }
 
-int tile_rows_for(int H, int sms) {
+// Gate rows per few-token tile (R <= 128) and whether the plan splits tiles by K.
+// - Large H: whole tiles.  128-row tiles unless they leave a partial wave of at least half the SMs;
+//   then an even share R = ceil(H / (waves * SMs)) fills whole waves.  The TMA box covers R weight rows,
+//   the MMA still computes 128 (rows past R are never stored), and the weight bytes read stay the same.
+// - Small H (fewer than half a wave of 128-row tiles): R = ceil(H * s / SMs) rows, so about SMs / s
+//   tiles, each split by K over about s CTAs.  s in {1, 2, 4, 8} minimises the estimated launch time:
+//   a CTA spends about kKBlockNs per K block whatever its rows (measured on B200), the weights stream
+//   at about kHbmBytesPerNs, and a split adds one exchange of int32 partials (kSplitNs).
+int tile_rows_for(int H, int K_blocks, int sms, bool can_split, bool* split) {
+    *split = false;
     const int t128 = (H + 127) / 128;
-    if (t128 % sms == 0 || 2 * t128 < sms) return 128;
-    const int waves = (t128 + sms - 1) / sms;
-    return (H + waves * sms - 1) / (waves * sms);
+    if (t128 % sms == 0) return 128;
+    if (2 * t128 >= sms) {
+        const int waves = (t128 + sms - 1) / sms;
+        return (H + waves * sms - 1) / (waves * sms);
+    }
+    constexpr double kKBlockNs = 470.0, kHbmBytesPerNs = 6400.0;
+    constexpr double kSplitNs[4] = {0.0, 2500.0, 3000.0, 4000.0};
+    const double hbm_ns = 2.0 * H * K_blocks * 128.0 / kHbmBytesPerNs;
+    int best_r = 128;
+    double best = 1e30;
+    for (int i = 0, s = 1; s <= 8; ++i, s *= 2) {
+        if (s > 1 && !can_split) break;
+        const int r = (H * s + sms - 1) / sms;
+        if (r > 128) break;
+        const int tiles = (H + r - 1) / r;
+        const double per_cta = static_cast<double>(tiles) * K_blocks / std::min(sms, tiles * s);
+        const double t = std::max(per_cta * kKBlockNs, hbm_ns) + kSplitNs[i];
+        if (t < best) {
+            best = t;
+            best_r = r;
+            *split = s > 1;
+        }
+    }
+    return best_r;
 }
 
 // Tile plan of a SwiGLU gate/up launch: orientation, gate rows per tile, activation box rows.  Few
 // tokens take weight-major tiles (the weights as the MMA's A operand; measured faster on B200 than
 // token-major tiles of the same rows) unless BF16 outlier columns need token-major tiles; either way
 // with balanced gate rows and an activation box of round16(M) rows.  Returns whether the tiles are
-// weight-major.
-bool plan_gate_up_tiles(reax::TcParams& p, int M, int H, bool weight_major_ok, int sms) {
+// weight-major; *split says whether the plan may split tiles by K.
+bool plan_gate_up_tiles(reax::TcParams& p, int M, int H, int K_blocks, bool weight_major_ok, bool can_split, int sms,
+                        bool* split) {
     const bool few = M <= kSwapMaxRows;
     const bool swap = weight_major_ok && few;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
-    p.tile_rows = few ? tile_rows_for(H, sms) : 128;
+    *split = can_split;
+    p.tile_rows = 128;
+    if (few) p.tile_rows = tile_rows_for(H, K_blocks, sms, can_split, split);
     p.tile_rows8 = (p.tile_rows + 7) & ~7;
     p.a_rows = M < reax::kBM ? ((M + 15) / 16) * 16 : reax::kBM;
     if (swap) set_swap_pipeline(p);
@@ -408,7 +437,8 @@ int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const vo
     reax::TcParams p;
     init_params(p);
     // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
-    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KH == 0, info->sms);
+    bool split_ok = false;
+    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, info->sms, &split_ok);
     if (KL) {
         if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
             return rc;
@@ -448,7 +478,7 @@ int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const vo
     p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
     p.early_b = early_b;
     int grid = 0;
-    plan_schedule(p, info->sms, KH == 0 && p.tile_rows == 128, &grid);
+    plan_schedule(p, info->sms, split_ok, &grid);
     return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
 }
 
@@ -608,7 +638,8 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
     reax::TcParams p;
     init_params(p);
-    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, true, info->sms);
+    bool split_ok = false;   // BF16 tiles are never split
+    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, K / 64, true, false, info->sms, &split_ok);
     if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : p.a_rows)) != REAX_OK)
         return rc;
     if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K, p.tile_rows)) !=
@@ -803,7 +834,8 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
 
     reax::TcParams p;
     init_params(p);
-    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KH == 0, info->sms);
+    bool split_ok = false;
+    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, info->sms, &split_ok);
     if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
         return rc;
     if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, p.tile_rows)) != REAX_OK)
@@ -833,7 +865,7 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     // Whole-tile plans need no partials; a plan that splits tiles is re-planned for at most
     // kNoAllocMaxCtas CTAs, whose partials the static scratch holds.
     int grid = 0;
-    plan_schedule(p, info->sms, KH == 0 && p.tile_rows == 128, &grid);
+    plan_schedule(p, info->sms, split_ok, &grid);
     int ctas = grid;
     if (p.sk_iters > 0 && grid > kNoAllocMaxCtas) {
         plan_schedule(p, kNoAllocMaxCtas, true, &grid);

@@ -24,6 +24,7 @@ enum : uint32_t {
     kStatusTimeoutAccEmpty = 1u << 3,  // MMA issuer waited too long for a free accumulator
     kStatusTimeoutDrain = 1u << 4,     // teardown waited too long for in-flight copies / MMAs
     kStatusSelfTest = 1u << 5,         // reax_selftest_wait(): the wait on a never-arriving barrier expired
+    kStatusPlanLimit = 1u << 6,        // a split tile had more contributors than a finisher can gather
 };
 
 REAX_DEVI uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }

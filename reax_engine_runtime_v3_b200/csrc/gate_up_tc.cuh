@@ -367,9 +367,13 @@ REAX_DEVI int contributors(const TcParams& p, int st, const int4* (&contrib)[kMa
     const int c_first = sk_owner(p, static_cast<long long>(st) * KB);
     const int c_last = sk_owner(p, static_cast<long long>(st + 1) * KB - 1);
     int n = 0;
-    for (int c = c_first; c <= c_last && n < kMaxContrib; ++c) {
+    for (int c = c_first; c <= c_last; ++c) {
         if (c == static_cast<int>(blockIdx.x)) continue;
         if (sk_begin(p, c + 1) <= sk_begin(p, c)) continue;
+        if (n == kMaxContrib) {   // the host plans at most kMaxContrib others; report rather than drop one
+            atomicOr(p.status, kStatusPlanLimit);
+            break;
+        }
         contrib[n++] = reinterpret_cast<const int4*>(p.ws_partials +
                                                       (static_cast<size_t>(c) * 2 + sk_slot(p, c, st)) * kSlotInts);
     }

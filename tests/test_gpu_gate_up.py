@@ -152,6 +152,18 @@ def test_project_entry_repeated_status_clean(M):
         assert torch.equal(out.view(torch.int16), two.view(torch.int16))
 
 
+@pytest.mark.parametrize("M,Hh", [(1, 1792), (64, 1792), (8, 3584), (33, 3584), (64, 7168)])
+def test_rank_shard_shapes(M, Hh):
+    """cfg2 as one rank of an H-sharded job sees it (K = 4096; H / 2, H / 4, H / 8 of 14336): few tiles,
+    each split by K over several CTAs, with the finisher gathering their int32 partials."""
+    from reax_engine_runtime_v3_b200 import _native
+    ws = _native.workspace(torch.device("cuda"))
+    _native.clear_status(ws)
+    g = H.gen(5 * M + Hh)
+    compare_int8(H.activations(g, M, 4096), H.int8_bank(g, 4096, Hh))
+    assert _native.read_status(ws) == 0, _native.describe_status(_native.read_status(ws))
+
+
 def test_cfg3_prefill_rows_sample():
     """BASELINE config 3 (M=4096, K=4096, H=14336): full GPU run, oracle on a sample of rows."""
     g = H.gen(3)
