@@ -429,7 +429,8 @@ def main():
         achieved = by / dur / 1e9
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                     "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs"}
-    roofline["traffic"] = ncu_traffic(args.workload)
+    # the committed capture is of the one-GPU launch; a rank of a sharded job moves 1/N of its bytes
+    roofline["traffic"] = ncu_traffic(args.workload) if world == 1 else None
     roofline["per_launch_us"] = {str(M): round(d * 1e6, 2) for M, d in per_bucket}
 
     # end to end through the public API with host buffers: every step copies its inputs from pinned
