@@ -372,42 +372,46 @@ def main():
     launches = args.steps * len(buckets) * (2 if int8 else 1)
 
     # dominant kernel (the GEMM) alone: a graph of back-to-back launches over the rotating weight
-    # copies, timed with events on its stream; per launch = replay time / launches (gaps included)
+    # copies, timed with events on its stream; per launch = replay time / launches (gaps included).  The
+    # INT8 GEMM is timed as the step runs it, with its weight stream started before its dependency wait
+    # (reax_project_i8 launches it that way behind the quantizer; here through reax_gate_up_i8_static),
+    # and once more as the plain reax_gate_up_i8, which waits first (per_launch_us_plain).
     from reax_engine_runtime_v3_b200.reaxv2.gate_up import gate_up_i8, quantize_rows
-    per_bucket = []
+    per_bucket, per_bucket_plain = [], []
     reps = 3 * copies
     with torch.cuda.stream(cap):
         pre = [quantize_rows(x, banks[0]) for x in xs] if int8 else None
         for bi, x in enumerate(xs):
             M = x.shape[0]
-
-            def gemm(r):
-                b = banks[r % copies]
-                if int8:
-                    low, high, sc = pre[bi]
-                    gate_up_i8(low, b.low_weight, high, b.high_weight, sc, b.scales, b.bias)
-                else:
-                    bf16.gate_up(x, b["w"])
-            gemm(0)
-            torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=cap):
-                for r in range(reps):
-                    gemm(r)
-            for _ in range(2):
-                g.replay()
-            torch.cuda.synchronize()
-            n_rep = max(1, args.steps // reps) + 2
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(cap)
-            for _ in range(n_rep):
-                g.replay()
-            e1.record(cap)
-            torch.cuda.synchronize()
-            d = e0.elapsed_time(e1) * 1e-3 / (n_rep * reps)
-            d = max_over_ranks(d, world)
-            per_bucket.append((M, d))
-            del g
+            for static in ((True, False) if int8 else (False,)):
+                def gemm(r):
+                    b = banks[r % copies]
+                    if int8:
+                        low, high, sc = pre[bi]
+                        gate_up_i8(low, b.low_weight, high, b.high_weight, sc, b.scales, b.bias,
+                                   static_weights=static)
+                    else:
+                        bf16.gate_up(x, b["w"])
+                gemm(0)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=cap):
+                    for r in range(reps):
+                        gemm(r)
+                for _ in range(2):
+                    g.replay()
+                torch.cuda.synchronize()
+                n_rep = max(1, args.steps // reps) + 2
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(cap)
+                for _ in range(n_rep):
+                    g.replay()
+                e1.record(cap)
+                torch.cuda.synchronize()
+                d = e0.elapsed_time(e1) * 1e-3 / (n_rep * reps)
+                d = max_over_ranks(d, world)
+                (per_bucket if static or not int8 else per_bucket_plain).append((M, d))
+                del g
     peaks, peak_kind = measured_peaks()
     prefill = min(buckets) >= 512
     if prefill:
@@ -432,22 +436,53 @@ def main():
     # the committed capture is of the one-GPU launch; a rank of a sharded job moves 1/N of its bytes
     roofline["traffic"] = ncu_traffic(args.workload) if world == 1 else None
     roofline["per_launch_us"] = {str(M): round(d * 1e6, 2) for M, d in per_bucket}
+    if per_bucket_plain:
+        roofline["per_launch_us_plain"] = {str(M): round(d * 1e6, 2) for M, d in per_bucket_plain}
 
-    # end to end through the public API with host buffers: every step copies its inputs from pinned
-    # host memory, runs the path and reads every output back to pinned host memory, all inside the
-    # replayed graph
+    # end to end through the public API with host buffers: every step copies each bucket's input from
+    # pinned host memory, runs the path and reads every output back to pinned host memory, all inside the
+    # replayed graph.  The copies run on two side streams, so a bucket's read-back overlaps the compute of
+    # the buckets after it and the inputs arrive ahead of their compute.  Buckets run largest first and a
+    # bucket of 1024 rows or more runs as four row pieces (the path is per token, so the outputs are the
+    # same); what stays exposed is the first piece's input and the last piece's output.
     e2e = None
     if not args.no_e2e:
         xs_host = [x.pin_memory() for x in xs_cpu]
         outs_host = [torch.empty((x.shape[0], h), dtype=torch.bfloat16).pin_memory() for x in xs_cpu]
         xs_dev = [torch.empty_like(x, device=dev) for x in xs_cpu]
+        pieces = []  # (bucket, first row, end row) in issue order
+        for j in sorted(range(len(xs_cpu)), key=lambda j: -xs_cpu[j].shape[0]):
+            M = xs_cpu[j].shape[0]
+            rows = -(-M // (4 if M >= 1024 else 1))
+            pieces += [(j, r, min(M, r + rows)) for r in range(0, M, rows)]
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
         def e2e_step(i):
             b = banks[i % copies]
-            for xh, xd, oh in zip(xs_host, xs_dev, outs_host):
-                xd.copy_(xh, non_blocking=True)
+            main = torch.cuda.current_stream(dev)
+            s_in.wait_stream(main)
+            s_out.wait_stream(main)
+            arrived = []
+            with torch.cuda.stream(s_in):
+                for j, r0, r1 in pieces:
+                    xs_dev[j][r0:r1].copy_(xs_host[j][r0:r1], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(s_in)
+                    arrived.append(ev)
+            outs = []  # alive until the step is enqueued, so no output buffer is reused under a read-back
+            for (j, r0, r1), ev in zip(pieces, arrived):
+                main.wait_event(ev)
+                xd = xs_dev[j][r0:r1]
                 o = gate_up.project(xd, b, "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(xd, b["w"])
-                oh.copy_(o, non_blocking=True)
+                outs.append(o)
+                done = torch.cuda.Event()
+                done.record(main)
+                s_out.wait_event(done)
+                with torch.cuda.stream(s_out):
+                    outs_host[j][r0:r1].copy_(o, non_blocking=True)
+            main.wait_stream(s_in)
+            main.wait_stream(s_out)
+            return outs
         with torch.cuda.stream(cap):
             e2e_step(0)
             torch.cuda.synchronize()
@@ -459,6 +494,13 @@ def main():
                 egraphs.append(g)
             for i in range(args.warmup):
                 egraphs[i % copies].replay()
+            torch.cuda.synchronize()
+            # the read-back of the last warm-up replay must equal the device step's outputs
+            last = banks[(args.warmup - 1) % copies]
+            for j, x in enumerate(xs):
+                o = gate_up.project(x, last, "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(x, last["w"])
+                if not torch.equal(o.cpu(), outs_host[j]):
+                    raise RuntimeError(f"e2e read-back of bucket M={x.shape[0]} differs from the device step")
         barrier(world)
         with torch.cuda.stream(cap):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -471,7 +513,9 @@ def main():
         e2e = {"value": tokens / (ems * 1e-3), "unit": "tokens/s",
                "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs_cpu),
                "d2h_bytes_per_step": sum(x.shape[0] * h * 2 for x in xs_cpu),
-               "how": "public API calls captured once per weight copy into CUDA graphs, replayed per step"}
+               "how": "public API calls captured once per weight copy into CUDA graphs, replayed per step; "
+                      "H2D and D2H on side streams overlapping compute, buckets largest first, buckets of "
+                      ">= 1024 rows in four row pieces"}
         del egraphs
     del graphs
 

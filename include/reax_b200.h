@@ -109,6 +109,16 @@ REAX_API int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, c
                     const float* sw, const float* bias, void* out, int M, int N2, int KL, int KH, int ldo,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- a5-a9 for weights that the preceding kernel does not write ----------------------------------------
+ * No counterpart in the reference: reax_gate_up_i8 with the same arguments and requirements, for a
+ * caller that guarantees that the kernel launched just before this one on the stream does not write W
+ * or WH (the usual case: banks are written once and then only read).  The GEMM then requests its
+ * first weight tiles before it waits for that kernel, so the weight stream starts under the tail of
+ * the previous launch.  A, AH, sa, sw and bias are still read only after the wait. */
+REAX_API int reax_gate_up_i8_static(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa,
+                                    const float* sw, const float* bias, void* out, int M, int N2, int KL, int KH,
+                                    int ldo, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- a1 + a4-a9: quantize, then the fused INT8 gate/up --------------------------------------------
  * Replaces reaxv2.gate_up.Native.project (reaxv2/gate_up.py:29-37): reax_quant_rows on x bf16 [M, K]
  * into low int8 [M, KL], high bf16 [M, KH] and scales float32 [M], then reax_gate_up_i8 on them with W,

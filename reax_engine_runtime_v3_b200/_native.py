@@ -41,6 +41,7 @@ SIGNATURES = {
     "reax_silu_mul": ([_P, _P, _P, _I, _I, _LL, _LL, _P], _I),
     "reax_silu_table": ([_P, _P], _I),
     "reax_gate_up_i8": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
+    "reax_gate_up_i8_static": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_gate_up_i8_noalloc": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "reax_project_i8": ([_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _SZ, _P],
                         _I),

@@ -607,6 +607,12 @@ int reax_gate_up_i8(const int8_t* A, const int8_t* W, const void* AH, const void
     return gate_up_i8_launch(A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, workspace, workspace_bytes, stream, 0);
 }
 
+int reax_gate_up_i8_static(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa,
+                           const float* sw, const float* bias, void* out, int M, int N2, int KL, int KH, int ldo,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+    return gate_up_i8_launch(A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, workspace, workspace_bytes, stream, 1);
+}
+
 int reax_project_i8(const void* x, const int32_t* low_columns, const int32_t* high_columns, const float* smoothing,
                     const float* centers, int center, const int8_t* W, const void* WH, const float* sw,
                     const float* bias, int8_t* low, void* high, float* scales, void* out, int M, int K, int KL, int KH,

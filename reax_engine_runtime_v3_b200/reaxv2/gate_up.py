@@ -37,8 +37,12 @@ def _next_pow2(n: int) -> int:
     return 1 << max(0, int(n) - 1).bit_length()
 
 
-def gate_up_i8(x, w, xh, wh, sa, sw, bias, out=None):
-    """INT8 gate/up + dequant + SwiGLU on the current stream; returns bf16 [M, N2/2] (or fills ``out``)."""
+def gate_up_i8(x, w, xh, wh, sa, sw, bias, out=None, static_weights=False):
+    """INT8 gate/up + dequant + SwiGLU on the current stream; returns bf16 [M, N2/2] (or fills ``out``).
+
+    ``static_weights=True`` promises that the kernel launched just before this one on the stream does not
+    write ``w`` or ``wh``; the GEMM then starts its weight stream before waiting for that kernel
+    (``reax_gate_up_i8_static``)."""
     m, kl = x.shape
     n2 = w.shape[0]
     kh = xh.shape[1] if xh is not None else 0
@@ -52,7 +56,9 @@ def gate_up_i8(x, w, xh, wh, sa, sw, bias, out=None):
         out = torch.empty((m, n2 // 2), device=x.device, dtype=torch.bfloat16)
     with torch.cuda.device(x.device):
         ws = _native.workspace(x.device)
-        _native.check(_native.load().reax_gate_up_i8(
+        lib = _native.load()
+        entry = lib.reax_gate_up_i8_static if static_weights else lib.reax_gate_up_i8
+        _native.check(entry(
             x.data_ptr(), w.data_ptr(), _native.ptr(xh) if kh else None, _native.ptr(wh) if kh else None,
             sa.data_ptr(), sw.data_ptr(), bias.data_ptr(), out.data_ptr(), m, n2, kl, kh, out.stride(0),
             ws.data_ptr(), ws.numel(), _native.stream_handle(x.device)))

@@ -152,6 +152,29 @@ def test_project_entry_repeated_status_clean(M):
         assert torch.equal(out.view(torch.int16), two.view(torch.int16))
 
 
+@pytest.mark.parametrize("M,Hh,KH", [(1, 14336, 0), (64, 14336, 0), (33, 1792, 0), (300, 2560, 128)])
+def test_static_weights_entry_back_to_back(M, Hh, KH):
+    """reax_gate_up_i8_static launched back to back (each launch streams its weights under the previous
+    one's tail, over rotating banks) gives the bits of reax_gate_up_i8 with no expired wait."""
+    from reax_engine_runtime_v3_b200 import _native
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import gate_up_i8, quantize_rows
+    g = H.gen(53 * M + Hh + KH)
+    banks = [H.bank_to(H.int8_bank(g, 4096, Hh, KH=KH, centered=KH > 0), "cuda") for _ in range(2)]
+    x = H.activations(g, M, 4096).cuda()
+    low, high, sc = quantize_rows(x, banks[0])
+    ws = _native.workspace(torch.device("cuda"))
+    _native.clear_status(ws)
+    outs = [gate_up_i8(low, b.low_weight, high, b.high_weight, sc, b.scales, b.bias, static_weights=True)
+            for b in banks * 4]
+    torch.cuda.synchronize()
+    assert _native.read_status(ws) == 0
+    for i, b in enumerate(banks):
+        plain = gate_up_i8(low, b.low_weight, high, b.high_weight, sc, b.scales, b.bias)
+        torch.cuda.synchronize()
+        for out in outs[i::2]:
+            assert torch.equal(out.view(torch.int16), plain.view(torch.int16))
+
+
 @pytest.mark.parametrize("M,Hh", [(1, 1792), (64, 1792), (8, 3584), (33, 3584), (64, 7168)])
 def test_rank_shard_shapes(M, Hh):
     """cfg2 as one rank of an H-sharded job sees it (K = 4096; H / 2, H / 4, H / 8 of 14336): few tiles,
