@@ -407,6 +407,36 @@ REAX_DEVI uint32_t swiglu2_bits(uint32_t gw, uint32_t uw, const uint16_t* tab) {
     return bf16x2_rn(mul2_rn(s2, bf16x2_to_f2(uw)));
 }
 
+// swiglu2_bits of N pairs at once, o[i] from (gw[i], uw[i]), with one warp vote for all of them: the
+// table loads of the pairs do not wait on one another.  All 32 lanes of the warp must call it together.
+template <int N>
+REAX_DEVI void swiglu2_bits_n(const uint32_t (&gw)[N], const uint32_t (&uw)[N], uint32_t (&o)[N],
+                              const uint16_t* tab) {
+    constexpr uint32_t lo = kSiluTabElo << 7;
+    bool in = true;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        in = in && ((gw[i] & 0x7FFFu) - lo) < kSiluTabHalf && (((gw[i] >> 16) & 0x7FFFu) - lo) < kSiluTabHalf;
+    uint32_t s0[N], s1[N];   // bf16(silu) of both gates as float32 bit patterns
+    if (__all_sync(0xFFFFFFFFu, in)) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const uint32_t b0 = gw[i] & 0xFFFFu, b1 = gw[i] >> 16;
+            s0[i] = static_cast<uint32_t>(tab[(b0 & 0x7FFFu) - lo + (b0 >> 15) * kSiluTabHalf]) << 16;
+            s1[i] = static_cast<uint32_t>(tab[(b1 & 0x7FFFu) - lo + (b1 >> 15) * kSiluTabHalf]) << 16;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            s0[i] = __float_as_uint(silu_tab(__uint_as_float(gw[i] << 16), tab));
+            s1[i] = __float_as_uint(silu_tab(__uint_as_float(gw[i] & 0xFFFF0000u), tab));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        o[i] = bf16x2_rn(mul2_rn((static_cast<uint64_t>(s1[i]) << 32) | s0[i], bf16x2_to_f2(uw[i])));
+}
+
 REAX_DEVI uint32_t pack_bf16x2(__nv_bfloat16 lo, __nv_bfloat16 hi) {
     return static_cast<uint32_t>(__bfloat16_as_ushort(lo)) | (static_cast<uint32_t>(__bfloat16_as_ushort(hi)) << 16);
 }

@@ -728,29 +728,44 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 const int n_contrib = whole ? 0 : contributors(p, st, contrib);
 
                 // The segment, specialised on the pairs of token columns a warp finishes (per_warp
-                // rounded up to 8, 16 or 32): no branch separates the pairs, so their chains overlap;
+                // rounded up to 8, 16 or 32) and taken in chunks of at most 8 pairs, so that a chunk's
+                // accumulators, partials and results stay in registers.  Within a chunk no branch
+                // separates the pairs (one warp vote for the chunk's SiLU), so their chains overlap;
                 // columns past the warp's real tokens compute on padding and are never stored.
                 auto segment = [&](auto pairs_c) -> bool {
                     constexpr int PAIRS = decltype(pairs_c)::value;
-                    // this warp's gate and up accumulators of its token columns
-                    auto load_acc = [&](uint32_t (&g)[2 * PAIRS], uint32_t (&u)[2 * PAIRS]) {
-                        tmem_ld_pairs_sync<PAIRS>(t_acc + tok_lo, t_acc + n_tok + tok_lo, g, u);
+                    constexpr int CH = PAIRS < 8 ? PAIRS : 8;
+                    constexpr int NCH = PAIRS / CH;
+                    // this warp's gate and up accumulators of chunk c of its token columns
+                    auto load_acc = [&](int c, uint32_t (&g)[2 * CH], uint32_t (&u)[2 * CH]) {
+                        const int t0 = tok_lo + 2 * CH * c;
+                        tmem_ld_pairs_sync<CH>(t_acc + t0, t_acc + n_tok + t0, g, u);
                     };
-                    int4 qg[PAIRS / 2], qu[PAIRS / 2];   // the first contributor's partial of these columns
-                    auto fetch_first = [&]() {
+                    // one contributor's int32 partial of chunk c: gate and up columns, four tokens per int4
+                    auto fetch = [&](const int4* src, int c, int4 (&pg)[CH / 2], int4 (&pu)[CH / 2]) {
 #pragma unroll
-                        for (int c = 0; c < PAIRS / 2; ++c) {
-                            qg[c] = __ldcg(contrib[0] + ((tok_lo + 4 * c) / 4) * kBM + r_tile);
-                            qu[c] = __ldcg(contrib[0] + ((n_tok + tok_lo + 4 * c) / 4) * kBM + r_tile);
+                        for (int i = 0; i < CH / 2; ++i) {
+                            const int t = tok_lo + 2 * CH * c + 4 * i;
+                            pg[i] = __ldcg(src + (t / 4) * kBM + r_tile);
+                            pu[i] = __ldcg(src + ((n_tok + t) / 4) * kBM + r_tile);
                         }
                     };
+                    auto add = [&](uint32_t (&g)[2 * CH], uint32_t (&u)[2 * CH], const int4 (&pg)[CH / 2],
+                                   const int4 (&pu)[CH / 2]) {
+#pragma unroll
+                        for (int i = 0; i < CH / 2; ++i) {
+                            g[4 * i] += pg[i].x; g[4 * i + 1] += pg[i].y; g[4 * i + 2] += pg[i].z; g[4 * i + 3] += pg[i].w;
+                            u[4 * i] += pu[i].x; u[4 * i + 1] += pu[i].y; u[4 * i + 2] += pu[i].z; u[4 * i + 3] += pu[i].w;
+                        }
+                    };
+                    int4 qg[CH / 2], qu[CH / 2];   // the first contributor's partial of chunk 0
                     // The contributor holding the tile's last K blocks waits (bounded) for the others
                     // instead of publishing, and fetches the first one's partial while its own last MMAs
                     // still run.
                     bool early = false;
                     if (!whole && seg.k1 == p.kb_int + p.kb_f16) {
                         early = wait_others_counted<EPI_WARPS>(p, seg, st, last_flag, kFinisherWaitNs);
-                        if (early && n_contrib > 0) fetch_first();
+                        if (early && n_contrib > 0) fetch(contrib[0], 0, qg, qu);
                     }
                     if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
                         raise_error(p, abort_flag, kStatusTimeoutAccFull);
@@ -759,80 +774,91 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     tc_fence_after();
                     bool finish = whole || early;
                     if (!finish) {
-                        // Publish this warp's gate columns and the matching up columns (one TMEM round trip),
-                        // then count this CTA's K blocks; the contributor whose count completes the tile
-                        // finishes it.  One thread fences for the CTA after the barrier.
-                        uint32_t g[2 * PAIRS], u[2 * PAIRS];
-                        load_acc(g, u);
+                        // Publish this warp's gate columns and the matching up columns (one TMEM round trip
+                        // per chunk), then count this CTA's K blocks; the contributor whose count completes
+                        // the tile finishes it.  One thread fences for the CTA after the barrier.
                         int4* slot = reinterpret_cast<int4*>(
                             p.ws_partials + (static_cast<size_t>(blockIdx.x) * 2 + sk_slot(p, blockIdx.x, st)) * kSlotInts);
 #pragma unroll
-                        for (int c = 0; c < PAIRS / 2; ++c)
-                            if (2 * PAIRS == per_warp || 4 * c < per_warp) {
-                                __stcg(slot + ((tok_lo + 4 * c) / 4) * kBM + r_tile,
-                                       make_int4(g[4 * c], g[4 * c + 1], g[4 * c + 2], g[4 * c + 3]));
-                                __stcg(slot + ((n_tok + tok_lo + 4 * c) / 4) * kBM + r_tile,
-                                       make_int4(u[4 * c], u[4 * c + 1], u[4 * c + 2], u[4 * c + 3]));
+                        for (int c = 0; c < NCH; ++c) {
+                            uint32_t g[2 * CH], u[2 * CH];
+                            load_acc(c, g, u);
+#pragma unroll
+                            for (int i = 0; i < CH / 2; ++i) {
+                                const int tw = 2 * CH * c + 4 * i;   // token offset within the warp's columns
+                                if (tw < per_warp) {
+                                    __stcg(slot + ((tok_lo + tw) / 4) * kBM + r_tile,
+                                           make_int4(g[4 * i], g[4 * i + 1], g[4 * i + 2], g[4 * i + 3]));
+                                    __stcg(slot + ((n_tok + tok_lo + tw) / 4) * kBM + r_tile,
+                                           make_int4(u[4 * i], u[4 * i + 1], u[4 * i + 2], u[4 * i + 3]));
+                                }
                             }
+                        }
                         finish = count_published<EPI_WARPS>(p, seg, st, last_flag);
-                        if (finish && n_contrib > 0) fetch_first();
+                        if (finish && n_contrib > 0) fetch(contrib[0], 0, qg, qu);
                     }
                     if (!finish) return true;
-                    uint32_t o[PAIRS];
-                    if (n_w > 0) {
-                        uint32_t g[2 * PAIRS], u[2 * PAIRS];
-                        load_acc(g, u);
+                    const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
+                    uint16_t* ot = reinterpret_cast<uint16_t*>(out_stage);
+                    const int ph = n0 & 7;
+#pragma unroll
+                    for (int c = 0; c < NCH; ++c) {
+                        const int tc = 2 * CH * c;   // the chunk's first token within the warp's columns
+                        if (tc >= n_w) break;        // no real token left for this warp (warp-uniform)
+                        uint32_t g[2 * CH], u[2 * CH];
+                        load_acc(c, g, u);
                         if (n_contrib > 0) {
-#pragma unroll
-                            for (int c = 0; c < PAIRS / 2; ++c) {
-                                g[4 * c] += qg[c].x; g[4 * c + 1] += qg[c].y; g[4 * c + 2] += qg[c].z; g[4 * c + 3] += qg[c].w;
-                                u[4 * c] += qu[c].x; u[4 * c + 1] += qu[c].y; u[4 * c + 2] += qu[c].z; u[4 * c + 3] += qu[c].w;
+                            if (c > 0) fetch(contrib[0], c, qg, qu);
+                            add(g, u, qg, qu);
+                            for (int ci = 1; ci < n_contrib; ++ci) {
+                                int4 pg[CH / 2], pu[CH / 2];
+                                fetch(contrib[ci], c, pg, pu);
+                                add(g, u, pg, pu);
                             }
                         }
-                        for (int ci = 1; ci < n_contrib; ++ci) {
-                            int4 pg[PAIRS / 2], pu[PAIRS / 2];
+                        // dequant, bf16, then SwiGLU of every token pair of the chunk through the SiLU table
+                        uint32_t gw[CH], uw[CH], o[CH];
 #pragma unroll
-                            for (int c = 0; c < PAIRS / 2; ++c) {
-                                pg[c] = __ldcg(contrib[ci] + ((tok_lo + 4 * c) / 4) * kBM + r_tile);
-                                pu[c] = __ldcg(contrib[ci] + ((n_tok + tok_lo + 4 * c) / 4) * kBM + r_tile);
-                            }
-#pragma unroll
-                            for (int c = 0; c < PAIRS / 2; ++c) {
-                                g[4 * c] += pg[c].x; g[4 * c + 1] += pg[c].y; g[4 * c + 2] += pg[c].z; g[4 * c + 3] += pg[c].w;
-                                u[4 * c] += pu[c].x; u[4 * c + 1] += pu[c].y; u[4 * c + 2] += pu[c].z; u[4 * c + 3] += pu[c].w;
-                            }
-                        }
-                        // SwiGLU of every token pair through the SiLU table
-                        const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
-#pragma unroll
-                        for (int i = 0; i < PAIRS; ++i) {
+                        for (int i = 0; i < CH; ++i) {
                             uint64_t vg, vu;
                             if constexpr (MODE == 0) {
-                                const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sa + tok_lo + 2 * i);
+                                const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(s_sa + tok_lo + tc + 2 * i);
                                 vg = dequant2(g[2 * i], g[2 * i + 1], sa2, swg2, bg2);
                                 vu = dequant2(u[2 * i], u[2 * i + 1], sa2, swu2, bu2);
                             } else {
                                 vg = f2(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
                                 vu = f2(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
                             }
-                            o[i] = swiglu2_bits(bf16x2_rn(vg), bf16x2_rn(vu), silu_tab_s);
+                            gw[i] = bf16x2_rn(vg);
+                            uw[i] = bf16x2_rn(vu);
+                        }
+                        swiglu2_bits_n<CH>(gw, uw, o, silu_tab_s);
+                        if (p.out_vec16) {
+                            // The tile's [tokens x columns] block goes through shared memory, each token row
+                            // placed at the 16-byte phase of its destination (ph = n0 % 8 halfwords; out is
+                            // 16-byte aligned and ldo a multiple of 8), so the copy writes whole aligned
+                            // 16-byte pieces and 2-byte stores only where a piece sticks out of [n0, n_end).
+                            if (col_ok) {
+#pragma unroll
+                                for (int i = 0; i < CH; ++i)
+                                    if (tc + 2 * i < per_warp) {
+                                        const int t = tok_lo + tc + 2 * i;
+                                        ot[t * kOutStagePitch + ph + r_tile] = static_cast<uint16_t>(o[i] & 0xFFFFu);
+                                        ot[(t + 1) * kOutStagePitch + ph + r_tile] = static_cast<uint16_t>(o[i] >> 16);
+                                    }
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < CH; ++i) {
+                                const int t = tok_lo + tc + 2 * i;
+                                if (col_ok && tc + 2 * i < n_w)
+                                    p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o[i] & 0xFFFFu);
+                                if (col_ok && tc + 2 * i + 1 < n_w)
+                                    p.out[static_cast<size_t>(t + 1) * p.ldo + j] = __ushort_as_bfloat16(o[i] >> 16);
+                            }
                         }
                     }
                     if (p.out_vec16) {
-                        // The tile's [tokens x columns] block goes through shared memory, each token row placed
-                        // at the 16-byte phase of its destination (ph = n0 % 8 halfwords; out is 16-byte
-                        // aligned and ldo a multiple of 8), so the copy writes whole aligned 16-byte pieces and
-                        // 2-byte stores only where a piece sticks out of [n0, n_end).
-                        uint16_t* ot = reinterpret_cast<uint16_t*>(out_stage);
-                        const int ph = n0 & 7;
-                        if (n_w > 0 && col_ok) {
-#pragma unroll
-                            for (int i = 0; i < PAIRS; ++i)
-                                if (2 * PAIRS == per_warp || 2 * i < per_warp) {
-                                    ot[(tok_lo + 2 * i) * kOutStagePitch + ph + r_tile] = static_cast<uint16_t>(o[i] & 0xFFFFu);
-                                    ot[(tok_lo + 2 * i + 1) * kOutStagePitch + ph + r_tile] = static_cast<uint16_t>(o[i] >> 16);
-                                }
-                        }
                         named_bar_sync(1, EPI_WARPS * 32);
                         if (!whole && threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
                         // one token row per warp and iteration, one 16-byte piece per lane (at most 17 pieces)
@@ -855,21 +881,9 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             }
                         }
                         named_bar_sync(1, EPI_WARPS * 32);   // the staging block is free again
-                    } else {
-                        if (n_w > 0) {
-#pragma unroll
-                            for (int i = 0; i < PAIRS; ++i) {
-                                const int t = tok_lo + 2 * i;
-                                if (col_ok && 2 * i < n_w)
-                                    p.out[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(o[i] & 0xFFFFu);
-                                if (col_ok && 2 * i + 1 < n_w)
-                                    p.out[static_cast<size_t>(t + 1) * p.ldo + j] = __ushort_as_bfloat16(o[i] >> 16);
-                            }
-                        }
-                        if (!whole) {
-                            named_bar_sync(1, EPI_WARPS * 32);
-                            if (threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
-                        }
+                    } else if (!whole) {
+                        named_bar_sync(1, EPI_WARPS * 32);
+                        if (threadIdx.x == kCtlThreads) p.ws_counters[st] = 0;
                     }
                     return true;
                 };
@@ -945,7 +959,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         uint32_t packed[16];
                         __nv_bfloat16* dst;
                         if constexpr (EPI == kEpiSwiglu) {
-                            // bf16 gate/up values of the 16 pairs, SiLU through the table
+                            // bf16 gate/up values of the 16 pairs, then their SiLU through the table (one vote)
+                            uint32_t gw[16], uw[16];
 #pragma unroll
                             for (int i = 0; i < 32; i += 2) {
                                 uint64_t vg, vu;
@@ -964,8 +979,10 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                                     vg = f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1]));
                                     vu = f2(__uint_as_float(u[i]), __uint_as_float(u[i + 1]));
                                 }
-                                packed[i / 2] = swiglu2_bits(bf16x2_rn(vg), bf16x2_rn(vu), silu_tab_s);
+                                gw[i / 2] = bf16x2_rn(vg);
+                                uw[i / 2] = bf16x2_rn(vu);
                             }
+                            swiglu2_bits_n<16>(gw, uw, packed, silu_tab_s);
                             dst = p.out + static_cast<size_t>(grow) * p.ldo + nt * rows + cc;
                         } else {
 #pragma unroll

@@ -84,6 +84,20 @@ def test_prepare_rows_baseline_shapes(M, K, kind):
     print(f"scales bit-equal to the IEEE oracle: {exact}/{n}")
 
 
+@pytest.mark.parametrize("M,K,KH,centered", [(1, 4096, 128, True), (7, 2603, 40, True), (148, 4096, 0, False),
+                                              (3, 9000, 16, False), (2, 40000, 0, False)])
+def test_prepare_rows_few_rows_edges(M, K, KH, centered):
+    """Decode-sized row counts with production-style banks: a ragged tail (KL % 8 != 0, unaligned x),
+    centred power-of-two smoothing with BF16 high columns, and a row longer than the codes the
+    registers hold (the second pass recomputes the values past them)."""
+    gen = H.gen(300 + M + K)
+    x = H.activations(gen, M, K)
+    bank = H.int8_bank(gen, K, 128, KH=KH, centered=centered, pow2_smoothing=True)
+    low, high, scales = run_prepare(x.cuda(), H.bank_to(bank, "cuda"))
+    nb = H.bank_numpy(bank)
+    check_quant(low, high, scales, H.bits(x), nb.low_columns, nb.high_columns, nb.smoothing, nb.centers, centered)
+
+
 def test_prepare_groups_vs_reference_golden():
     G = golden()
     M, K, P, Gs, HP = (int(v) for v in G["groups_shape"])
