@@ -517,10 +517,26 @@ int reax_quant_rows(const void* x, const int32_t* low_columns, const int32_t* hi
     if (rc != REAX_OK) return rc;
     const int aligned_x = (aligned(x, 16) && K % 8 == 0) ? 1 : 0;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    return launch_dependent("quant_rows launch", reax::quant_rows_kernel<kQuantDivision>, dim3(M), dim3(reax::kQuantThreads), s,
-                        static_cast<const __nv_bfloat16*>(x), static_cast<const int*>(low_columns),
-                        static_cast<const int*>(high_columns), smoothing, centers, low,
-                        static_cast<__nv_bfloat16*>(high), scales, K, KL, KH, center ? 1 : 0, aligned_x);
+    // more rows than four per SM: narrower CTAs (wide enough to hold a row's values up to 8192 columns),
+    // more rows in flight on each SM
+    if (M > 4 * info->sms && KL <= 32 * reax::kQuantThreadsMany)
+        return launch_dependent("quant_rows launch", reax::quant_rows_kernel<kQuantDivision, reax::kQuantThreadsMany>,
+                                dim3(M), dim3(reax::kQuantThreadsMany), s, static_cast<const __nv_bfloat16*>(x),
+                                static_cast<const int*>(low_columns), static_cast<const int*>(high_columns), smoothing,
+                                centers, low, static_cast<__nv_bfloat16*>(high), scales, K, KL, KH, center ? 1 : 0,
+                                aligned_x);
+    if (M > 4 * info->sms && KL <= 64 * reax::kQuantThreadsMany)
+        return launch_dependent("quant_rows launch",
+                                reax::quant_rows_kernel<kQuantDivision, 2 * reax::kQuantThreadsMany>, dim3(M),
+                                dim3(2 * reax::kQuantThreadsMany), s, static_cast<const __nv_bfloat16*>(x),
+                                static_cast<const int*>(low_columns), static_cast<const int*>(high_columns), smoothing,
+                                centers, low, static_cast<__nv_bfloat16*>(high), scales, K, KL, KH, center ? 1 : 0,
+                                aligned_x);
+    return launch_dependent("quant_rows launch", reax::quant_rows_kernel<kQuantDivision, reax::kQuantThreads>, dim3(M),
+                            dim3(reax::kQuantThreads), s, static_cast<const __nv_bfloat16*>(x),
+                            static_cast<const int*>(low_columns), static_cast<const int*>(high_columns), smoothing,
+                            centers, low, static_cast<__nv_bfloat16*>(high), scales, K, KL, KH, center ? 1 : 0,
+                            aligned_x);
 }
 
 int reax_quant_groups(const void* x, const int32_t* low_columns, const int32_t* high_columns, const float* centers,

@@ -72,11 +72,13 @@ REAX_DEVI void load8_columns(const __nv_bfloat16* xr, const int* src, int c0, bo
 // ------------------------------------------------------------------------------ a1: per-token quantization
 // One CTA per row (reaxv2/quantize.py:5-29).  Pass 1: v = (x - centre) / smoothing, absmax over the
 // row; scale = max(absmax, 1e-12) / 127.  Pass 2 stores nearbyint(div_rn(v, scale)) clamped to
-// [-127, 127].  The first kQuantHeld chunks of 8 columns of each thread (rows up to 16384 columns with
-// kQuantThreads threads) keep v in registers between the passes; columns past them are recomputed from
-// a re-read of the row (same float ops, same result).
+// [-127, 127].  The first kQuantHeld chunks of 8 columns of each thread (rows up to 32 x THREADS
+// columns) keep v in registers between the passes; columns past them are recomputed from a re-read of
+// the row (same float ops, same result).  Few rows take kQuantThreads threads per row, so that each
+// row's work is spread wide; many rows take kQuantThreadsMany, so that more rows are in flight per SM.
 constexpr int kQuantHeld = 4;
 constexpr int kQuantThreads = 512;
+constexpr int kQuantThreadsMany = 128;
 
 // v for 8 consecutive low columns starting at c0.
 template <int DIV>
@@ -168,8 +170,8 @@ REAX_DEVI void quant_row(const __nv_bfloat16* xr, const int* low_columns, const 
     }
 }
 
-template <int DIV>
-__global__ void __launch_bounds__(kQuantThreads) quant_rows_kernel(const __nv_bfloat16* __restrict__ x,
+template <int DIV, int THREADS>
+__global__ void __launch_bounds__(THREADS) quant_rows_kernel(const __nv_bfloat16* __restrict__ x,
                                                          const int* __restrict__ low_columns,
                                                          const int* __restrict__ high_columns,
                                                          const float* __restrict__ smoothing,

@@ -98,6 +98,18 @@ def test_prepare_rows_few_rows_edges(M, K, KH, centered):
     check_quant(low, high, scales, H.bits(x), nb.low_columns, nb.high_columns, nb.smoothing, nb.centers, centered)
 
 
+@pytest.mark.parametrize("M,K,KH,centered", [(1000, 4096, 128, True), (700, 6003, 16, True), (600, 9000, 0, False)])
+def test_prepare_rows_many_rows(M, K, KH, centered):
+    """Prefill-sized row counts take narrower CTAs (128 threads up to 4096 low columns, 256 up to 8192,
+    512 past that), with BF16 high columns, a ragged tail and centring."""
+    gen = H.gen(500 + M + K)
+    x = H.activations(gen, M, K)
+    bank = H.int8_bank(gen, K, 128, KH=KH, centered=centered, pow2_smoothing=True)
+    low, high, scales = run_prepare(x.cuda(), H.bank_to(bank, "cuda"))
+    nb = H.bank_numpy(bank)
+    check_quant(low, high, scales, H.bits(x), nb.low_columns, nb.high_columns, nb.smoothing, nb.centers, centered)
+
+
 def test_prepare_groups_vs_reference_golden():
     G = golden()
     M, K, P, Gs, HP = (int(v) for v in G["groups_shape"])
