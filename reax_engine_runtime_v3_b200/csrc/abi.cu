@@ -254,9 +254,11 @@ void set_swap_pipeline(reax::TcParams& p) {
 //   the MMA still computes 128 (rows past R are never stored), and the weight bytes read stay the same.
 // - Small H (fewer than half a wave of 128-row tiles): R = ceil(H * s / SMs) rows, so about SMs / s
 //   tiles, each split by K over about s CTAs.  s in {1, 2, 4, 8} minimises the estimated launch time:
-//   a CTA spends about kKBlockNs per K block whatever its rows (measured on B200), the weights stream
-//   at about kHbmBytesPerNs, and a split adds one exchange of int32 partials (kSplitNs).
-int tile_rows_for(int H, int K_blocks, int sms, bool can_split, bool* split) {
+//   a CTA spends about kKBlockNs per K block whatever its rows, the weights stream at about
+//   kHbmBytesPerNs, and a split adds the exchange of int32 partials, kSplitNs[s] + kSplitTokNs[s] per
+//   token column of the tile (the finisher gathers s - 1 partials of 2 x 128 x n_tok words).  The
+//   constants are fitted to launches timed on B200 at K = 4096, H = 1792 and 3584, n_tok = 16 .. 64.
+int tile_rows_for(int H, int K_blocks, int n_tok, int sms, bool can_split, bool* split) {
     *split = false;
     const int t128 = (H + 127) / 128;
     if (t128 % sms == 0) return 128;
@@ -265,7 +267,8 @@ int tile_rows_for(int H, int K_blocks, int sms, bool can_split, bool* split) {
         return (H + waves * sms - 1) / (waves * sms);
     }
     constexpr double kKBlockNs = 470.0, kHbmBytesPerNs = 6400.0;
-    constexpr double kSplitNs[4] = {0.0, 2500.0, 3000.0, 4000.0};
+    constexpr double kSplitNs[4] = {0.0, 2860.0, 2930.0, 5920.0};
+    constexpr double kSplitTokNs[4] = {0.0, 40.0, 57.0, 136.0};
     const double hbm_ns = 2.0 * H * K_blocks * 128.0 / kHbmBytesPerNs;
     int best_r = 128;
     double best = 1e30;
@@ -275,7 +278,7 @@ int tile_rows_for(int H, int K_blocks, int sms, bool can_split, bool* split) {
         if (r > 128) break;
         const int tiles = (H + r - 1) / r;
         const double per_cta = static_cast<double>(tiles) * K_blocks / std::min(sms, tiles * s);
-        const double t = std::max(per_cta * kKBlockNs, hbm_ns) + kSplitNs[i];
+        const double t = std::max(per_cta * kKBlockNs, hbm_ns) + kSplitNs[i] + kSplitTokNs[i] * n_tok;
         if (t < best) {
             best = t;
             best_r = r;
@@ -297,7 +300,7 @@ bool plan_gate_up_tiles(reax::TcParams& p, int M, int H, int K_blocks, bool weig
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
     *split = can_split;
     p.tile_rows = 128;
-    if (few) p.tile_rows = tile_rows_for(H, K_blocks, sms, can_split, split);
+    if (few) p.tile_rows = tile_rows_for(H, K_blocks, ((M + 15) / 16) * 16, sms, can_split, split);
     p.tile_rows8 = (p.tile_rows + 7) & ~7;
     p.a_rows = M < reax::kBM ? ((M + 15) / 16) * 16 : reax::kBM;
     if (swap) set_swap_pipeline(p);

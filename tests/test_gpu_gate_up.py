@@ -96,11 +96,13 @@ def test_split_and_wave_shapes(M, K, Hh):
     compare_int8(H.activations(g, M, K), H.int8_bank(g, K, Hh))
 
 
-@pytest.mark.parametrize("M,K,Hh", [(5, 512, 4096), (33, 512, 10240), (64, 512, 28672), (17, 256, 18944)])
+@pytest.mark.parametrize("M,K,Hh", [(5, 512, 4096), (33, 512, 10240), (64, 512, 28672), (17, 256, 18944),
+                                    (8, 16384, 1792)])
 def test_weight_major_plans(M, K, Hh):
-    """Few tokens (weight-major tiles): 128-row tiles split by K (H = 4096), balanced tiles of
-    ceil(H / SMs) rows with a short last tile and 24 tokens per warp (H = 10240, M = 33), balanced tiles
-    over two waves (H = 28672), and 128-row tiles filling exactly one wave of 148 SMs (H = 18944)."""
+    """Few tokens (weight-major tiles): short tiles of ceil(H / SMs) rows (H = 4096, K = 512), balanced
+    tiles of ceil(H / SMs) rows with a short last tile and 24 tokens per warp (H = 10240, M = 33),
+    balanced tiles over two waves (H = 28672), 128-row tiles filling exactly one wave of 148 SMs
+    (H = 18944), and a long K on a small H, whose tiles are split over 8 CTAs (7 partials gathered)."""
     g = H.gen(7 * M + K + Hh)
     compare_int8(H.activations(g, M, K), H.int8_bank(g, K, Hh))
 
