@@ -74,6 +74,19 @@ REAX_API int reax_quant_groups(const void* x, const int32_t* low_columns, const 
                       const float* centers, const float* smoothing, int8_t* low, void* high, float* scales,
                       int M, int K, int G, int HP, int P, void* stream);
 
+/* ---- rotated quantizer of the INT8 down projection -------------------------------------------------
+ * Replaces reaxv2.rotation.Native.prepare (reaxv2/rotation.py:14-30), which launches
+ * rotation_g{G}_b{B}_t{T} (kernel-source/legacy-v2/src/block_rotation.cu:5-65) with grid (M, parts).
+ * For row r and part p, value o < group is x[r, p*chunk + o] - centers[p*chunk + o] when o < chunk and
+ * the column is below K (0 otherwise), negated when bit 16 of column * 1103515245 + 12345 (uint32) is
+ * set; Walsh-Hadamard butterflies (lo, hi) -> (lo + hi, lo - hi) on aligned blocks of `block` values,
+ * index bit 0 first; scale = max(1e-12, absmax) * fl(1/127); codes float2int_rn(div_rn(v, scale)).
+ * x bf16 [M, K], centers float32 [K] -> low int8 [M, parts*group], scales float32 [parts, M].
+ * Requires block a power of two (>= 2) dividing group, group % 32 == 0, chunk <= group, and
+ * group / min(256, largest power of two dividing group) <= 24 (every reference rotation_* shape). */
+REAX_API int reax_quant_rotated(const void* x, const float* centers, int8_t* low, float* scales, int M, int K,
+                                int chunk, int parts, int group, int block, void* stream);
+
 /* ---- a3: ordered fp32 sum of bf16 partials -----------------------------------------------------
  * Replaces reaxv2.quantize.reduce_kernel (reaxv2/quantize.py:55-61, launched at reaxv2/sliced.py:45-46).
  * partials bf16 [P, total] -> out bf16 [total]. */

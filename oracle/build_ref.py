@@ -1,6 +1,7 @@
 """Compile the reference's own gate/up CUDA kernels from their sources into ``oracle/_ref/`` (checker only).
 
-The reference ships CUDA sources for its INT8 gate/up and grouped-projection kernels; they are
+The reference ships CUDA sources for its INT8 gate/up, grouped-projection and rotated-quantizer
+kernels; they are
 self-contained (one .cu + one .cuh each, no external libraries), so they build directly with nvcc.  The
 flags are the reference's own (``-O3 --cubin``, kernel-source/legacy-v2/manifest.json) with the
 architecture changed from sm_120a to sm_100a.  Outputs go to ``oracle/_ref/`` only (git-ignored); the
@@ -19,6 +20,7 @@ OUT = HERE / "_ref"
 SOURCES = {
     "native_hybrid8.cubin": "kernel-source/legacy-v2/src/native_hybrid8.cu",
     "sliced_linear8.cubin": "kernel-source/legacy-v2/src/sliced_linear8.cu",
+    "block_rotation.cubin": "kernel-source/legacy-v2/src/block_rotation.cu",
 }
 
 

@@ -300,6 +300,67 @@ def sliced_project(x_bits, bank):
     return reduce_partials(partials)
 
 
+# ---------------------------------------------------------------------- (f) rotated quantizer of the down projection
+
+
+def rotation_negated(columns: np.ndarray) -> np.ndarray:
+    """Columns whose value the rotation negates: bit 16 of ``column * 1103515245 + 12345`` in uint32
+    arithmetic (kernel-source/legacy-v2/src/block_rotation.cu:17-18)."""
+    h = (np.asarray(columns, dtype=np.uint64) * np.uint64(1103515245) + np.uint64(12345)) & np.uint64(0xFFFFFFFF)
+    return (h & np.uint64(65536)) != 0
+
+
+def prepare_rotated(x_bits, centers, chunk, parts, group, block):
+    """Restates ``prepare_row<G,T,B>`` (kernel-source/legacy-v2/src/block_rotation.cu:5-65), launched by
+    ``reaxv2.rotation.Native.prepare`` (reaxv2/rotation.py:14-30) with grid (M, parts).
+
+    For row r and part p, value o in [0, group) is ``x[r, c] - centers[c]`` at column c = p*chunk + o when
+    o < chunk and c < K, else 0 (:13-16); it is negated when the column's hash bit is set, even when it is
+    a zero pad (:17-18).  Walsh-Hadamard butterflies (lo, hi) -> (lo + hi, lo - hi) then run on aligned
+    blocks of ``block`` values, index bit 0 first (:20-45); the scale is ``max(1e-12, absmax) * fl(1/127)``
+    (:46-58) and the codes ``float2int_rn(div_rn(v, scale))`` without a clamp (:60-62).
+    Returns (low int8 [M, parts*group], scales float32 [parts, M]).
+    """
+    x = bf16_to_f32(x_bits)
+    M, K = x.shape
+    centers = np.asarray(centers, dtype=F32)
+    low = np.zeros((M, parts * group), dtype=np.int8)
+    scales = np.zeros((parts, M), dtype=F32)
+    o = np.arange(group)
+    for part in range(parts):
+        col = part * chunk + o
+        valid = (o < chunk) & (col < K)
+        v = np.zeros((M, group), dtype=F32)
+        v[:, valid] = (x[:, col[valid]] - centers[col[valid]][None, :]).astype(F32)
+        v = np.where(rotation_negated(col)[None, :], -v, v).astype(F32)
+        d = 1
+        while d < block:
+            lo = o[(o & d) == 0]
+            a, b = v[:, lo].copy(), v[:, lo + d].copy()
+            v[:, lo] = (a + b).astype(F32)
+            v[:, lo + d] = (a - b).astype(F32)
+            d *= 2
+        amax = np.fmax.reduce(np.abs(v), axis=1, initial=F32(0.0)).astype(F32)
+        scale = (np.fmax(amax, F32(1.0e-12)) * (F32(1.0) / F32(127.0))).astype(F32)
+        q = np.rint((v / scale[:, None]).astype(F32))
+        q = np.nan_to_num(q, nan=0.0)
+        low[:, part * group:(part + 1) * group] = q.astype(np.int32).astype(np.int8)
+        scales[part] = scale
+    return low, scales
+
+
+def rotated_project(x_bits, bank):
+    """Restates ``reaxv2.rotation.Native.project`` (reaxv2/rotation.py:12-13 -> reaxv2/sliced.py:20-47):
+    the rotated quantizer, the grouped INT8 partials (no BF16 columns) and the ordered fold."""
+    low, scales = prepare_rotated(x_bits, bank.centers, bank.chunk, bank.parts, bank.group, bank.block)
+    partials = sliced_partials(low, bank.low_weight, np.zeros((low.shape[0], 0), np.uint16),
+                               np.zeros((bank.low_weight.shape[0], 0), np.uint16), scales, bank.scales, bank.bias,
+                               bank.group, 0, bank.parts)
+    if bank.parts == 1:
+        return partials[0]
+    return reduce_partials(partials)
+
+
 # ------------------------------------------------------------------------------------------- a12: BF16 mixed-origin path
 
 

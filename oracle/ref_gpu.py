@@ -10,6 +10,8 @@ reference's launch contract:
 * ``slice_*`` (reaxv2/sliced.py:20-47): parameters (A, W, AH, WH, sa, sw, bias, partials, M, N, KL, KH,
   group, hp, mb), grid (blocks, 1, P), dynamic shared memory read from the ``<name>_required_smem``
   device global of the module.
+* ``rotation_g{G}_b{B}_t{T}`` (reaxv2/rotation.py:14-30): parameters (x, centers, low, scales, M, K,
+  chunk, parts), grid (M, parts, 1), T threads, 4 * G bytes of dynamic shared memory.
 """
 from __future__ import annotations
 
@@ -122,3 +124,19 @@ class Sliced8(Module):
                     [t.data_ptr() for t in (low, w, high, wh, scales, sw, bias, out)],
                     [m, n, parts * group, parts * hp, group, hp, mb])
         return out
+
+
+class Rotation(Module):
+    """The reference's rotated quantizer (kernel-source/legacy-v2/src/block_rotation.cu)."""
+
+    def __init__(self):
+        super().__init__("block_rotation.cubin")
+
+    def prepare(self, x, centers, chunk, parts, group, block, threads):
+        m, k = x.shape
+        fn, _ = self.function(f"rotation_g{group}_b{block}_t{threads}", 4 * group)
+        low = torch.empty((m, parts * group), device=x.device, dtype=torch.int8)
+        scales = torch.empty((parts, m), device=x.device, dtype=torch.float32)
+        self.launch(fn, (m, parts, 1), threads, 4 * group, [t.data_ptr() for t in (x, centers, low, scales)],
+                    [m, k, chunk, parts])
+        return low, scales

@@ -35,6 +35,7 @@ SIGNATURES = {
     "reax_workspace_bytes": ([_I], _SZ),
     "reax_set_wait_timeout_ns": ([_ULL], None),
     "reax_quant_rows": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
+    "reax_quant_rotated": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
     "reax_quant_groups": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "reax_reduce_partials": ([_P, _P, _LL, _I, _P], _I),
     "reax_fold_partials": ([_P, _P, _P, _I, _I, _I, _I, _P], _I),

@@ -542,6 +542,41 @@ int reax_quant_rows(const void* x, const int32_t* low_columns, const int32_t* hi
                             aligned_x);
 }
 
+int reax_quant_rotated(const void* x, const float* centers, int8_t* low, float* scales, int M, int K, int chunk,
+                       int parts, int group, int block, void* stream) {
+    if (M < 0 || K <= 0 || chunk <= 0 || parts < 1 || group <= 0 || block < 2)
+        return fail(REAX_ERR_INVALID, "quant_rotated: bad sizes M=%d K=%d chunk=%d parts=%d group=%d block=%d", M, K,
+                    chunk, parts, group, block);
+    if ((block & (block - 1)) != 0 || group % block != 0 || group % 32 != 0 || chunk > group)
+        return fail(REAX_ERR_INVALID,
+                    "quant_rotated: needs block a power of two dividing group, group %% 32 == 0 and chunk <= group "
+                    "(group=%d block=%d chunk=%d)", group, block, chunk);
+    const int threads = std::min(reax::kRotMaxThreads, group & -group);
+    if (group / threads > reax::kRotMaxV)
+        return fail(REAX_ERR_INVALID, "quant_rotated: group %d needs %d values per thread (at most %d)", group,
+                    group / threads, reax::kRotMaxV);
+    if (M == 0) return REAX_OK;
+    if (!x || !centers || !low || !scales) return fail(REAX_ERR_INVALID, "quant_rotated: NULL pointer argument");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(M, parts, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(group + 32) * sizeof(float);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, reax::quant_rotated_kernel, static_cast<const __nv_bfloat16*>(x), centers,
+                                       low, scales, M, K, chunk, parts, group, block);
+    if (e != cudaSuccess) return cuda_fail(e, "quant_rotated launch");
+    return REAX_OK;
+}
+
 int reax_quant_groups(const void* x, const int32_t* low_columns, const int32_t* high_columns, const float* centers,
                       const float* smoothing, int8_t* low, void* high, float* scales, int M, int K, int G, int HP,
                       int P, void* stream) {

@@ -237,6 +237,84 @@ __global__ void __launch_bounds__(256) quant_groups_kernel(const __nv_bfloat16* 
     }
 }
 
+// -------------------------------------------------------------- rotated quantizer of the down projection
+// One CTA of T threads per (row, part) (block_rotation.cu:5-65, launched by reaxv2/rotation.py:14-30).
+// Thread t holds values o = t + j * T, j < V = group / T: the part's centred input columns, negated by
+// the column's hash bit, zero past the part's chunk or past K.  Walsh-Hadamard butterflies
+// (lo, hi) -> (lo + hi, lo - hi) run on aligned blocks of `block` values, index bit 0 first: bits 0-4 are
+// lane bits (warp shuffles), the higher bits go through shared memory one stage per barrier.  Every
+// value goes through the same additions in the same order as the reference's thread layout gives it,
+// so the transform, the scale max(1e-12, absmax) * fl(1/127) and the codes float2int_rn(div_rn(v, scale))
+// (no clamp) are bit-identical.
+constexpr int kRotMaxV = 24;         // values per thread
+constexpr int kRotMaxThreads = 256;  // the largest power of two dividing the group, at most this
+
+__global__ void __launch_bounds__(kRotMaxThreads) quant_rotated_kernel(
+    const __nv_bfloat16* __restrict__ x, const float* __restrict__ centers, int8_t* __restrict__ low,
+    float* __restrict__ scales, int M, int K, int chunk, int parts, int group, int block) {
+    extern __shared__ float rot_s[];   // group floats, then 32 for the maximum
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const int T = blockDim.x, V = group / T;
+    const int t = threadIdx.x, lane = t & 31;
+    const int row = blockIdx.x, part = blockIdx.y;
+    const __nv_bfloat16* xr = x + static_cast<size_t>(row) * K;
+    float v[kRotMaxV];
+#pragma unroll
+    for (int j = 0; j < kRotMaxV; ++j) {
+        v[j] = 0.f;
+        if (j < V) {
+            const int o = t + j * T, c = part * chunk + o;
+            float a = 0.f;
+            if (o < chunk && c < K) a = __fsub_rn(__bfloat162float(xr[c]), __ldg(centers + c));
+            const uint32_t h = static_cast<uint32_t>(c) * 1103515245u + 12345u;
+            v[j] = (h & 65536u) ? -a : a;
+        }
+    }
+    // index bits 0-4: lanes
+#pragma unroll
+    for (int d = 1; d < 32; d *= 2) {
+        if (d >= block) break;
+#pragma unroll
+        for (int j = 0; j < kRotMaxV; ++j) {
+            if (j >= V) break;   // the same for the whole CTA
+            const float partner = __shfl_xor_sync(0xffffffffu, v[j], d);
+            v[j] = (lane & d) ? __fsub_rn(partner, v[j]) : __fadd_rn(v[j], partner);
+        }
+    }
+    // index bits 5 .. log2(block) - 1: pairs through shared memory
+    if (block > 32) {
+#pragma unroll
+        for (int j = 0; j < kRotMaxV; ++j)
+            if (j < V) rot_s[t + j * T] = v[j];
+        for (int d = 32; d < block; d *= 2) {
+            __syncthreads();
+            for (int q = t; q < group / 2; q += T) {
+                const int lo = ((q & ~(d - 1)) << 1) | (q & (d - 1));
+                const float a = rot_s[lo], b = rot_s[lo + d];
+                rot_s[lo] = __fadd_rn(a, b);
+                rot_s[lo + d] = __fsub_rn(a, b);
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kRotMaxV; ++j)
+            if (j < V) v[j] = rot_s[t + j * T];
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < kRotMaxV; ++j)
+        if (j < V) m = fmaxf(m, fabsf(v[j]));
+    float* red = rot_s + group;
+    m = group_max_nonneg(m, red, t, T, [] { __syncthreads(); });
+    const float scale = __fmul_rn(fmaxf(m, 1.0e-12f), 1.0f / 127.0f);
+    if (t == 0) scales[static_cast<size_t>(part) * M + row] = scale;
+    int8_t* lr = low + static_cast<size_t>(row) * parts * group + static_cast<size_t>(part) * group;
+#pragma unroll
+    for (int j = 0; j < kRotMaxV; ++j)
+        if (j < V) lr[t + j * T] = static_cast<int8_t>(__float2int_rn(__fdiv_rn(v[j], scale)));
+}
+
 // ------------------------------------------------------------------ a3 / a12: ordered partial reductions
 // out[i] = bf16(((float(p0[i]) + float(p1[i])) + ...) over `count(row)` partials, float32 adds in
 // partial order (reaxv2/quantize.py:55-61; runtime/mixed_origin_bf16.py:8-17).  With `split` null

@@ -1,0 +1,95 @@
+"""GPU parity of the rotated INT8 down projection (reaxv2/rotation.py) against the CPU oracle and the
+reference's own rotation_* kernels, compiled from source for sm_100a (oracle/_ref/block_rotation.cubin).
+
+The rotated quantizer's codes and scales are bit-identical: the butterflies add and subtract float32
+values in the reference's stage order (index bit 0 first), the scale is a float32 multiply by
+fl(1/127) and the codes an IEEE division rounded to nearest even.  The projection (rotated quantizer,
+grouped INT8 partials, ordered fold) is then bit-identical as well.
+"""
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import ref_gpu
+from oracle import reax_oracle as ro
+from tests import helpers as H
+
+pytestmark = pytest.mark.gpu
+
+# (M, K, chunk, parts, group, block): the down projection's input width K = 9216 in three group
+# shapes, the GDN output projection's K = 4096 with a group padded past its chunk and past K, a
+# 1408-column group, a K that ends inside the last part, and a block narrower than a warp.
+CASES = [(1, 9216, 3072, 3, 3072, 1024), (7, 9216, 2304, 4, 2304, 256), (64, 9216, 1024, 9, 1024, 64),
+         (5, 4096, 1280, 4, 1344, 64), (3, 4096, 1408, 3, 1408, 128), (16, 1000, 512, 2, 512, 512),
+         (33, 2560, 512, 5, 512, 8)]
+
+
+def inputs(M, K, seed):
+    g = H.gen(seed)
+    x = H.activations(g, M, K)
+    centers = (torch.randn(K, generator=g) * 0.05).float()
+    return x, centers
+
+
+@pytest.mark.parametrize("M,K,chunk,parts,group,block", CASES)
+def test_rotated_quantizer_vs_oracle(M, K, chunk, parts, group, block):
+    from reax_engine_runtime_v3_b200.reaxv2.rotation import quantize_rotated
+    x, centers = inputs(M, K, M + K + group + block)
+    low, scales = quantize_rotated(x.cuda(), centers.cuda(), chunk, parts, group, block)
+    torch.cuda.synchronize()
+    lo, sc = ro.prepare_rotated(H.bits(x), centers.numpy(), chunk, parts, group, block)
+    assert np.array_equal(scales.cpu().numpy().view(np.int32), sc.view(np.int32))
+    assert np.array_equal(low.cpu().numpy(), lo)
+
+
+@pytest.mark.skipif(not ref_gpu.available("block_rotation.cubin"), reason="reference rotation kernel not built")
+@pytest.mark.parametrize("M,K,chunk,parts,group,block,threads", [
+    (1, 9216, 3072, 3, 3072, 1024, 256), (7, 9216, 2304, 4, 2304, 256, 64), (64, 9216, 1024, 9, 1024, 64, 64),
+    (5, 4096, 1280, 4, 1344, 64, 64), (3, 4096, 1408, 3, 1408, 128, 128), (16, 1000, 512, 2, 512, 512, 128)])
+def test_rotated_quantizer_bit_identical_to_reference_kernel(M, K, chunk, parts, group, block, threads):
+    from reax_engine_runtime_v3_b200.reaxv2.rotation import quantize_rotated
+    x, centers = inputs(M, K, 7 * M + K + group)
+    xd, cd = x.cuda(), centers.cuda()
+    low, scales = quantize_rotated(xd, cd, chunk, parts, group, block)
+    ref_low, ref_scales = ref_gpu.Rotation().prepare(xd, cd, chunk, parts, group, block, threads)
+    torch.cuda.synchronize()
+    assert torch.equal(scales.view(torch.int32), ref_scales.view(torch.int32))
+    assert torch.equal(low, ref_low)
+
+
+def rotated_bank(g, K, parts, group, block, N):
+    return SimpleNamespace(
+        width=K, parts=parts, group=group, block=block, chunk=-(-K // parts), hp=0,
+        centers=(torch.randn(K, generator=g) * 0.05).float(),
+        low_weight=torch.randint(-127, 128, (N, parts * group), generator=g, dtype=torch.int32).to(torch.int8),
+        high_weight=torch.zeros(N, 0, dtype=torch.bfloat16),
+        scales=(1e-3 + 9e-3 * torch.rand(parts, N, generator=g)).float(),
+        bias=(torch.randn(parts, N, generator=g) * 0.05).float())
+
+
+@pytest.mark.parametrize("M,K,parts,group,block,N", [(1, 9216, 3, 3072, 1024, 2560), (64, 9216, 4, 2304, 256, 2560),
+                                                     (17, 4096, 4, 1024, 64, 2560), (8, 4096, 3, 1408, 128, 512)])
+def test_rotated_projection(M, K, parts, group, block, N):
+    """The down projection as the runtime calls it (assets.py:82 -> rotation.Native.project), against
+    the oracle's composition and against the reference's kernels composed the same way."""
+    from reax_engine_runtime_v3_b200.reaxv2.rotation import Native as Rotation
+    from reax_engine_runtime_v3_b200.reaxv2.sliced import Native as Sliced
+    g = H.gen(M + K + group + N)
+    x = H.activations(g, M, K)
+    bank = rotated_bank(g, K, parts, group, block, N)
+    bd = H.bank_to(bank, "cuda")
+    native = Rotation(Sliced(None), None, 128)
+    ours = native.project(x.cuda(), bd, "slice_m128n256")
+    torch.cuda.synchronize()
+    want = ro.rotated_project(H.bits(x), H.bank_numpy(bank))
+    assert np.array_equal(H.bits(ours), want)
+    if ref_gpu.available("block_rotation.cubin") and ref_gpu.available("sliced_linear8.cubin"):
+        threads = 64   # a thread count every reference rotation_* group shape has
+        low, scales = ref_gpu.Rotation().prepare(x.cuda(), bd.centers, bank.chunk, parts, group, block, threads)
+        empty_a = torch.zeros(M, 0, dtype=torch.bfloat16, device="cuda")
+        partials = ref_gpu.Sliced8().partials(low, bd.low_weight, empty_a, bd.high_weight, scales, bd.scales,
+                                              bd.bias, group, 0, parts)
+        torch.cuda.synchronize()
+        assert np.array_equal(H.bits(ours), ro.reduce_partials(H.bits(partials)))
