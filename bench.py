@@ -50,6 +50,11 @@ WORKLOADS = {
               "config 5b: Student-t X, buckets M={128,512,2048}, BF16 Wg/Wu ~ N(0,0.02) [14336, 4096]"),
 }
 DEFAULT_WORKLOAD = "cfg2"
+# The rotated INT8 down projection that consumes the gate/up output (reaxv2/assets.py:65-82 ->
+# reaxv2/rotation.py): decode buckets, input width K = 9216, N = 2560 output columns, 4 rotated groups of
+# 2304 columns, Walsh-Hadamard blocks of 256 (a reference rotation_g2304_b256 shape).
+DOWN = dict(buckets=(1, 8, 32, 64), K=9216, N=2560, group=2304, parts=4, block=256)
+DOWN_METRIC = "rotated INT8 down projection tokens/s"
 
 
 def parse():
@@ -58,7 +63,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["down"], default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--measure-int8-peak", action="store_true", help="print torch._int_mm int8 throughput and exit")
@@ -262,6 +267,8 @@ def cpu_run(name: str, budget_s: float = 12.0):
 def run_reference(args, world, rank):
     if rank != 0:
         return 0
+    if args.workload == "down":
+        return run_down_reference(args)
     buckets, K, H, kind, srange, desc = WORKLOADS[args.workload]
     times = []
     tok_s = None
@@ -283,6 +290,223 @@ def run_reference(args, world, rank):
     return 0
 
 
+# ---------------------------------------------------------------------------------- down projection workload
+def down_inputs(copies):
+    from types import SimpleNamespace
+    g = torch.Generator().manual_seed(20261202)
+    K, N, G, P, B = DOWN["K"], DOWN["N"], DOWN["group"], DOWN["parts"], DOWN["block"]
+    xs = [torch.randn(M, K, generator=g).to(torch.bfloat16) for M in DOWN["buckets"]]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    banks = []
+    for c in range(copies):
+        gc = torch.Generator().manual_seed(2000 + c)
+        banks.append(SimpleNamespace(
+            width=K, parts=P, group=G, block=B, chunk=K // P, hp=0,
+            centers=(torch.randn(K, generator=gc) * 0.05).to(dev),
+            low_weight=torch.randint(-127, 128, (N, P * G), generator=gc, dtype=torch.int8).to(dev),
+            high_weight=torch.zeros(N, 0, dtype=torch.bfloat16, device=dev),
+            scales=(1e-3 + 9e-3 * torch.rand(P, N, generator=gc)).to(dev),
+            bias=(torch.randn(P, N, generator=gc) * 0.05).to(dev)))
+    return xs, banks
+
+
+def down_cpu_run(budget_s: float = 12.0):
+    """The oracle's rotated projection on the host cores over a bounded sample (all buckets, 256 of the
+    N output columns), scaled to full width."""
+    from types import SimpleNamespace
+    from oracle import reax_oracle as ro
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    K, N, G, P, B = DOWN["K"], DOWN["N"], DOWN["group"], DOWN["parts"], DOWN["block"]
+    g = np.random.default_rng(9)
+    cols = 256
+    bank = SimpleNamespace(parts=P, group=G, block=B, chunk=K // P, centers=(g.standard_normal(K) * 0.05).astype(np.float32),
+                           low_weight=g.integers(-127, 128, (cols, P * G), dtype=np.int8),
+                           scales=(1e-3 + 9e-3 * g.random((P, cols))).astype(np.float32),
+                           bias=(g.standard_normal((P, cols)) * 0.05).astype(np.float32))
+    xs = [ro.f32_to_bf16(g.standard_normal((M, K)).astype(np.float32)) for M in DOWN["buckets"]]
+    tokens = sum(len(x) for x in xs)
+    t0 = time.perf_counter()
+    passes = 0
+    while True:
+        for x in xs:
+            ro.rotated_project(x, bank)
+        passes += 1
+        if time.perf_counter() - t0 > budget_s or passes >= 50:
+            break
+    dt = time.perf_counter() - t0
+    sample = (f"{passes} passes over buckets {list(len(x) for x in xs)} rows x {cols}/{N} output columns "
+              f"(scaled to full width), {dt:.1f} s")
+    return tokens * passes / dt * (cols / N), threads, sample
+
+
+def down_desc():
+    return (f"rotated INT8 down projection, decode buckets M={{1,8,32,64}}, K={DOWN['K']}, N={DOWN['N']}, "
+            f"{DOWN['parts']} groups of {DOWN['group']}, Walsh-Hadamard blocks of {DOWN['block']}")
+
+
+def run_down_reference(args):
+    times = []
+    threads, sample = os.cpu_count() or 1, ""
+    for i in range(args.warmup + args.steps):
+        v, threads, sample = down_cpu_run(budget_s=1.5 if args.steps > 20 else 4.0)
+        if i >= args.warmup:
+            times.append(v)
+    tok_s = statistics.median(times)
+    line = {"impl": "reference", "metric": DOWN_METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sum(DOWN["buckets"]) / tok_s * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "s8", "data": "synthetic",
+            "config": {"workload": down_desc(), "parallelism": "host cores"},
+            "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_down(args, world, rank, local):
+    """The rotated down projection (rotated quantizer -> grouped INT8 partials -> ordered fold) through the
+    reference's API (reaxv2.rotation.Native.project), timed like the gate/up step."""
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"error": "the down workload runs on one GPU"}), flush=True)
+        torch.distributed.destroy_process_group()
+        return 0
+    from reax_engine_runtime_v3_b200.reaxv2.rotation import Native as Rotation, quantize_rotated
+    from reax_engine_runtime_v3_b200.reaxv2.sliced import Native as Sliced, sliced_i8
+    K, N, G, P, B = DOWN["K"], DOWN["N"], DOWN["group"], DOWN["parts"], DOWN["block"]
+    buckets = DOWN["buckets"]
+    copies = 3
+    dev = torch.device("cuda", local)
+    xs_cpu, banks = down_inputs(copies)
+    xs = [x.to(dev) for x in xs_cpu]
+    native = Rotation(Sliced(None), None, 128)
+
+    def bank_of(i, j):
+        return banks[(i * len(buckets) + j) % copies]
+
+    def step(i):
+        return [native.project(x, bank_of(i, j), "slice_m128n256") for j, x in enumerate(xs)]
+
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(torch.cuda.current_stream(dev))
+
+    def graphs_of(fn):
+        gs = []
+        for c in range(copies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                fn(c)
+            gs.append(g)
+        return gs
+
+    def timed(gs, n):
+        for i in range(args.warmup):
+            gs[i % len(gs)].replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cap)
+        for i in range(n):
+            gs[i % len(gs)].replay()
+        e1.record(cap)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    with torch.cuda.stream(cap):
+        for i in range(args.warmup):
+            step(i)
+        torch.cuda.synchronize()
+        graphs = graphs_of(step)
+        sampler = ClockSampler(local)
+        sampler.start()
+        ms = timed(graphs, args.steps)
+        clocks = sampler.stop()
+        # dominant kernel (the grouped INT8 GEMM) and the quantizer, back to back per bucket
+        per_gemm, per_quant = [], []
+        for x in xs:
+            M = x.shape[0]
+            low, sc = quantize_rotated(x, banks[0].centers, K // P, P, G, B)
+            parts_buf = torch.empty(P, M, N, dtype=torch.bfloat16, device=dev)
+            reps = 3 * copies
+            gg = graphs_of(lambda c: [sliced_i8(low, banks[r % copies].low_weight, None, None, sc, banks[r % copies].scales,
+                                                banks[r % copies].bias, parts_buf, G, 0, P) for r in range(reps)])
+            per_gemm.append((M, timed(gg, max(2, args.steps // reps)) * 1e-3 / reps))
+            gq = graphs_of(lambda c: [quantize_rotated(x, banks[r % copies].centers, K // P, P, G, B) for r in range(reps)])
+            per_quant.append((M, timed(gq, max(2, args.steps // reps)) * 1e-3 / reps))
+            del gg, gq
+        # end to end with host buffers (inputs from pinned memory, outputs back), copies on side streams
+        xs_host = [x.pin_memory() for x in xs_cpu]
+        outs_host = [torch.empty((x.shape[0], N), dtype=torch.bfloat16).pin_memory() for x in xs_cpu]
+        xs_dev = [torch.empty_like(x, device=dev) for x in xs_cpu]
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        order = sorted(range(len(buckets)), key=lambda j: -buckets[j])
+
+        def e2e_step(i):
+            main = torch.cuda.current_stream(dev)
+            s_in.wait_stream(main)
+            s_out.wait_stream(main)
+            arrived = []
+            with torch.cuda.stream(s_in):
+                for j in order:
+                    xs_dev[j].copy_(xs_host[j], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(s_in)
+                    arrived.append(ev)
+            outs = []
+            for j, ev in zip(order, arrived):
+                main.wait_event(ev)
+                o = native.project(xs_dev[j], bank_of(i, j), "slice_m128n256")
+                outs.append(o)
+                done = torch.cuda.Event()
+                done.record(main)
+                s_out.wait_event(done)
+                with torch.cuda.stream(s_out):
+                    outs_host[j].copy_(o, non_blocking=True)
+            main.wait_stream(s_in)
+            main.wait_stream(s_out)
+            return outs
+        e2e_step(0)
+        torch.cuda.synchronize()
+        eg = graphs_of(e2e_step)
+        ems = timed(eg, args.steps)
+        # the last replay's read-back must equal the device path's outputs for the same weight copies
+        last = (args.steps - 1) % copies
+        for j, x in enumerate(xs):
+            o = native.project(x, bank_of(last, j), "slice_m128n256")
+            if not torch.equal(o.cpu(), outs_host[j]):
+                raise RuntimeError(f"down e2e read-back of bucket M={x.shape[0]} differs from the device path")
+        status = 0
+        del eg, graphs
+    tokens = sum(buckets)
+    peaks, peak_kind = measured_peaks()
+    by = sum(N * P * G + P * N * 8 + M * P * G + P * M * 4 + P * M * N * 2 for M, _ in per_gemm)
+    dur = sum(d for _, d in per_gemm)
+    achieved = by / dur / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                "kernel": "grouped INT8 GEMM (tc_gemm_kernel, plain epilogue, one partial per group)",
+                "per_launch_us": {str(M): round(d * 1e6, 2) for M, d in per_gemm},
+                "quantizer_per_launch_us": {str(M): round(d * 1e6, 2) for M, d in per_quant}}
+    cpu = None
+    if not args.no_cpu_baseline:
+        v, threads, sample = down_cpu_run()
+        cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
+    line = {"metric": DOWN_METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "s8",
+            "data": "synthetic (seeded N(0,1) activations, uniform int8 rotated weights)",
+            "config": {"workload": down_desc(), "tokens_per_step": tokens, "parallelism": "1 GPU",
+                       "l2": f"{copies} rotating weight copies, a different copy on consecutive calls"},
+            "roofline": roofline, "cpu_baseline": cpu,
+            "e2e": {"value": tokens / (ems * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs_cpu),
+                    "d2h_bytes_per_step": sum(x.shape[0] * N * 2 for x in xs_cpu),
+                    "how": "public API calls captured into CUDA graphs; H2D and D2H on side streams"},
+            "gpu_launches": args.steps * len(buckets) * 3, "clocks": clocks, "device_status": status,
+            "timing": "CUDA-graph replay of the captured step"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # -------------------------------------------------------------------------------------------------- GPU leg
 def main():
     args = parse()
@@ -299,6 +523,8 @@ def main():
                                              device_id=torch.device("cuda", local))
     if args.measure_int8_peak:
         return measure_int8_peak()
+    if args.workload == "down":
+        return run_down(args, world, rank, local)
 
     from reax_engine_runtime_v3_b200 import _native
     from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native

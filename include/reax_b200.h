@@ -82,8 +82,8 @@ REAX_API int reax_quant_groups(const void* x, const int32_t* low_columns, const 
  * set; Walsh-Hadamard butterflies (lo, hi) -> (lo + hi, lo - hi) on aligned blocks of `block` values,
  * index bit 0 first; scale = max(1e-12, absmax) * fl(1/127); codes float2int_rn(div_rn(v, scale)).
  * x bf16 [M, K], centers float32 [K] -> low int8 [M, parts*group], scales float32 [parts, M].
- * Requires block a power of two (>= 2) dividing group, group % 32 == 0, chunk <= group, and
- * group / min(256, largest power of two dividing group) <= 24 (every reference rotation_* shape). */
+ * Requires block a power of two (>= 2) dividing group, group <= 8192 and chunk <= group (every
+ * reference rotation_* shape). */
 REAX_API int reax_quant_rotated(const void* x, const float* centers, int8_t* low, float* scales, int M, int K,
                                 int chunk, int parts, int group, int block, void* stream);
 

@@ -547,32 +547,49 @@ int reax_quant_rotated(const void* x, const float* centers, int8_t* low, float* 
     if (M < 0 || K <= 0 || chunk <= 0 || parts < 1 || group <= 0 || block < 2)
         return fail(REAX_ERR_INVALID, "quant_rotated: bad sizes M=%d K=%d chunk=%d parts=%d group=%d block=%d", M, K,
                     chunk, parts, group, block);
-    if ((block & (block - 1)) != 0 || group % block != 0 || group % 32 != 0 || chunk > group)
+    if ((block & (block - 1)) != 0 || group % block != 0 || group > reax::kRotMaxGroup || chunk > group)
         return fail(REAX_ERR_INVALID,
-                    "quant_rotated: needs block a power of two dividing group, group %% 32 == 0 and chunk <= group "
-                    "(group=%d block=%d chunk=%d)", group, block, chunk);
-    const int threads = std::min(reax::kRotMaxThreads, group & -group);
-    if (group / threads > reax::kRotMaxV)
-        return fail(REAX_ERR_INVALID, "quant_rotated: group %d needs %d values per thread (at most %d)", group,
-                    group / threads, reax::kRotMaxV);
+                    "quant_rotated: needs block a power of two dividing group, group <= %d and chunk <= group "
+                    "(group=%d block=%d chunk=%d)", reax::kRotMaxGroup, group, block, chunk);
     if (M == 0) return REAX_OK;
     if (!x || !centers || !low || !scales) return fail(REAX_ERR_INVALID, "quant_rotated: NULL pointer argument");
     int dev;
     DeviceInfo* info;
     int rc = current_device(&dev, &info);
     if (rc != REAX_OK) return rc;
+    // groups of 64 V columns for the V of every reference group shape keep the values in registers
+    using RotKernel = void (*)(const __nv_bfloat16*, const float*, int8_t*, float*, int, int, int, int, int, int);
+    RotKernel kernel = reax::quant_rotated_kernel;
+    int threads = reax::kRotThreads;
+    size_t smem = static_cast<size_t>(group + 32) * sizeof(float);
+    // the register kernel needs block / 64 to divide V (true whenever block divides group)
+    if (group % 64 == 0 && block <= 1024) {
+        switch (group / 64) {
+            case 8: kernel = reax::quant_rotated_regs_kernel<8>; break;
+            case 16: kernel = reax::quant_rotated_regs_kernel<16>; break;
+            case 21: kernel = reax::quant_rotated_regs_kernel<21>; break;
+            case 22: kernel = reax::quant_rotated_regs_kernel<22>; break;
+            case 36: kernel = reax::quant_rotated_regs_kernel<36>; break;
+            case 48: kernel = reax::quant_rotated_regs_kernel<48>; break;
+            default: break;
+        }
+        if (kernel != reax::quant_rotated_kernel) {
+            threads = 64;
+            smem = 0;
+        }
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(M, parts, 1);
     cfg.blockDim = dim3(threads, 1, 1);
-    cfg.dynamicSmemBytes = static_cast<size_t>(group + 32) * sizeof(float);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, reax::quant_rotated_kernel, static_cast<const __nv_bfloat16*>(x), centers,
-                                       low, scales, M, K, chunk, parts, group, block);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<const __nv_bfloat16*>(x), centers, low, scales, M, K,
+                                       chunk, parts, group, block);
     if (e != cudaSuccess) return cuda_fail(e, "quant_rotated launch");
     return REAX_OK;
 }

@@ -238,81 +238,122 @@ __global__ void __launch_bounds__(256) quant_groups_kernel(const __nv_bfloat16* 
 }
 
 // -------------------------------------------------------------- rotated quantizer of the down projection
-// One CTA of T threads per (row, part) (block_rotation.cu:5-65, launched by reaxv2/rotation.py:14-30).
-// Thread t holds values o = t + j * T, j < V = group / T: the part's centred input columns, negated by
-// the column's hash bit, zero past the part's chunk or past K.  Walsh-Hadamard butterflies
-// (lo, hi) -> (lo + hi, lo - hi) run on aligned blocks of `block` values, index bit 0 first: bits 0-4 are
-// lane bits (warp shuffles), the higher bits go through shared memory one stage per barrier.  Every
-// value goes through the same additions in the same order as the reference's thread layout gives it,
-// so the transform, the scale max(1e-12, absmax) * fl(1/127) and the codes float2int_rn(div_rn(v, scale))
-// (no clamp) are bit-identical.
-constexpr int kRotMaxV = 24;         // values per thread
-constexpr int kRotMaxThreads = 256;  // the largest power of two dividing the group, at most this
+// One CTA per (row, part) (block_rotation.cu:5-65, launched by reaxv2/rotation.py:14-30).  The part's
+// group values sit in shared memory: the centred input columns, negated by the column's hash bit, zero
+// past the part's chunk or past K.  Walsh-Hadamard butterflies (lo, hi) -> (lo + hi, lo - hi) then run
+// on aligned blocks of `block` values, one stage per index bit, bit 0 first, each stage's pairs shared
+// out over the threads.  Every value goes through the same additions in the same order as in the
+// reference (whose thread layout spreads the same stages over lanes, warps and registers), so the
+// transform, the scale max(1e-12, absmax) * fl(1/127) and the codes float2int_rn(div_rn(v, scale)) (no
+// clamp) are bit-identical.  The kernel is a few short loops, so a CTA starts without fetching a long
+// unrolled body.
+constexpr int kRotThreads = 256;
+constexpr int kRotMaxGroup = 8192;
 
-__global__ void __launch_bounds__(kRotMaxThreads) quant_rotated_kernel(
+__global__ void __launch_bounds__(kRotThreads) quant_rotated_kernel(
     const __nv_bfloat16* __restrict__ x, const float* __restrict__ centers, int8_t* __restrict__ low,
     float* __restrict__ scales, int M, int K, int chunk, int parts, int group, int block) {
-    extern __shared__ float rot_s[];   // group floats, then 32 for the maximum
+    extern __shared__ float rot_s[];   // group values, then 32 floats for the maximum
     grid_dependency_wait();
     grid_dependents_launch();
-    const int T = blockDim.x, V = group / T;
+    const int t = threadIdx.x, T = blockDim.x;
+    const int row = blockIdx.x, part = blockIdx.y;
+    const __nv_bfloat16* xr = x + static_cast<size_t>(row) * K;
+    for (int o = t; o < group; o += T) {
+        const int c = part * chunk + o;
+        float a = 0.f;
+        if (o < chunk && c < K) a = __fsub_rn(__bfloat162float(xr[c]), __ldg(centers + c));
+        const uint32_t h = static_cast<uint32_t>(c) * 1103515245u + 12345u;
+        rot_s[o] = (h & 65536u) ? -a : a;
+    }
+    for (int d = 1; d < block; d *= 2) {
+        __syncthreads();
+        for (int q = t; q < group / 2; q += T) {
+            const int lo = ((q & ~(d - 1)) << 1) | (q & (d - 1));
+            const float a = rot_s[lo], b = rot_s[lo + d];
+            rot_s[lo] = __fadd_rn(a, b);
+            rot_s[lo + d] = __fsub_rn(a, b);
+        }
+    }
+    __syncthreads();
+    float m = 0.f;
+    for (int o = t; o < group; o += T) m = fmaxf(m, fabsf(rot_s[o]));
+    m = group_max_nonneg(m, rot_s + group, t, T, [] { __syncthreads(); });
+    const float scale = __fmul_rn(fmaxf(m, 1.0e-12f), 1.0f / 127.0f);
+    if (t == 0) scales[static_cast<size_t>(part) * M + row] = scale;
+    int8_t* lr = low + static_cast<size_t>(row) * parts * group + static_cast<size_t>(part) * group;
+    for (int o = t; o < group; o += T) lr[o] = static_cast<int8_t>(__float2int_rn(__fdiv_rn(rot_s[o], scale)));
+}
+
+// The same quantizer with the values in registers, for groups of 64 V columns (V compile-time): one CTA
+// of 64 threads per (row, part), thread t holding values o = t + 64 j.  Index bits 0-4 are lane bits
+// (warp shuffles), bit 5 the warp bit (one exchange through shared memory), bits 6 and up the register
+// index (pairs j, j ^ d); the stages still run bit 0 first, so the results are those of
+// quant_rotated_kernel.  Every reference group shape (512 .. 3072 columns) has an instantiation.
+template <int V>
+__global__ void __launch_bounds__(64) quant_rotated_regs_kernel(
+    const __nv_bfloat16* __restrict__ x, const float* __restrict__ centers, int8_t* __restrict__ low,
+    float* __restrict__ scales, int M, int K, int chunk, int parts, int group, int block) {
+    __shared__ float rot_s[64 * V + 32];
+    grid_dependency_wait();
+    grid_dependents_launch();
     const int t = threadIdx.x, lane = t & 31;
     const int row = blockIdx.x, part = blockIdx.y;
     const __nv_bfloat16* xr = x + static_cast<size_t>(row) * K;
-    float v[kRotMaxV];
+    float v[V];
 #pragma unroll
-    for (int j = 0; j < kRotMaxV; ++j) {
-        v[j] = 0.f;
-        if (j < V) {
-            const int o = t + j * T, c = part * chunk + o;
-            float a = 0.f;
-            if (o < chunk && c < K) a = __fsub_rn(__bfloat162float(xr[c]), __ldg(centers + c));
-            const uint32_t h = static_cast<uint32_t>(c) * 1103515245u + 12345u;
-            v[j] = (h & 65536u) ? -a : a;
-        }
+    for (int j = 0; j < V; ++j) {
+        const int o = t + j * 64, c = part * chunk + o;
+        float a = 0.f;
+        if (o < chunk && c < K) a = __fsub_rn(__bfloat162float(xr[c]), __ldg(centers + c));
+        const uint32_t h = static_cast<uint32_t>(c) * 1103515245u + 12345u;
+        v[j] = (h & 65536u) ? -a : a;
     }
-    // index bits 0-4: lanes
+    // index bits 0-4: lanes (every shuffle runs; stages at or past the block keep their value)
 #pragma unroll
     for (int d = 1; d < 32; d *= 2) {
-        if (d >= block) break;
+        const bool on = d < block;
 #pragma unroll
-        for (int j = 0; j < kRotMaxV; ++j) {
-            if (j >= V) break;   // the same for the whole CTA
+        for (int j = 0; j < V; ++j) {
             const float partner = __shfl_xor_sync(0xffffffffu, v[j], d);
-            v[j] = (lane & d) ? __fsub_rn(partner, v[j]) : __fadd_rn(v[j], partner);
+            const float r = (lane & d) ? __fsub_rn(partner, v[j]) : __fadd_rn(v[j], partner);
+            v[j] = on ? r : v[j];
         }
     }
-    // index bits 5 .. log2(block) - 1: pairs through shared memory
+    // index bit 5: the other warp, through shared memory
     if (block > 32) {
 #pragma unroll
-        for (int j = 0; j < kRotMaxV; ++j)
-            if (j < V) rot_s[t + j * T] = v[j];
-        for (int d = 32; d < block; d *= 2) {
-            __syncthreads();
-            for (int q = t; q < group / 2; q += T) {
-                const int lo = ((q & ~(d - 1)) << 1) | (q & (d - 1));
-                const float a = rot_s[lo], b = rot_s[lo + d];
-                rot_s[lo] = __fadd_rn(a, b);
-                rot_s[lo + d] = __fsub_rn(a, b);
-            }
-        }
+        for (int j = 0; j < V; ++j) rot_s[t + j * 64] = v[j];
         __syncthreads();
 #pragma unroll
-        for (int j = 0; j < kRotMaxV; ++j)
-            if (j < V) v[j] = rot_s[t + j * T];
+        for (int j = 0; j < V; ++j) {
+            const float partner = rot_s[(t ^ 32) + j * 64];
+            v[j] = (t & 32) ? __fsub_rn(partner, v[j]) : __fadd_rn(v[j], partner);
+        }
+    }
+    // index bits 6 and up: register pairs (V is a multiple of block / 64, so j ^ d < V in every stage run)
+#pragma unroll
+    for (int d = 1; d < 16; d *= 2) {
+        if (d * 64 < block) {
+            float next[V];
+#pragma unroll
+            for (int j = 0; j < V; ++j) {
+                const float w = (j ^ d) < V ? v[j ^ d] : 0.f;
+                next[j] = (j & d) ? __fsub_rn(w, v[j]) : __fadd_rn(v[j], w);
+            }
+#pragma unroll
+            for (int j = 0; j < V; ++j) v[j] = next[j];
+        }
     }
     float m = 0.f;
 #pragma unroll
-    for (int j = 0; j < kRotMaxV; ++j)
-        if (j < V) m = fmaxf(m, fabsf(v[j]));
-    float* red = rot_s + group;
-    m = group_max_nonneg(m, red, t, T, [] { __syncthreads(); });
+    for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(v[j]));
+    m = group_max_nonneg(m, rot_s + 64 * V, t, 64, [] { __syncthreads(); });
     const float scale = __fmul_rn(fmaxf(m, 1.0e-12f), 1.0f / 127.0f);
     if (t == 0) scales[static_cast<size_t>(part) * M + row] = scale;
     int8_t* lr = low + static_cast<size_t>(row) * parts * group + static_cast<size_t>(part) * group;
 #pragma unroll
-    for (int j = 0; j < kRotMaxV; ++j)
-        if (j < V) lr[t + j * T] = static_cast<int8_t>(__float2int_rn(__fdiv_rn(v[j], scale)));
+    for (int j = 0; j < V; ++j) lr[t + j * 64] = static_cast<int8_t>(__float2int_rn(__fdiv_rn(v[j], scale)));
 }
 
 // ------------------------------------------------------------------ a3 / a12: ordered partial reductions

@@ -73,6 +73,7 @@ def test_install_registers_reference_module_names():
         import runtime.mixed_origin_bf16 as m
         assert g.__name__.startswith("reax_engine_runtime_v3_b200") and hasattr(m, "fold")
         assert hasattr(sys.modules["reaxv2.quantize"], "_prepare")
+        assert hasattr(sys.modules["reaxv2.rotation"], "selected_kernel")
     finally:
         for k, v in saved.items():
             if v is None:

@@ -20,10 +20,11 @@ pytestmark = pytest.mark.gpu
 
 # (M, K, chunk, parts, group, block): the down projection's input width K = 9216 in three group
 # shapes, the GDN output projection's K = 4096 with a group padded past its chunk and past K, a
-# 1408-column group, a K that ends inside the last part, and a block narrower than a warp.
+# 1408-column group, a K that ends inside the last part, a block narrower than a warp, and two groups
+# of no reference shape (the shared-memory kernel instead of the register one).
 CASES = [(1, 9216, 3072, 3, 3072, 1024), (7, 9216, 2304, 4, 2304, 256), (64, 9216, 1024, 9, 1024, 64),
          (5, 4096, 1280, 4, 1344, 64), (3, 4096, 1408, 3, 1408, 128), (16, 1000, 512, 2, 512, 512),
-         (33, 2560, 512, 5, 512, 8)]
+         (33, 2560, 512, 5, 512, 8), (4, 3000, 700, 5, 768, 256), (2, 500, 96, 6, 96, 32)]
 
 
 def inputs(M, K, seed):
