@@ -7,6 +7,7 @@ Drop-in modules mirror the reference's import names and call signatures:
   reax_engine_runtime_v3_b200.reaxv2.gate_up    <- reaxv2/gate_up.py    (CONFIGS, Native)
   reax_engine_runtime_v3_b200.reaxv2.sliced     <- reaxv2/sliced.py     (CONFIGS, Native)
   reax_engine_runtime_v3_b200.reaxv2.rotation   <- reaxv2/rotation.py   (Native, selected_kernel)
+  reax_engine_runtime_v3_b200.reaxv2.assets     <- reaxv2/assets.py     (Assets, Policy)
   reax_engine_runtime_v3_b200.reaxv2.wide_warp_hybrid <- private/snapshots/*/wide_warp_hybrid.py (Native)
   reax_engine_runtime_v3_b200.runtime.mixed_origin_bf16      <- runtime/mixed_origin_bf16.py
   reax_engine_runtime_v3_b200.runtime.split_gated_projection <- runtime/split_gated_projection.py
@@ -32,7 +33,7 @@ def install() -> None:
         "reaxv2": pkg_reaxv2,
         "runtime": pkg_runtime,
     }
-    for sub in ("quantize", "driver", "gate_up", "sliced", "rotation", "wide_warp_hybrid"):
+    for sub in ("quantize", "driver", "gate_up", "sliced", "rotation", "assets", "wide_warp_hybrid"):
         names[f"reaxv2.{sub}"] = importlib.import_module(f"{__name__}.reaxv2.{sub}")
     for sub in ("mixed_origin_bf16", "split_gated_projection"):
         names[f"runtime.{sub}"] = importlib.import_module(f"{__name__}.runtime.{sub}")

@@ -94,3 +94,24 @@ def test_rotated_projection(M, K, parts, group, block, N):
                                               bd.bias, group, 0, parts)
         torch.cuda.synchronize()
         assert np.array_equal(H.bits(ours), ro.reduce_partials(H.bits(partials)))
+
+
+def test_asset_policy_runs_the_rotated_projection(tmp_path):
+    """A frozen bank loaded by the asset drop-in (reaxv2/assets.py) and routed by its policy runs the rotated
+    projection on the GPU with the oracle's bits."""
+    from tests.test_assets_cpu import core_with_layers, write_assets
+    from reax_engine_runtime_v3_b200.reaxv2.assets import Assets
+    g = H.gen(4242)
+    K, parts, group, block, N, M = 2048, 2, 1024, 64, 512, 17
+    bank = rotated_bank(g, K, parts, group, block, N)
+    payload = {"schema": 1, "checkpoint_start": 12, "gate_up": {}, "projections": {(14, "down", K): vars(bank)},
+               "chunk_for": {(14, "down", 64): K}, "projection_routes": {},
+               "rotation_routes": {("down", 64, 16, 8): dict(kernel="slice_m128n256", drop=0, threads=128)},
+               "rotation_cap": 8}
+    write_assets(tmp_path, payload)
+    assets = Assets(tmp_path)
+    assets.bind(core_with_layers(32))
+    x = H.activations(g, M, K)
+    out = assets.policy.project(14, "down", x.cuda(), 64)
+    torch.cuda.synchronize()
+    assert np.array_equal(H.bits(out), ro.rotated_project(H.bits(x), H.bank_numpy(bank)))
