@@ -74,7 +74,8 @@ def test_fold_vs_reference_golden():
     assert np.array_equal(H.bits(out), GOLDEN["fold_out"])
 
 
-@pytest.mark.parametrize("P,G,HP,M,N", [(1, 2560, 0, 64, 12288), (2, 1280, 0, 200, 512), (2, 512, 64, 130, 768)])
+@pytest.mark.parametrize("P,G,HP,M,N", [(1, 2560, 0, 64, 12288), (2, 1280, 0, 200, 512), (2, 512, 64, 130, 768),
+                                        (3, 1024, 0, 17, 1536), (2, 512, 64, 9, 768)])
 def test_sliced_projection(P, G, HP, M, N):
     """Grouped INT8 projection (reaxv2/sliced.py): bit-exact when HP == 0, tolerance otherwise."""
     from types import SimpleNamespace

@@ -72,8 +72,10 @@ def test_hybrid_outlier_columns_close_to_reference_kernel():
 
 
 @pytest.mark.skipif(not ref_gpu.available("sliced_linear8.cubin"), reason="reference sliced kernel not built")
-@pytest.mark.parametrize("P,G,M,N", [(1, 2560, 64, 12288), (2, 1280, 200, 512), (4, 512, 33, 1024)])
+@pytest.mark.parametrize("P,G,M,N", [(1, 2560, 64, 12288), (2, 1280, 200, 512), (4, 512, 33, 1024),
+                                     (2, 1024, 1, 1536), (2, 1024, 33, 1536), (3, 512, 64, 2560)])
 def test_sliced_partials_bit_identical_to_reference_kernel(P, G, M, N):
+    """Decode-sized and prefill-sized token counts, one to four groups, N from 1024 to 12288."""
     from reax_engine_runtime_v3_b200.reaxv2.sliced import sliced_i8
     g = H.gen(P + G + M)
     dev = torch.device("cuda")
