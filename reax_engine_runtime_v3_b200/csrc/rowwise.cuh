@@ -81,7 +81,7 @@ constexpr int kQuantThreads = 512;
 constexpr int kQuantThreadsMany = 128;
 
 // v for 8 consecutive low columns starting at c0.
-template <int DIV>
+template <int DIV, bool FAST = false>
 REAX_DEVI void quant_prep8(const __nv_bfloat16* xr, const int* low_columns, const float* smoothing,
                            const float* centers, int c0, int center, bool aligned_x, float (&t)[8]) {
     int idx[8];
@@ -96,16 +96,40 @@ REAX_DEVI void quant_prep8(const __nv_bfloat16* xr, const int* low_columns, cons
         ce[0] = c0v.x; ce[1] = c0v.y; ce[2] = c0v.z; ce[3] = c0v.w;
         ce[4] = c1v.x; ce[5] = c1v.y; ce[6] = c1v.z; ce[7] = c1v.w;
     }
+    // x / 1 is x under both divisions, so chunks whose smoothing is all ones (every BASELINE bank) skip it
+    bool ones = FAST;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) t[i] = quant_div<DIV>(center ? __fsub_rn(t[i], ce[i]) : t[i], sm[i]);
+    for (int i = 0; i < 8; ++i) ones = ones && sm[i] == 1.0f;
+    if (ones) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] = center ? __fsub_rn(t[i], ce[i]) : t[i];
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] = quant_div<DIV>(center ? __fsub_rn(t[i], ce[i]) : t[i], sm[i]);
+    }
 }
 
-// Codes of 8 values, stored at lr[c0..c0+8).
-REAX_DEVI void quant_store8(int8_t* lr, int c0, const float (&t)[8], float scale, bool vec_store) {
+// nearbyint(div_rn(t, scale)) with a multiply for almost every value.  q = t * inv, inv = fl(1 / scale),
+// is within 3 * 2^-24 * |t / scale| of the exact quotient, and the correctly rounded quotient within
+// 2^-24 * |t / scale|; the quantizer's |t / scale| stays below 128 (|t| <= absmax, scale ~ absmax / 127),
+// so both lie within 2^-15 of each other and round to the same integer unless q is within 2^-14 of a
+// half-integer.  Those values, and NaN, take the IEEE division.
+template <bool FAST>
+REAX_DEVI float quant_rint_div(float t, float scale, float inv) {
+    if constexpr (!FAST) return rintf(__fdiv_rn(t, scale));
+    const float q = __fmul_rn(t, inv);
+    const float n = rintf(q);
+    if (fabsf(__fsub_rn(q, n)) < 0.5f - 6.103515625e-05f) return n;
+    return rintf(__fdiv_rn(t, scale));
+}
+
+// Codes of 8 values, stored at lr[c0..c0+8); inv = fl(1 / scale).
+template <bool FAST>
+REAX_DEVI void quant_store8(int8_t* lr, int c0, const float (&t)[8], float scale, float inv, bool vec_store) {
     uint32_t packed[2] = {0u, 0u};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float r = fminf(fmaxf(rintf(__fdiv_rn(t[i], scale)), -127.f), 127.f);
+        const float r = fminf(fmaxf(quant_rint_div<FAST>(t[i], scale, inv), -127.f), 127.f);
         packed[i / 4] |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * (i % 4));
     }
     if (vec_store) {
@@ -118,7 +142,9 @@ REAX_DEVI void quant_store8(int8_t* lr, int c0, const float (&t)[8], float scale
 
 // The low columns of one row, quantized by nthreads threads (tid in [0, nthreads)): codes into lr and
 // the scale into *scale_out; bar() synchronizes the nthreads threads, red holds nthreads / 32 floats.
-template <int DIV, class Bar>
+// FAST (the many-rows kernels): codes by quant_rint_div's multiply and unit smoothing skipped, for
+// throughput; decode rows keep the plain division, whose latency is shorter.  Same codes either way.
+template <int DIV, bool FAST, class Bar>
 REAX_DEVI void quant_row(const __nv_bfloat16* xr, const int* low_columns, const float* smoothing,
                          const float* centers, int center, bool aligned_x, int KL, int tid, int nthreads, float* red,
                          Bar bar, int8_t* lr, float* scale_out) {
@@ -130,14 +156,14 @@ REAX_DEVI void quant_row(const __nv_bfloat16* xr, const int* low_columns, const 
     for (int j = 0; j < kQuantHeld; ++j) {
         const int c0 = tid * 8 + j * step;
         if (c0 < KL8) {
-            quant_prep8<DIV>(xr, low_columns, smoothing, centers, c0, center, aligned_x, held[j]);
+            quant_prep8<DIV, FAST>(xr, low_columns, smoothing, centers, c0, center, aligned_x, held[j]);
 #pragma unroll
             for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(held[j][i]));
         }
     }
     for (int c0 = tid * 8 + kQuantHeld * step; c0 < KL8; c0 += step) {
         float t[8];
-        quant_prep8<DIV>(xr, low_columns, smoothing, centers, c0, center, aligned_x, t);
+        quant_prep8<DIV, FAST>(xr, low_columns, smoothing, centers, c0, center, aligned_x, t);
 #pragma unroll
         for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(t[i]));
     }
@@ -149,23 +175,24 @@ REAX_DEVI void quant_row(const __nv_bfloat16* xr, const int* low_columns, const 
     }
     amax = group_max_nonneg(amax, red, tid, nthreads, bar);
     const float scale = quant_div<DIV>(fmaxf(amax, 1.0e-12f), 127.0f);
+    const float inv = FAST ? __frcp_rn(scale) : 0.f;
     if (tid == 0) *scale_out = scale;
     const bool vec_store = (KL & 7) == 0;
 #pragma unroll
     for (int j = 0; j < kQuantHeld; ++j) {
         const int c0 = tid * 8 + j * step;
-        if (c0 < KL8) quant_store8(lr, c0, held[j], scale, vec_store);
+        if (c0 < KL8) quant_store8<FAST>(lr, c0, held[j], scale, inv, vec_store);
     }
     for (int c0 = tid * 8 + kQuantHeld * step; c0 < KL8; c0 += step) {
         float t[8];
-        quant_prep8<DIV>(xr, low_columns, smoothing, centers, c0, center, aligned_x, t);
-        quant_store8(lr, c0, t, scale, vec_store);
+        quant_prep8<DIV, FAST>(xr, low_columns, smoothing, centers, c0, center, aligned_x, t);
+        quant_store8<FAST>(lr, c0, t, scale, inv, vec_store);
     }
     for (int c = KL8 + tid; c < KL; c += nthreads) {
         float t = __bfloat162float(xr[__ldg(low_columns + c)]);
         if (center) t = __fsub_rn(t, __ldg(centers + c));
         t = quant_div<DIV>(t, __ldg(smoothing + c));
-        const float r = fminf(fmaxf(rintf(__fdiv_rn(t, scale)), -127.f), 127.f);
+        const float r = fminf(fmaxf(quant_rint_div<FAST>(t, scale, inv), -127.f), 127.f);
         lr[c] = static_cast<int8_t>(static_cast<int>(r));
     }
 }
@@ -184,8 +211,9 @@ __global__ void __launch_bounds__(THREADS) quant_rows_kernel(const __nv_bfloat16
     const int row = blockIdx.x;
     const __nv_bfloat16* xr = x + static_cast<size_t>(row) * K;
     if (KL > 0) {
-        quant_row<DIV>(xr, low_columns, smoothing, centers, center, aligned_x != 0, KL, threadIdx.x, blockDim.x, red,
-                       [] { __syncthreads(); }, low + static_cast<size_t>(row) * KL, scales + row);
+        quant_row<DIV, THREADS != kQuantThreads>(xr, low_columns, smoothing, centers, center, aligned_x != 0, KL,
+                                                 threadIdx.x, blockDim.x, red, [] { __syncthreads(); },
+                                                 low + static_cast<size_t>(row) * KL, scales + row);
     } else if (threadIdx.x == 0) {
         scales[row] = 1.0f;
     }

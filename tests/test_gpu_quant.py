@@ -110,6 +110,34 @@ def test_prepare_rows_many_rows(M, K, KH, centered):
     check_quant(low, high, scales, H.bits(x), nb.low_columns, nb.high_columns, nb.smoothing, nb.centers, centered)
 
 
+@pytest.mark.parametrize("M", [3, 700])
+def test_prepare_rows_rounding_ties(M):
+    """Quotients on and next to half-integers: with absmax 127 the scale is 1, so k + 0.5 values are exact
+    ties (round half to even) and values one bf16 step away sit just inside or outside them; rows with
+    other absmax values put quotients within a few ulps of half-integers.  The codes must follow
+    nearbyint(div_rn) exactly (the kernel multiplies by the reciprocal and divides only near ties)."""
+    from types import SimpleNamespace
+    K = 512
+    half = np.arange(-126, 127, dtype=np.float32) + np.float32(0.5)
+    base = np.concatenate([[127.0], half, np.nextafter(half, np.float32(200)), np.nextafter(half, np.float32(-200))])
+    base = base.astype(np.float32)[:K]
+    rows = []
+    g = np.random.default_rng(M)
+    for r in range(M):
+        row = np.zeros(K, np.float32)
+        row[:len(base)] = base * (1.0 if r % 2 == 0 else np.float32(1.0 + 2.0 ** -(8 + r % 7)))
+        row[len(base):] = g.standard_normal(K - len(base)).astype(np.float32)
+        rows.append(row)
+    x_bits = ro.f32_to_bf16(np.stack(rows))
+    dev = torch.device("cuda")
+    bank = SimpleNamespace(width=K, centered=False, low_columns=torch.arange(K, dtype=torch.int32, device=dev),
+                           high_columns=torch.zeros(0, dtype=torch.int32, device=dev),
+                           smoothing=torch.ones(K, device=dev), centers=torch.zeros(K, device=dev))
+    low, high, scales = run_prepare(H.from_bits(x_bits, dev), bank)
+    check_quant(low, high, scales, x_bits, np.arange(K), np.zeros(0, np.int64), np.ones(K, np.float32),
+                np.zeros(K, np.float32), False)
+
+
 def test_prepare_groups_vs_reference_golden():
     G = golden()
     M, K, P, Gs, HP = (int(v) for v in G["groups_shape"])
