@@ -540,17 +540,43 @@ def main():
     bf16 = Bf16Native()
     stream = torch.cuda.current_stream()
 
-    # consecutive calls always read different weight copies, across buckets and across steps
+    # Two lanes, as the reference runtime replays two lanes' graphs at the same time
+    # (runtime/bootstrap.py:29, vendor/s1eng/s1eng/kprio.py:1-4): the buckets, largest first, are dealt to
+    # the lanes alternately from both ends (cfg2: M = 64 then 1 on one lane, 32 then 8 on the other), and
+    # the second lane runs on its own stream, forked from and joined to the step's stream.  A bucket's
+    # slot is its place in the interleaved call order; consecutive calls on a lane, and calls running at
+    # the same time, always read different weight copies.
+    order = sorted(range(len(buckets)), key=lambda j: -buckets[j])
+    lanes = [[], []]
+    for k in range((len(order) + 1) // 2):
+        lanes[k % 2] += sorted({order[k], order[len(order) - 1 - k]}, key=lambda j: -buckets[j])
+    lanes = [ln for ln in lanes if ln]
+    slot_of = {j: 2 * k + l for l, ln in enumerate(lanes) for k, j in enumerate(ln)}
+    side = torch.cuda.Stream(dev)
+
     def bank_of(i, j):
-        return banks[(i * len(buckets) + j) % copies]
+        return banks[(4 * i + slot_of[j]) % copies]
+
+    def run_lanes(work):
+        """work(j) for every bucket j, lane 0 on the current stream and lane 1 on the side stream."""
+        main = torch.cuda.current_stream(dev)
+        outs = []
+        if len(lanes) > 1:
+            side.wait_stream(main)
+        for l, ln in enumerate(lanes):
+            with torch.cuda.stream(main if l == 0 else side):
+                outs += [work(j) for j in ln]
+        if len(lanes) > 1:
+            main.wait_stream(side)
+        return outs
 
     def step(i, inputs=None):
-        for j, x in enumerate(inputs or xs):
+        xs_ = inputs or xs
+
+        def work(j):
             b = bank_of(i, j)
-            if int8:
-                gate_up.project(x, b, "hybrid8_b128n256_s64n256")
-            else:
-                bf16.gate_up(x, b["w"])
+            return gate_up.project(xs_[j], b, "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(xs_[j], b["w"])
+        return run_lanes(work)
 
     # Every timed loop replays CUDA graphs captured from the public API calls, as the reference runtime
     # replays its captured decode steps (runtime/capture.py); one graph per rotating weight copy.  The
@@ -675,45 +701,53 @@ def main():
 
     # end to end through the public API with host buffers: every step copies each bucket's input from
     # pinned host memory, runs the path and reads every output back to pinned host memory, all inside the
-    # replayed graph.  The copies run on two side streams, so a bucket's read-back overlaps the compute of
-    # the buckets after it and the inputs arrive ahead of their compute.  Buckets run largest first and a
-    # bucket of 1024 rows or more runs as four row pieces (the path is per token, so the outputs are the
-    # same); what stays exposed is the first piece's input and the last piece's output.
+    # replayed graph.  The compute runs on the step's two lanes; the copies run on two more streams, so a
+    # bucket's read-back overlaps the compute after it and the inputs arrive ahead of their compute.
+    # Inputs go largest first and a bucket of 1024 rows or more runs as four row pieces (the path is per
+    # token, so the outputs are the same); what stays exposed is the first piece's input and the last
+    # piece's output.
     e2e = None
     if not args.no_e2e:
         xs_host = [x.pin_memory() for x in xs_cpu]
         outs_host = [torch.empty((x.shape[0], h), dtype=torch.bfloat16).pin_memory() for x in xs_cpu]
         xs_dev = [torch.empty_like(x, device=dev) for x in xs_cpu]
-        pieces = []  # (bucket, first row, end row) in issue order
-        for j in sorted(range(len(xs_cpu)), key=lambda j: -xs_cpu[j].shape[0]):
+
+        def pieces_of(j):
             M = xs_cpu[j].shape[0]
             rows = -(-M // (4 if M >= 1024 else 1))
-            pieces += [(j, r, min(M, r + rows)) for r in range(0, M, rows)]
+            return [(j, r, min(M, r + rows)) for r in range(0, M, rows)]
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
         def e2e_step(i):
             main = torch.cuda.current_stream(dev)
             s_in.wait_stream(main)
             s_out.wait_stream(main)
-            arrived = []
+            arrived = {}
             with torch.cuda.stream(s_in):
-                for j, r0, r1 in pieces:
-                    xs_dev[j][r0:r1].copy_(xs_host[j][r0:r1], non_blocking=True)
-                    ev = torch.cuda.Event()
-                    ev.record(s_in)
-                    arrived.append(ev)
-            outs = []  # alive until the step is enqueued, so no output buffer is reused under a read-back
-            for (j, r0, r1), ev in zip(pieces, arrived):
-                main.wait_event(ev)
-                xd = xs_dev[j][r0:r1]
-                b = bank_of(i, j)
-                o = gate_up.project(xd, b, "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(xd, b["w"])
-                outs.append(o)
-                done = torch.cuda.Event()
-                done.record(main)
-                s_out.wait_event(done)
-                with torch.cuda.stream(s_out):
-                    outs_host[j][r0:r1].copy_(o, non_blocking=True)
+                for j in order:
+                    for piece in pieces_of(j):
+                        xs_dev[j][piece[1]:piece[2]].copy_(xs_host[j][piece[1]:piece[2]], non_blocking=True)
+                        ev = torch.cuda.Event()
+                        ev.record(s_in)
+                        arrived[piece] = ev
+
+            def work(j):
+                lane = torch.cuda.current_stream(dev)
+                outs = []   # alive until the step is enqueued, so no output buffer is reused under a read-back
+                for piece in pieces_of(j):
+                    _, r0, r1 = piece
+                    lane.wait_event(arrived[piece])
+                    xd = xs_dev[j][r0:r1]
+                    b = bank_of(i, j)
+                    o = gate_up.project(xd, b, "hybrid8_b128n256_s64n256") if int8 else bf16.gate_up(xd, b["w"])
+                    outs.append(o)
+                    done = torch.cuda.Event()
+                    done.record(lane)
+                    s_out.wait_event(done)
+                    with torch.cuda.stream(s_out):
+                        outs_host[j][r0:r1].copy_(o, non_blocking=True)
+                return outs
+            outs = run_lanes(work)
             main.wait_stream(s_in)
             main.wait_stream(s_out)
             return outs
@@ -748,8 +782,8 @@ def main():
                "h2d_bytes_per_step": sum(x.numel() * 2 for x in xs_cpu),
                "d2h_bytes_per_step": sum(x.shape[0] * h * 2 for x in xs_cpu),
                "how": "public API calls captured once per weight copy into CUDA graphs, replayed per step; "
-                      "H2D and D2H on side streams overlapping compute, buckets largest first, buckets of "
-                      ">= 1024 rows in four row pieces"}
+                      "compute on two lanes, H2D and D2H on side streams overlapping it, inputs largest first, "
+                      "buckets of >= 1024 rows in four row pieces"}
         del egraphs
     del graphs
 
@@ -765,6 +799,7 @@ def main():
                 "data": "synthetic (seeded N(0,1) or Student-t activations, uniform int8 / N(0,0.02) bf16 weights)",
                 "config": {"workload": desc, "tokens_per_step": tokens, "K": K, "H": H, "H_per_gpu": h,
                            "parallelism": f"H-shard x{world}" if world > 1 else "1 GPU",
+                           "lanes": [[buckets[j] for j in ln] for ln in lanes],
                            "l2": f"{copies} rotating weight copies ({copies * 2 * h * K * (1 if int8 else 2) / 1e6:.0f} MB > 126 MB L2), "
                                  "a different copy on consecutive calls"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
