@@ -196,6 +196,34 @@ def test_cfg3_prefill_rows_sample():
     compare_int8(H.activations(g, 4096, 4096), H.int8_bank(g, 4096, 14336), rows=rows)
 
 
+def test_cfg4_rank_shard_rows_sample():
+    """BASELINE config 4 as one rank of its 8-way job sees it: X [8192, 8192] (the 256-thread quantizer),
+    3584 gate rows and their up rows of an int8 [28672, 8192] bank, scales U(5e-4, 5e-3); full GPU run,
+    oracle on a sample of rows."""
+    g = H.gen(4)
+    rows = np.concatenate([np.arange(0, 24), np.arange(4090, 4106), np.arange(8192 - 24, 8192)])
+    compare_int8(H.activations(g, 8192, 8192), H.int8_bank(g, 8192, 3584, scale_lo=5e-4, scale_hi=5e-3), rows=rows)
+
+
+def test_empty_batch():
+    """M = 0: every entry point returns an empty result without launching (the runtime may call a
+    bucket with no rows)."""
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import gate_up_i8, quantize_rows
+    from reax_engine_runtime_v3_b200.reaxv2.rotation import quantize_rotated
+    g = H.gen(0)
+    bank = H.bank_to(H.int8_bank(g, 1024, 512), "cuda")
+    x = torch.zeros(0, 1024, dtype=torch.bfloat16, device="cuda")
+    out = run_project(x, bank)
+    assert out.shape == (0, 512)
+    low, high, sc = quantize_rows(x, bank)
+    assert low.shape == (0, 1024) and sc.shape == (0,)
+    out2 = gate_up_i8(low, bank.low_weight, high, bank.high_weight, sc, bank.scales, bank.bias)
+    assert out2.shape == (0, 512)
+    rl, rs = quantize_rotated(x, torch.zeros(1024, device="cuda"), 512, 2, 512, 64)
+    torch.cuda.synchronize()
+    assert rl.shape == (0, 1024) and rs.shape == (2, 0)
+
+
 def test_cfg5_outliers():
     """BASELINE config 5a: Student-t activations with 8 channels x50, buckets 128 / 512 / 2048."""
     g = H.gen(5)
