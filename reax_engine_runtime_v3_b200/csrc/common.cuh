@@ -40,7 +40,6 @@ REAX_DEVI void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 REAX_DEVI void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-REAX_DEVI void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 REAX_DEVI void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
@@ -290,9 +289,6 @@ REAX_DEVI float bf16_round(float v) { return __bfloat162float(__float2bfloat16_r
 // float32: the arithmetic of the reference's silu_f32 (hybrid8_tiles.cuh:675).
 REAX_DEVI float silu_f32(float x) { return __fdiv_rn(x, 1.0f + expf(-x)); }
 
-// bf16(silu_f32(x)): the value the reference's SwiGLU multiplies by (hybrid8_tiles.cuh:676-678).
-REAX_DEVI float silu_bf16_value(float x) { return bf16_round(silu_f32(x)); }
-
 // ------------------------------------------------------------------------------------------ SiLU table
 // For a bf16-valued x, bf16(silu_f32(x)) depends only on the 16-bit pattern of x, and outside the
 // exponent fields [kSiluTabElo, kSiluTabEhi] (|x| in [2^-10, 128)) it needs no table:
@@ -306,7 +302,8 @@ REAX_DEVI float silu_bf16_value(float x) { return bf16_round(silu_f32(x)); }
 //                    multiplied by u next, which gives the canonical NaN whatever the payload, so
 //                    one NaN serves for all of them.
 // The 2 x 17 x 128 patterns in between are tabulated by the exact formula (8.5 KiB of shared memory).
-// The test over all 65536 bf16 patterns compares this path with silu_bf16_value.
+// The test over all 65536 bf16 patterns compares this path with bf16(silu_f32(x)), the value the
+// reference's SwiGLU multiplies by (hybrid8_tiles.cuh:676-678).
 constexpr uint32_t kSiluTabElo = 117;                                   // 2^-10
 constexpr uint32_t kSiluTabEhi = 133;                                   // [64, 128)
 constexpr uint32_t kSiluTabHalf = (kSiluTabEhi - kSiluTabElo + 1) * 128;  // patterns of one sign
@@ -360,11 +357,6 @@ REAX_DEVI uint64_t add2_rn(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
-REAX_DEVI uint64_t fma2_rn(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
 // two float32 -> packed bf16x2 (round to nearest even), low lane first
 REAX_DEVI uint32_t bf16x2_rn(uint64_t v) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(f2_lo(v), f2_hi(v));
@@ -385,30 +377,11 @@ REAX_DEVI uint64_t dequant2(uint32_t a0, uint32_t a1, uint64_t sa2, uint64_t sw2
     return f2(v0, v1);
 }
 
-// silu_tab of a pair.
-REAX_DEVI uint64_t silu2_tab(uint64_t g2, const uint16_t* tab) { return f2(silu_tab(f2_lo(g2), tab), silu_tab(f2_hi(g2), tab)); }
-
-// SwiGLU of a (gate, up) pair given as packed bf16x2 words: bf16x2 of bf16(silu(g) * u), lane-wise.
-// When every lane of the warp has both gate values inside the table's range (the usual case) the
-// SiLU is one shared-memory load per value; otherwise the warp takes silu_tab's full case analysis.
-// All 32 lanes of the warp must call it together.
-REAX_DEVI uint32_t swiglu2_bits(uint32_t gw, uint32_t uw, const uint16_t* tab) {
-    const uint32_t b0 = gw & 0xFFFFu, b1 = gw >> 16;
-    const uint32_t r0 = (b0 & 0x7FFFu) - (kSiluTabElo << 7), r1 = (b1 & 0x7FFFu) - (kSiluTabElo << 7);
-    uint32_t s0, s1;   // bf16(silu) as float32 bit patterns
-    if (__all_sync(0xFFFFFFFFu, r0 < kSiluTabHalf && r1 < kSiluTabHalf)) {
-        s0 = static_cast<uint32_t>(tab[r0 + (b0 >> 15) * kSiluTabHalf]) << 16;
-        s1 = static_cast<uint32_t>(tab[r1 + (b1 >> 15) * kSiluTabHalf]) << 16;
-    } else {
-        s0 = __float_as_uint(silu_tab(__uint_as_float(b0 << 16), tab));
-        s1 = __float_as_uint(silu_tab(__uint_as_float(b1 << 16), tab));
-    }
-    const uint64_t s2 = (static_cast<uint64_t>(s1) << 32) | s0;
-    return bf16x2_rn(mul2_rn(s2, bf16x2_to_f2(uw)));
-}
-
-// swiglu2_bits of N pairs at once, o[i] from (gw[i], uw[i]), with one warp vote for all of them: the
-// table loads of the pairs do not wait on one another.  All 32 lanes of the warp must call it together.
+// SwiGLU of N (gate, up) pairs given as packed bf16x2 words: o[i] = bf16x2 of bf16(silu(g) * u), lane-wise,
+// from (gw[i], uw[i]).  When every lane of the warp has all its gate values inside the table's range (the
+// usual case) each SiLU is one shared-memory load, and one warp vote covers all N pairs, so their table
+// loads do not wait on one another; otherwise the warp takes silu_tab's full case analysis.  All 32 lanes
+// of the warp must call it together.
 template <int N>
 REAX_DEVI void swiglu2_bits_n(const uint32_t (&gw)[N], const uint32_t (&uw)[N], uint32_t (&o)[N],
                               const uint16_t* tab) {
