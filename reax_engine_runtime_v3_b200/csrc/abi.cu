@@ -557,27 +557,40 @@ int reax_quant_rotated(const void* x, const float* centers, int8_t* low, float* 
     DeviceInfo* info;
     int rc = current_device(&dev, &info);
     if (rc != REAX_OK) return rc;
-    // groups of 64 V columns for the V of every reference group shape keep the values in registers
+    // Groups of the reference shapes keep their values in registers: 64 threads per (row, part), or 128
+    // when there are few rows (decode), so that each thread's chain of butterflies is half as long.
     using RotKernel = void (*)(const __nv_bfloat16*, const float*, int8_t*, float*, int, int, int, int, int, int);
-    RotKernel kernel = reax::quant_rotated_kernel;
+    RotKernel kernel = nullptr;
     int threads = reax::kRotThreads;
     size_t smem = static_cast<size_t>(group + 32) * sizeof(float);
-    // the register kernel needs block / 64 to divide V (true whenever block divides group)
-    if (group % 64 == 0 && block <= 1024) {
-        switch (group / 64) {
-            case 8: kernel = reax::quant_rotated_regs_kernel<8>; break;
-            case 16: kernel = reax::quant_rotated_regs_kernel<16>; break;
-            case 21: kernel = reax::quant_rotated_regs_kernel<21>; break;
-            case 22: kernel = reax::quant_rotated_regs_kernel<22>; break;
-            case 36: kernel = reax::quant_rotated_regs_kernel<36>; break;
-            case 48: kernel = reax::quant_rotated_regs_kernel<48>; break;
-            default: break;
+    if (block <= 1024) {
+        const bool few = static_cast<long long>(M) * parts <= 2LL * info->sms;
+        if (few && group % 128 == 0) {
+            switch (group / 128) {
+                case 4: kernel = reax::quant_rotated_regs_kernel<128, 4>; break;
+                case 8: kernel = reax::quant_rotated_regs_kernel<128, 8>; break;
+                case 11: kernel = reax::quant_rotated_regs_kernel<128, 11>; break;
+                case 18: kernel = reax::quant_rotated_regs_kernel<128, 18>; break;
+                case 24: kernel = reax::quant_rotated_regs_kernel<128, 24>; break;
+                default: break;
+            }
+            if (kernel) threads = 128;
         }
-        if (kernel != reax::quant_rotated_kernel) {
-            threads = 64;
-            smem = 0;
+        if (!kernel && group % 64 == 0) {
+            switch (group / 64) {
+                case 8: kernel = reax::quant_rotated_regs_kernel<64, 8>; break;
+                case 16: kernel = reax::quant_rotated_regs_kernel<64, 16>; break;
+                case 21: kernel = reax::quant_rotated_regs_kernel<64, 21>; break;
+                case 22: kernel = reax::quant_rotated_regs_kernel<64, 22>; break;
+                case 36: kernel = reax::quant_rotated_regs_kernel<64, 36>; break;
+                case 48: kernel = reax::quant_rotated_regs_kernel<64, 48>; break;
+                default: break;
+            }
+            if (kernel) threads = 64;
         }
+        if (kernel) smem = 0;
     }
+    if (!kernel) kernel = reax::quant_rotated_kernel;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(M, parts, 1);
     cfg.blockDim = dim3(threads, 1, 1);

@@ -313,16 +313,17 @@ __global__ void __launch_bounds__(kRotThreads) quant_rotated_kernel(
     for (int o = t; o < group; o += T) lr[o] = static_cast<int8_t>(__float2int_rn(__fdiv_rn(rot_s[o], scale)));
 }
 
-// The same quantizer with the values in registers, for groups of 64 V columns (V compile-time): one CTA
-// of 64 threads per (row, part), thread t holding values o = t + 64 j.  Index bits 0-4 are lane bits
-// (warp shuffles), bit 5 the warp bit (one exchange through shared memory), bits 6 and up the register
-// index (pairs j, j ^ d); the stages still run bit 0 first, so the results are those of
-// quant_rotated_kernel.  Every reference group shape (512 .. 3072 columns) has an instantiation.
-template <int V>
-__global__ void __launch_bounds__(64) quant_rotated_regs_kernel(
+// The same quantizer with the values in registers, for groups of T V columns (T and V compile-time): one
+// CTA of T threads per (row, part), thread t holding values o = t + T j.  Index bits 0-4 are lane bits
+// (warp shuffles), the warp bits go through shared memory (one exchange each), the higher bits are the
+// register index (pairs j, j ^ d); the stages still run bit 0 first, so the results are those of
+// quant_rotated_kernel.  Every reference group shape (512 .. 3072 columns) has a 64-thread
+// instantiation; 128 threads halve each thread's chain for the few-row launches of decode.
+template <int T, int V>
+__global__ void __launch_bounds__(T) quant_rotated_regs_kernel(
     const __nv_bfloat16* __restrict__ x, const float* __restrict__ centers, int8_t* __restrict__ low,
     float* __restrict__ scales, int M, int K, int chunk, int parts, int group, int block) {
-    __shared__ float rot_s[64 * V + 32];
+    __shared__ float rot_s[T * V + 32];
     grid_dependency_wait();
     grid_dependents_launch();
     const int t = threadIdx.x, lane = t & 31;
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(64) quant_rotated_regs_kernel(
     float v[V];
 #pragma unroll
     for (int j = 0; j < V; ++j) {
-        const int o = t + j * 64, c = part * chunk + o;
+        const int o = t + j * T, c = part * chunk + o;
         float a = 0.f;
         if (o < chunk && c < K) a = __fsub_rn(__bfloat162float(xr[c]), __ldg(centers + c));
         const uint32_t h = static_cast<uint32_t>(c) * 1103515245u + 12345u;
@@ -348,21 +349,24 @@ __global__ void __launch_bounds__(64) quant_rotated_regs_kernel(
             v[j] = on ? r : v[j];
         }
     }
-    // index bit 5: the other warp, through shared memory
-    if (block > 32) {
+    // the warp bits: one exchange through shared memory each
 #pragma unroll
-        for (int j = 0; j < V; ++j) rot_s[t + j * 64] = v[j];
+    for (int d = 32; d < T; d *= 2) {
+        if (d >= block) break;   // the same for the whole CTA
+#pragma unroll
+        for (int j = 0; j < V; ++j) rot_s[t + j * T] = v[j];
         __syncthreads();
 #pragma unroll
         for (int j = 0; j < V; ++j) {
-            const float partner = rot_s[(t ^ 32) + j * 64];
-            v[j] = (t & 32) ? __fsub_rn(partner, v[j]) : __fadd_rn(v[j], partner);
+            const float partner = rot_s[(t ^ d) + j * T];
+            v[j] = (t & d) ? __fsub_rn(partner, v[j]) : __fadd_rn(v[j], partner);
         }
+        __syncthreads();
     }
-    // index bits 6 and up: register pairs (V is a multiple of block / 64, so j ^ d < V in every stage run)
+    // the higher bits: register pairs (V is a multiple of block / T, so j ^ d < V in every stage run)
 #pragma unroll
     for (int d = 1; d < 16; d *= 2) {
-        if (d * 64 < block) {
+        if (d * T < block) {
             float next[V];
 #pragma unroll
             for (int j = 0; j < V; ++j) {
@@ -376,12 +380,12 @@ __global__ void __launch_bounds__(64) quant_rotated_regs_kernel(
     float m = 0.f;
 #pragma unroll
     for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(v[j]));
-    m = group_max_nonneg(m, rot_s + 64 * V, t, 64, [] { __syncthreads(); });
+    m = group_max_nonneg(m, rot_s + T * V, t, T, [] { __syncthreads(); });
     const float scale = __fmul_rn(fmaxf(m, 1.0e-12f), 1.0f / 127.0f);
     if (t == 0) scales[static_cast<size_t>(part) * M + row] = scale;
     int8_t* lr = low + static_cast<size_t>(row) * parts * group + static_cast<size_t>(part) * group;
 #pragma unroll
-    for (int j = 0; j < V; ++j) lr[t + j * 64] = static_cast<int8_t>(__float2int_rn(__fdiv_rn(v[j], scale)));
+    for (int j = 0; j < V; ++j) lr[t + j * T] = static_cast<int8_t>(__float2int_rn(__fdiv_rn(v[j], scale)));
 }
 
 // ------------------------------------------------------------------ a3 / a12: ordered partial reductions
