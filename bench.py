@@ -787,6 +787,35 @@ def main():
         del egraphs
     del graphs
 
+    # The optional collective: the all-gather of the largest bucket's output into the concatenated
+    # [M, H] (sharding.gather_output, NCCL), timed on its own; it is not part of `value`.
+    allgather = None
+    if world > 1:
+        from reax_engine_runtime_v3_b200.sharding import gather_output
+        jmax = max(range(len(buckets)), key=lambda j: buckets[j])
+        with torch.cuda.stream(cap):
+            local = gate_up.project(xs[jmax], banks[0], "hybrid8_b128n256_s64n256") if int8 else \
+                bf16.gate_up(xs[jmax], banks[0]["w"])
+            full = gather_output(local, world)
+            torch.cuda.synchronize()
+            if not torch.equal(full[:, rank * h:(rank + 1) * h], local):
+                raise RuntimeError("all-gather: this rank's columns of the gathered output differ from its shard")
+            for _ in range(3):
+                gather_output(local, world)
+            barrier(world)
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n_gather = max(3, args.steps // 5)
+            g0.record(cap)
+            for _ in range(n_gather):
+                gather_output(local, world)
+            g1.record(cap)
+            torch.cuda.synchronize()
+        gms = max_over_ranks(g0.elapsed_time(g1) / n_gather, world)
+        total = local.numel() * 2 * world
+        allgather = {"bucket_M": buckets[jmax], "ms": gms, "bytes_total": total,
+                     "bus_gbs": total * (world - 1) / world / (gms * 1e-3) / 1e9,
+                     "how": "torch.distributed.all_gather_into_tensor (NCCL) into [W, M, H/W], reordered to [M, H]"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, threads, sample = cpu_run(args.workload)
@@ -803,6 +832,7 @@ def main():
                            "l2": f"{copies} rotating weight copies ({copies * 2 * h * K * (1 if int8 else 2) / 1e6:.0f} MB > 126 MB L2), "
                                  "a different copy on consecutive calls"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
+                "allgather": allgather,
                 "device_status": status, "timing": "CUDA-graph replay of the captured step",
                 "eager_ms_per_step": eager_ms}
         print(json.dumps(line), flush=True)
