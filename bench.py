@@ -200,6 +200,39 @@ def ncu_traffic(workload):
     return None
 
 
+def deal_lanes(buckets):
+    """Two lanes, as the reference runtime replays two lanes' graphs at the same time
+    (runtime/bootstrap.py:29, vendor/s1eng/s1eng/kprio.py:1-4): the buckets, largest first, dealt to the
+    lanes from both ends (cfg2: M = 64 then 1 on one lane, 32 then 8 on the other).  Returns the lanes
+    (lists of bucket indices, empty ones dropped) and each bucket's slot, its place in the interleaved
+    call order."""
+    order = sorted(range(len(buckets)), key=lambda j: -buckets[j])
+    lanes = [[], []]
+    for k in range((len(order) + 1) // 2):
+        lanes[k % 2] += sorted({order[k], order[len(order) - 1 - k]}, key=lambda j: -buckets[j])
+    lanes = [ln for ln in lanes if ln]
+    return lanes, {j: 2 * k + l for l, ln in enumerate(lanes) for k, j in enumerate(ln)}
+
+
+def lane_runner(lanes, dev):
+    """run(work): work(j) for every bucket, lane 0 on the current stream and lane 1 on a side stream
+    forked from and joined to it (inside a graph capture too)."""
+    side = torch.cuda.Stream(dev)
+
+    def run(work):
+        main = torch.cuda.current_stream(dev)
+        outs = []
+        if len(lanes) > 1:
+            side.wait_stream(main)
+        for l, ln in enumerate(lanes):
+            with torch.cuda.stream(main if l == 0 else side):
+                outs += [work(j) for j in ln]
+        if len(lanes) > 1:
+            main.wait_stream(side)
+        return outs
+    return run
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -381,11 +414,14 @@ def run_down(args, world, rank, local):
     xs = [x.to(dev) for x in xs_cpu]
     native = Rotation(Sliced(None), None, 128)
 
+    lanes, slot_of = deal_lanes(buckets)
+    run_lanes = lane_runner(lanes, dev)
+
     def bank_of(i, j):
-        return banks[(i * len(buckets) + j) % copies]
+        return banks[(4 * i + slot_of[j]) % copies]
 
     def step(i):
-        return [native.project(x, bank_of(i, j), "slice_m128n256") for j, x in enumerate(xs)]
+        return run_lanes(lambda j: native.project(xs[j], bank_of(i, j), "slice_m128n256"))
 
     cap = torch.cuda.Stream(dev)
     cap.wait_stream(torch.cuda.current_stream(dev))
@@ -540,35 +576,14 @@ def main():
     bf16 = Bf16Native()
     stream = torch.cuda.current_stream()
 
-    # Two lanes, as the reference runtime replays two lanes' graphs at the same time
-    # (runtime/bootstrap.py:29, vendor/s1eng/s1eng/kprio.py:1-4): the buckets, largest first, are dealt to
-    # the lanes alternately from both ends (cfg2: M = 64 then 1 on one lane, 32 then 8 on the other), and
-    # the second lane runs on its own stream, forked from and joined to the step's stream.  A bucket's
-    # slot is its place in the interleaved call order; consecutive calls on a lane, and calls running at
-    # the same time, always read different weight copies.
+    # The step's buckets run on two lanes (deal_lanes).  Consecutive calls on a lane, and calls running
+    # at the same time, always read different weight copies.
     order = sorted(range(len(buckets)), key=lambda j: -buckets[j])
-    lanes = [[], []]
-    for k in range((len(order) + 1) // 2):
-        lanes[k % 2] += sorted({order[k], order[len(order) - 1 - k]}, key=lambda j: -buckets[j])
-    lanes = [ln for ln in lanes if ln]
-    slot_of = {j: 2 * k + l for l, ln in enumerate(lanes) for k, j in enumerate(ln)}
-    side = torch.cuda.Stream(dev)
+    lanes, slot_of = deal_lanes(buckets)
+    run_lanes = lane_runner(lanes, dev)
 
     def bank_of(i, j):
         return banks[(4 * i + slot_of[j]) % copies]
-
-    def run_lanes(work):
-        """work(j) for every bucket j, lane 0 on the current stream and lane 1 on the side stream."""
-        main = torch.cuda.current_stream(dev)
-        outs = []
-        if len(lanes) > 1:
-            side.wait_stream(main)
-        for l, ln in enumerate(lanes):
-            with torch.cuda.stream(main if l == 0 else side):
-                outs += [work(j) for j in ln]
-        if len(lanes) > 1:
-            main.wait_stream(side)
-        return outs
 
     def step(i, inputs=None):
         xs_ = inputs or xs
