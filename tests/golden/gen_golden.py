@@ -1,7 +1,7 @@
 """Generate golden vectors by running the reference's own Triton kernels on the CPU.
 
-Run in a container where the reference project is mounted (default ``/root/reference``, or pass
-its path as the first argument).  The reference's ``reaxv2/quantize.py`` kernels (``_prepare``,
+Run in a container where the reference project is mounted (its path as the first argument, or the
+default mount point).  The reference's ``reaxv2/quantize.py`` kernels (``_prepare``,
 ``prepare_kernel``, ``reduce_kernel``) and ``runtime/mixed_origin_bf16.py``'s ``fold`` are
 executed unmodified by Triton's CPU interpreter (``TRITON_INTERPRET=1``).  The interpreter cannot
 lower the two libdevice calls of ``quantize.py:20,44``; they are supplied with their documented
