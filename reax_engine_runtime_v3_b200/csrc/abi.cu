@@ -311,6 +311,10 @@ bool plan_gate_up_tiles(reax::TcParams& p, int M, int H, int K_blocks, bool weig
 }
 
 int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
+    // Grouped / mixed-origin (plain epilogue) plans always deal whole tiles: their K-split path is not
+    // used (forced on, it measured slower and did not match the oracle), so refuse such a plan.
+    if (epi == reax::kEpiPlain && p.sk_iters > 0)
+        return fail(REAX_ERR_INVALID, "internal: a plain-epilogue plan must not split tiles by K");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(reax::kCtlThreads + 32 * kEpiWarps, 1, 1);
