@@ -561,54 +561,64 @@ int reax_quant_rotated(const void* x, const float* centers, int8_t* low, float* 
     DeviceInfo* info;
     int rc = current_device(&dev, &info);
     if (rc != REAX_OK) return rc;
-    // Groups of the reference shapes keep their values in registers: 64 threads per (row, part), or 128
-    // when there are few rows (decode), so that each thread's chain of butterflies is half as long.
-    using RotKernel = void (*)(const __nv_bfloat16*, const float*, int8_t*, float*, int, int, int, int, int, int);
-    RotKernel kernel = nullptr;
-    int threads = reax::kRotThreads;
-    size_t smem = static_cast<size_t>(group + 32) * sizeof(float);
-    if (block <= 1024) {
-        const bool few = static_cast<long long>(M) * parts <= 2LL * info->sms;
-        if (few && group % 128 == 0) {
-            switch (group / 128) {
-                case 4: kernel = reax::quant_rotated_regs_kernel<128, 4>; break;
-                case 8: kernel = reax::quant_rotated_regs_kernel<128, 8>; break;
-                case 11: kernel = reax::quant_rotated_regs_kernel<128, 11>; break;
-                case 18: kernel = reax::quant_rotated_regs_kernel<128, 18>; break;
-                case 24: kernel = reax::quant_rotated_regs_kernel<128, 24>; break;
-                default: break;
-            }
-            if (kernel) threads = 128;
-        }
-        if (!kernel && group % 64 == 0) {
-            switch (group / 64) {
-                case 8: kernel = reax::quant_rotated_regs_kernel<64, 8>; break;
-                case 16: kernel = reax::quant_rotated_regs_kernel<64, 16>; break;
-                case 21: kernel = reax::quant_rotated_regs_kernel<64, 21>; break;
-                case 22: kernel = reax::quant_rotated_regs_kernel<64, 22>; break;
-                case 36: kernel = reax::quant_rotated_regs_kernel<64, 36>; break;
-                case 48: kernel = reax::quant_rotated_regs_kernel<64, 48>; break;
-                default: break;
-            }
-            if (kernel) threads = 64;
-        }
-        if (kernel) smem = 0;
-    }
-    if (!kernel) kernel = reax::quant_rotated_kernel;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(M, parts, 1);
-    cfg.blockDim = dim3(threads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
     cfg.stream = static_cast<cudaStream_t>(stream);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<const __nv_bfloat16*>(x), centers, low, scales, M, K,
-                                       chunk, parts, group, block);
-    if (e != cudaSuccess) return cuda_fail(e, "quant_rotated launch");
-    return REAX_OK;
+    const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+    cudaError_t e;
+    // Groups of a multiple of 64 columns (every reference shape) keep their values in registers, V
+    // consecutive columns per thread.
+    int V = 0;
+    for (int c : {8, 4, 2})
+        if (!V && group % (32 * c) == 0 && group / c <= 1024) V = c;
+    if (!V) {
+        cfg.blockDim = dim3(reax::kRotThreads, 1, 1);
+        cfg.dynamicSmemBytes = static_cast<size_t>(group + 32) * sizeof(float);
+        e = cudaLaunchKernelEx(&cfg, reax::quant_rotated_kernel, xb, centers, low, scales, M, K, chunk, parts, group,
+                               block);
+        return e == cudaSuccess ? REAX_OK : cuda_fail(e, "quant_rotated launch");
+    }
+    const auto aligned = [](const void* p, int bytes) { return reinterpret_cast<uintptr_t>(p) % bytes == 0; };
+    const bool vec = K % V == 0 && chunk % V == 0 && aligned(x, 16) && aligned(centers, 16) && aligned(low, V);
+    // Many rows: persistent CTAs of group / (V R) threads, each walking rows of one part; three runs per
+    // thread for two-column runs in groups of a multiple of 192 columns, so that a thread has six values.
+    if (vec) {
+        using RowsKernel = void (*)(const __nv_bfloat16*, const float*, int8_t*, float*, int, int, int, int, int, int);
+        const int R = V == 2 && (group / 64) % 3 == 0 ? 3 : 1;
+        const RowsKernel rk = V == 8 ? reax::quant_rotated_rows_kernel<8, 1>
+                              : V == 4 ? reax::quant_rotated_rows_kernel<4, 1>
+                              : R == 3 ? reax::quant_rotated_rows_kernel<2, 3>
+                                       : reax::quant_rotated_rows_kernel<2, 1>;
+        const int threads = group / (V * R);
+        const size_t smem = static_cast<size_t>(64 + (block > 32 * V ? group : 0)) * sizeof(float);
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rk, threads, smem) != cudaSuccess || per_sm < 1)
+            per_sm = 1;
+        const long long resident = static_cast<long long>(per_sm) * info->sms;
+        if (static_cast<long long>(M) * parts >= 2 * resident) {
+            cfg.gridDim = dim3(static_cast<unsigned>(std::max<long long>(1, std::min<long long>(M, resident / parts))),
+                               parts, 1);
+            cfg.blockDim = dim3(threads, 1, 1);
+            cfg.dynamicSmemBytes = smem;
+            e = cudaLaunchKernelEx(&cfg, rk, xb, centers, low, scales, M, K, chunk, parts, group, block);
+            return e == cudaSuccess ? REAX_OK : cuda_fail(e, "quant_rotated launch");
+        }
+    }
+    // Few rows: one CTA of group / V threads per (row, part).
+    using LaneKernel = void (*)(const __nv_bfloat16*, const float*, int8_t*, float*, int, int, int, int, int, int,
+                                int);
+    const LaneKernel lk = V == 8 ? reax::quant_rotated_lanes_kernel<8>
+                          : V == 4 ? reax::quant_rotated_lanes_kernel<4>
+                                   : reax::quant_rotated_lanes_kernel<2>;
+    cfg.blockDim = dim3(group / V, 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(32 + (block > 32 * V ? group : 0)) * sizeof(float);
+    e = cudaLaunchKernelEx(&cfg, lk, xb, centers, low, scales, M, K, chunk, parts, group, block, vec ? 1 : 0);
+    return e == cudaSuccess ? REAX_OK : cuda_fail(e, "quant_rotated launch");
 }
 
 int reax_quant_groups(const void* x, const int32_t* low_columns, const int32_t* high_columns, const float* centers,

@@ -357,6 +357,16 @@ REAX_DEVI uint64_t add2_rn(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+REAX_DEVI uint64_t sub2_rn(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+REAX_DEVI uint64_t fma2_rn(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
 // two float32 -> packed bf16x2 (round to nearest even), low lane first
 REAX_DEVI uint32_t bf16x2_rn(uint64_t v) {
     const __nv_bfloat162 h = __floats2bfloat162_rn(f2_lo(v), f2_hi(v));

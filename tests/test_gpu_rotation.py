@@ -20,11 +20,17 @@ pytestmark = pytest.mark.gpu
 
 # (M, K, chunk, parts, group, block): the down projection's input width K = 9216 in three group
 # shapes, the GDN output projection's K = 4096 with a group padded past its chunk and past K, a
-# 1408-column group, a K that ends inside the last part, a block narrower than a warp, and two groups
-# of no reference shape (the shared-memory kernel instead of the register one).
+# 1408-column group, a K that ends inside the last part, a block narrower than a warp, a chunk that is
+# no multiple of eight (scalar loads and stores), blocks that span two and four warps, and a group of no
+# multiple of 64 columns (the shared-memory kernel).  The second list has launches of many rows (one warp
+# per row and part), in every group shape instantiated for them, with row counts that leave a partial CTA.
 CASES = [(1, 9216, 3072, 3, 3072, 1024), (7, 9216, 2304, 4, 2304, 256), (64, 9216, 1024, 9, 1024, 64),
          (5, 4096, 1280, 4, 1344, 64), (3, 4096, 1408, 3, 1408, 128), (16, 1000, 512, 2, 512, 512),
-         (33, 2560, 512, 5, 512, 8), (4, 3000, 700, 5, 768, 256), (2, 500, 96, 6, 96, 32)]
+         (33, 2560, 512, 5, 512, 8), (4, 3000, 700, 5, 768, 256), (9, 5120, 2560, 2, 2560, 512),
+         (6, 4096, 2048, 2, 2048, 1024), (2, 500, 96, 6, 96, 32)]
+MANY_ROWS = [(1024, 9216, 2304, 4, 2304, 256), (250, 9216, 3072, 3, 3072, 1024), (301, 4096, 1408, 3, 1408, 128),
+             (222, 4096, 1280, 4, 1344, 64), (600, 1000, 512, 2, 512, 512), (150, 5000, 1020, 5, 1024, 256),
+             (201, 2560, 512, 5, 512, 8), (150, 8192, 2048, 4, 2048, 1024), (300, 9216, 1024, 9, 1024, 64)]
 
 
 def inputs(M, K, seed):
@@ -34,13 +40,80 @@ def inputs(M, K, seed):
     return x, centers
 
 
-@pytest.mark.parametrize("M,K,chunk,parts,group,block", CASES)
+@pytest.mark.parametrize("M,K,chunk,parts,group,block", CASES + MANY_ROWS)
 def test_rotated_quantizer_vs_oracle(M, K, chunk, parts, group, block):
     from reax_engine_runtime_v3_b200.reaxv2.rotation import quantize_rotated
     x, centers = inputs(M, K, M + K + group + block)
     low, scales = quantize_rotated(x.cuda(), centers.cuda(), chunk, parts, group, block)
     torch.cuda.synchronize()
     lo, sc = ro.prepare_rotated(H.bits(x), centers.numpy(), chunk, parts, group, block)
+    assert np.array_equal(scales.cpu().numpy().view(np.int32), sc.view(np.int32))
+    assert np.array_equal(low.cpu().numpy(), lo)
+
+
+def _offset_copy(t, elements):
+    """A contiguous copy of t whose data starts `elements` elements past an allocation boundary."""
+    buf = torch.empty(t.numel() + elements, dtype=t.dtype, device=t.device)
+    view = buf[elements:].view(t.shape)
+    view.copy_(t)
+    return view
+
+
+@pytest.mark.parametrize("M,K,chunk,parts,group,block", [(3, 9216, 2304, 4, 2304, 256), (5, 4096, 1408, 3, 1408, 128),
+                                                         (4, 4096, 1280, 4, 1344, 64), (600, 9216, 2304, 4, 2304, 256),
+                                                         (301, 4096, 1408, 3, 1408, 128),
+                                                         (222, 4096, 1280, 4, 1344, 64)])
+@pytest.mark.parametrize("x_off,c_off", [(1, 0), (0, 1), (4, 2)])
+def test_rotated_quantizer_unaligned_inputs(M, K, chunk, parts, group, block, x_off, c_off):
+    """Input rows or centers that do not start on a vector boundary take the scalar loads."""
+    from reax_engine_runtime_v3_b200.reaxv2.rotation import quantize_rotated
+    x, centers = inputs(M, K, 3 * M + K + x_off + 5 * c_off)
+    low, scales = quantize_rotated(_offset_copy(x.cuda(), x_off), _offset_copy(centers.cuda(), c_off), chunk, parts,
+                                   group, block)
+    torch.cuda.synchronize()
+    lo, sc = ro.prepare_rotated(H.bits(x), centers.numpy(), chunk, parts, group, block)
+    assert np.array_equal(scales.cpu().numpy().view(np.int32), sc.view(np.int32))
+    assert np.array_equal(low.cpu().numpy(), lo)
+
+
+def _near_half_rows(rows, K, seed):
+    """bf16 rows whose rotated values (block 2, zero centers, every odd column zero, so both outputs
+    of a pair are +-x) have quotients v / scale within 2^-13 of a half-integer: the codes the kernel
+    must take from the division itself rather than from v * (1 / scale)."""
+    rng = np.random.default_rng(seed)
+    out = np.zeros((rows, K), dtype=np.uint16)
+    found = 0
+    for r in range(rows):
+        top = np.uint16(0x3F80 + rng.integers(0, 0x400))            # the row maximum, in [1, 256)
+        top_f = ro.bf16_to_f32(np.array([top], np.uint16))[0]
+        scale = np.float32(np.float32(max(top_f, np.float32(1e-12))) * np.float32(np.float32(1) / np.float32(127)))
+        cand = np.arange(0x3C00, top, dtype=np.uint16)              # positive bf16 values below the maximum
+        q = (ro.bf16_to_f32(cand) / scale).astype(np.float32)
+        near = cand[np.abs(np.abs(q - np.floor(q)) - np.float32(0.5)) < np.float32(2.0 ** -13)]
+        pick = rng.choice(near, size=min(len(near), K // 2 - 1), replace=False) if len(near) else near
+        found += len(pick)
+        row = np.zeros(K, dtype=np.uint16)
+        row[0] = top
+        row[2:2 + 2 * len(pick):2] = pick
+        out[r] = row
+    return out, found
+
+
+@pytest.mark.parametrize("M", [256, 700])
+def test_rotated_quantizer_near_half_quotients(M):
+    from reax_engine_runtime_v3_b200.reaxv2.rotation import quantize_rotated
+    K = 512
+    xb, found = _near_half_rows(M, K, 11)
+    assert found >= 100
+    x = H.from_bits(xb)
+    centers = torch.zeros(K)
+    low, scales = quantize_rotated(x.cuda(), centers.cuda(), K, 1, K, 2)
+    torch.cuda.synchronize()
+    lo, sc = ro.prepare_rotated(xb, centers.numpy(), K, 1, K, 2)
+    # the inputs bite: rounding v * (1 / scale) instead of v / scale changes some of the codes
+    v = np.abs(ro.bf16_to_f32(xb))
+    naive = np.rint((v * (np.float32(1) / sc[0])[:, None]).astype(np.float32)).astype(np.int64)
+    assert (naive != np.abs(lo.astype(np.int64))).any()
     assert np.array_equal(scales.cpu().numpy().view(np.int32), sc.view(np.int32))
     assert np.array_equal(low.cpu().numpy(), lo)
 
