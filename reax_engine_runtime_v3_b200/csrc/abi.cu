@@ -585,15 +585,14 @@ int reax_quant_rotated(const void* x, const float* centers, int8_t* low, float* 
     }
     const auto aligned = [](const void* p, int bytes) { return reinterpret_cast<uintptr_t>(p) % bytes == 0; };
     const bool vec = K % V == 0 && chunk % V == 0 && aligned(x, 16) && aligned(centers, 16) && aligned(low, V);
-    // Many rows: persistent CTAs of group / (V R) threads, each walking rows of one part; three runs per
-    // thread for two-column runs in groups of a multiple of 192 columns, so that a thread has six values.
-    if (vec) {
+    // Many rows of two-column runs (groups of an odd multiple of 64 columns): persistent CTAs of
+    // group / (2 R) threads, each walking rows of one part, three runs per thread when the group is a
+    // multiple of 192 columns, so that a thread has six values.  Wider runs measured faster with one CTA
+    // per (row, part) at every row count.
+    if (vec && V == 2) {
         using RowsKernel = void (*)(const __nv_bfloat16*, const float*, int8_t*, float*, int, int, int, int, int, int);
-        const int R = V == 2 && (group / 64) % 3 == 0 ? 3 : 1;
-        const RowsKernel rk = V == 8 ? reax::quant_rotated_rows_kernel<8, 1>
-                              : V == 4 ? reax::quant_rotated_rows_kernel<4, 1>
-                              : R == 3 ? reax::quant_rotated_rows_kernel<2, 3>
-                                       : reax::quant_rotated_rows_kernel<2, 1>;
+        const int R = (group / 64) % 3 == 0 ? 3 : 1;
+        const RowsKernel rk = R == 3 ? reax::quant_rotated_rows_kernel<2, 3> : reax::quant_rotated_rows_kernel<2, 1>;
         const int threads = group / (V * R);
         const size_t smem = static_cast<size_t>(64 + (block > 32 * V ? group : 0)) * sizeof(float);
         int per_sm = 0;
@@ -609,7 +608,7 @@ int reax_quant_rotated(const void* x, const float* centers, int8_t* low, float* 
             return e == cudaSuccess ? REAX_OK : cuda_fail(e, "quant_rotated launch");
         }
     }
-    // Few rows: one CTA of group / V threads per (row, part).
+    // Otherwise one CTA of group / V threads per (row, part).
     using LaneKernel = void (*)(const __nv_bfloat16*, const float*, int8_t*, float*, int, int, int, int, int, int,
                                 int);
     const LaneKernel lk = V == 8 ? reax::quant_rotated_lanes_kernel<8>

@@ -325,7 +325,8 @@ __global__ void __launch_bounds__(kRotThreads) quant_rotated_kernel(
 //    1.5 * 2^23 (exact for |q| < 2^22; the sum's low byte is the code mod 256).  v * inv is within
 //    2^-16 of v / scale and fl(v / scale) within 2^-17, because |v / scale| <= 127 (1 + 2^-22): so
 //    when v * inv is more than 2^-14 away from a half-integer, rint of either is the same integer.
-//    The other quotients (and NaN, and v = inf) take float2int_rn(div_rn(v, scale)) itself.
+//    A thread with any other quotient (or a NaN, or v = inf) divides all its values:
+//    float2int_rn(div_rn(v, scale)).
 // vec (host-checked: 16-byte aligned x rows and centers, K and chunk multiples of V, V-byte aligned
 // codes) lets a thread load its run as vectors.
 template <int V>
@@ -406,21 +407,30 @@ __global__ void __launch_bounds__(1024) quant_rotated_lanes_kernel(
         }
         __syncthreads();
     }
+    // the group's maximum: one redux per warp, one barrier, one redux over the warps' maxima
     float m = 0.f;
 #pragma unroll
     for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(v[j]));
-    m = group_max_nonneg(m, rot_s, t, blockDim.x, [] { __syncthreads(); });
+    const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+    if (lane == 0) rot_s[t >> 5] = __uint_as_float(wm);
+    __syncthreads();
+    m = __uint_as_float(
+        __reduce_max_sync(0xffffffffu, lane < (blockDim.x >> 5) ? __float_as_uint(rot_s[lane]) : 0u));
     const float scale = __fmul_rn(fmaxf(m, 1.0e-12f), 1.0f / 127.0f);
     if (t == 0) scales[static_cast<size_t>(part) * M + row] = scale;
     const float inv = __frcp_rn(scale);
     uint32_t code[V];
+    bool ok = true;
 #pragma unroll
     for (int j = 0; j < V; ++j) {
         const float q = __fmul_rn(v[j], inv);
         const float r = __fadd_rn(q, 12582912.0f);
         code[j] = __float_as_uint(r);
-        if (!(fabsf(__fsub_rn(q, __fsub_rn(r, 12582912.0f))) < 0.5f - 6.103515625e-05f))
-            code[j] = static_cast<uint32_t>(__float2int_rn(__fdiv_rn(v[j], scale)));
+        ok = ok && fabsf(__fsub_rn(q, __fsub_rn(r, 12582912.0f))) < 0.5f - 6.103515625e-05f;
+    }
+    if (!ok) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) code[j] = static_cast<uint32_t>(__float2int_rn(__fdiv_rn(v[j], scale)));
     }
     int8_t* lr = low + static_cast<size_t>(row) * parts * group + static_cast<size_t>(part) * group + o0;
     if (vec) {

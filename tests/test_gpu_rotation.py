@@ -22,15 +22,17 @@ pytestmark = pytest.mark.gpu
 # shapes, the GDN output projection's K = 4096 with a group padded past its chunk and past K, a
 # 1408-column group, a K that ends inside the last part, a block narrower than a warp, a chunk that is
 # no multiple of eight (scalar loads and stores), blocks that span two and four warps, and a group of no
-# multiple of 64 columns (the shared-memory kernel).  The second list has launches of many rows (one warp
-# per row and part), in every group shape instantiated for them, with row counts that leave a partial CTA.
+# multiple of 64 columns (the shared-memory kernel).  The second list has launches of many rows, among
+# them groups of an odd multiple of 64 columns (the persistent row-walking kernel, with three runs per
+# thread and with one), with row counts that leave some CTAs a row fewer than others.
 CASES = [(1, 9216, 3072, 3, 3072, 1024), (7, 9216, 2304, 4, 2304, 256), (64, 9216, 1024, 9, 1024, 64),
          (5, 4096, 1280, 4, 1344, 64), (3, 4096, 1408, 3, 1408, 128), (16, 1000, 512, 2, 512, 512),
          (33, 2560, 512, 5, 512, 8), (4, 3000, 700, 5, 768, 256), (9, 5120, 2560, 2, 2560, 512),
          (6, 4096, 2048, 2, 2048, 1024), (2, 500, 96, 6, 96, 32)]
 MANY_ROWS = [(1024, 9216, 2304, 4, 2304, 256), (250, 9216, 3072, 3, 3072, 1024), (301, 4096, 1408, 3, 1408, 128),
-             (222, 4096, 1280, 4, 1344, 64), (600, 1000, 512, 2, 512, 512), (150, 5000, 1020, 5, 1024, 256),
-             (201, 2560, 512, 5, 512, 8), (150, 8192, 2048, 4, 2048, 1024), (300, 9216, 1024, 9, 1024, 64)]
+             (601, 4096, 1280, 4, 1344, 64), (600, 1000, 512, 2, 512, 512), (150, 5000, 1020, 5, 1024, 256),
+             (201, 2560, 512, 5, 512, 8), (150, 8192, 2048, 4, 2048, 1024), (300, 9216, 1024, 9, 1024, 64),
+             (1501, 1280, 320, 4, 320, 64), (1499, 1216, 304, 4, 320, 32)]
 
 
 def inputs(M, K, seed):
