@@ -518,7 +518,8 @@ def run_down(args, world, rank, local):
     dur = sum(d for _, d in per_gemm)
     achieved = by / dur / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": ncu_traffic("down"),
                 "kernel": "grouped INT8 GEMM (tc_gemm_kernel, plain epilogue, one partial per group)",
                 "per_launch_us": {str(M): round(d * 1e6, 2) for M, d in per_gemm},
                 "quantizer_per_launch_us": {str(M): round(d * 1e6, 2) for M, d in per_quant}}
