@@ -313,139 +313,84 @@ __global__ void __launch_bounds__(kRotThreads) quant_rotated_kernel(
     for (int o = t; o < group; o += T) lr[o] = static_cast<int8_t>(__float2int_rn(__fdiv_rn(rot_s[o], scale)));
 }
 
-// The same quantizer with V consecutive columns per thread and group / V threads per (row, part): index
-// bits below log2(V) are register bits, the next five lane bits (one shuffle each) and the rest warp
-// bits (one shared-memory exchange each), so a 256-column block with V = 8 never leaves its warp.  The
-// stages still run bit 0 first with the same roundings:
-//  - a lane stage is one fused multiply-add, fma(+1, lo, hi) = lo + hi on the low lane and
-//    fma(-1, hi, lo) = lo - hi on the high lane (the product by +-1 is exact, so one rounding);
-//  - the column sign is bit 16 of the hash, carried at bit 31 of the hash shifted left by 15
-//    ((h << 15) is linear in the column mod 2^32) and xor-ed into the float;
-//  - the code of v is rint(v * inv) with inv = rcp_rn(scale), the rounding done by adding and removing
-//    1.5 * 2^23 (exact for |q| < 2^22; the sum's low byte is the code mod 256).  v * inv is within
-//    2^-16 of v / scale and fl(v / scale) within 2^-17, because |v / scale| <= 127 (1 + 2^-22): so
-//    when v * inv is more than 2^-14 away from a half-integer, rint of either is the same integer.
-//    A thread with any other quotient (or a NaN, or v = inf) divides all its values:
-//    float2int_rn(div_rn(v, scale)).
-// vec (host-checked: 16-byte aligned x rows and centers, K and chunk multiples of V, V-byte aligned
-// codes) lets a thread load its run as vectors.
-template <int V>
-__global__ void __launch_bounds__(1024) quant_rotated_lanes_kernel(
-    const __nv_bfloat16* __restrict__ x, const float* __restrict__ centers, int8_t* __restrict__ low,
-    float* __restrict__ scales, int M, int K, int chunk, int parts, int group, int block, int vec) {
-    static_assert(V == 2 || V == 4 || V == 8, "two, four or eight columns per thread");
-    extern __shared__ float rot_s[];   // 32 floats for the maximum, then the group when it has warp bits
-    grid_dependency_wait();
-    grid_dependents_launch();
-    const int t = threadIdx.x, lane = t & 31;
-    const int row = blockIdx.x, part = blockIdx.y;
-    const int o0 = t * V, c0 = part * chunk + o0;
-    const __nv_bfloat16* xr = x + static_cast<size_t>(row) * K;
-    float v[V];
-    if (vec && o0 < chunk && c0 < K) {
-        __nv_bfloat16 xb[V];
-        float cv[V];
-        if constexpr (V == 8) {
-            *reinterpret_cast<uint4*>(xb) = __ldg(reinterpret_cast<const uint4*>(xr + c0));
-            *reinterpret_cast<float4*>(cv) = __ldg(reinterpret_cast<const float4*>(centers + c0));
-            *reinterpret_cast<float4*>(cv + 4) = __ldg(reinterpret_cast<const float4*>(centers + c0) + 1);
-        } else if constexpr (V == 4) {
-            *reinterpret_cast<uint2*>(xb) = __ldg(reinterpret_cast<const uint2*>(xr + c0));
-            *reinterpret_cast<float4*>(cv) = __ldg(reinterpret_cast<const float4*>(centers + c0));
-        } else {
-            *reinterpret_cast<uint32_t*>(xb) = __ldg(reinterpret_cast<const uint32_t*>(xr + c0));
-            *reinterpret_cast<float2*>(cv) = __ldg(reinterpret_cast<const float2*>(centers + c0));
+// ----------------------------------------------- register-resident rotated quantization (two kernels)
+// A thread holds R runs of V consecutive columns, run k at group index o = k T V + t V (T threads, a
+// multiple of 32).  Index bits below log2(V) are register bits and the next five lane bits; a block
+// wider than 32 V columns has its higher stages exchanged through shared memory by index, two barriers
+// each.  Column pairs travel as packed float32 pairs (add, sub and fma .rn.f32x2 round each lane as
+// the scalar op does).  The stages run bit 0 first with the reference's roundings.  A lane or exchange
+// stage is one fused multiply-add per pair: fma(+1, lo, hi) = lo + hi on the low side and
+// fma(-1, hi, lo) = lo - hi on the high side (the product by +-1 is exact, so the one rounding is the
+// sum's).  ex holds the group for the exchanges; every thread of the CTA calls together.
+template <int V, int R>
+REAX_DEVI void rot_stages(uint64_t (&p)[R][V / 2], int t, int T, int block, float* ex) {
+    constexpr int W = V / 2;
+    const int lane = t & 31;
+    // index bit 0, inside a pair (block >= 2), then the register bits between pairs
+#pragma unroll
+    for (int k = 0; k < R; ++k)
+#pragma unroll
+        for (int i = 0; i < W; ++i) {
+            const float a = f2_lo(p[k][i]), b = f2_hi(p[k][i]);
+            p[k][i] = f2(__fadd_rn(a, b), __fsub_rn(a, b));
         }
 #pragma unroll
-        for (int j = 0; j < V; ++j) v[j] = __fsub_rn(__bfloat162float(xb[j]), cv[j]);
-    } else {
+    for (int dp = 1; dp < W; dp *= 2) {
+        if (2 * dp >= block) break;
 #pragma unroll
-        for (int j = 0; j < V; ++j) {
-            const int c = c0 + j;
-            v[j] = (o0 + j < chunk && c < K) ? __fsub_rn(__bfloat162float(xr[c]), __ldg(centers + c)) : 0.f;
-        }
+        for (int k = 0; k < R; ++k)
+#pragma unroll
+            for (int i = 0; i < W; ++i) {
+                if (i & dp) continue;
+                const uint64_t a = p[k][i], b = p[k][i + dp];
+                p[k][i] = add2_rn(a, b);
+                p[k][i + dp] = sub2_rn(a, b);
+            }
     }
-    const uint32_t hs0 = (static_cast<uint32_t>(c0) * 1103515245u + 12345u) << 15;
-#pragma unroll
-    for (int j = 0; j < V; ++j) {
-        const uint32_t hs = hs0 + static_cast<uint32_t>(j) * (1103515245u << 15);
-        v[j] = __uint_as_float(__float_as_uint(v[j]) ^ (hs & 0x80000000u));
-    }
-    // register bits
-#pragma unroll
-    for (int d = 1; d < V; d *= 2) {
-        if (d >= block) break;
-#pragma unroll
-        for (int j = 0; j < V; ++j) {
-            if (j & d) continue;
-            const float a = v[j], b = v[j + d];
-            v[j] = __fadd_rn(a, b);
-            v[j + d] = __fsub_rn(a, b);
-        }
-    }
-    // lane bits (index distance V * dl)
+    // lane bits (index distance V dl)
 #pragma unroll
     for (int dl = 1; dl < 32; dl *= 2) {
         if (V * dl >= block) break;   // the same for the whole CTA
-        const float sgn = (lane & dl) ? -1.f : 1.f;
+        const float s = (lane & dl) ? -1.f : 1.f;
+        const uint64_t sg = f2(s, s);
 #pragma unroll
-        for (int j = 0; j < V; ++j) v[j] = __fmaf_rn(sgn, v[j], __shfl_xor_sync(0xffffffffu, v[j], dl));
+        for (int k = 0; k < R; ++k)
+#pragma unroll
+            for (int i = 0; i < W; ++i) {
+                const float a = __shfl_xor_sync(0xffffffffu, f2_lo(p[k][i]), dl);
+                const float b = __shfl_xor_sync(0xffffffffu, f2_hi(p[k][i]), dl);
+                p[k][i] = fma2_rn(sg, p[k][i], f2(a, b));
+            }
     }
-    // warp bits (index distance 32 V dw)
-    float* ex = rot_s + 32;
-    for (int dw = 1; 32 * V * dw < block; dw *= 2) {
+    // wider stages (index distance D >= 32 V) through shared memory
+    for (int D = 32 * V; D < block; D *= 2) {
 #pragma unroll
-        for (int j = 0; j < V; j += 2) *reinterpret_cast<float2*>(ex + o0 + j) = make_float2(v[j], v[j + 1]);
+        for (int k = 0; k < R; ++k)
+#pragma unroll
+            for (int i = 0; i < W; ++i) *reinterpret_cast<uint64_t*>(ex + (k * T + t) * V + 2 * i) = p[k][i];
         __syncthreads();
-        const float sgn = (t & (32 * dw)) ? -1.f : 1.f;
-        const float* pv = ex + (o0 ^ (32 * V * dw));
 #pragma unroll
-        for (int j = 0; j < V; j += 2) {
-            const float2 p = *reinterpret_cast<const float2*>(pv + j);
-            v[j] = __fmaf_rn(sgn, v[j], p.x);
-            v[j + 1] = __fmaf_rn(sgn, v[j + 1], p.y);
+        for (int k = 0; k < R; ++k) {
+            const int o0 = (k * T + t) * V;
+            const float s = (o0 & D) ? -1.f : 1.f;
+            const uint64_t sg = f2(s, s);
+#pragma unroll
+            for (int i = 0; i < W; ++i)
+                p[k][i] = fma2_rn(sg, p[k][i], *reinterpret_cast<const uint64_t*>(ex + (o0 ^ D) + 2 * i));
         }
         __syncthreads();
     }
-    // the group's maximum: one redux per warp, one barrier, one redux over the warps' maxima
+}
+
+// The thread's absmax (fmaxf passes over NaN, as the reference's maximum does).
+template <int V, int R>
+REAX_DEVI float rot_absmax(const uint64_t (&p)[R][V / 2]) {
     float m = 0.f;
 #pragma unroll
-    for (int j = 0; j < V; ++j) m = fmaxf(m, fabsf(v[j]));
-    const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
-    if (lane == 0) rot_s[t >> 5] = __uint_as_float(wm);
-    __syncthreads();
-    m = __uint_as_float(
-        __reduce_max_sync(0xffffffffu, lane < (blockDim.x >> 5) ? __float_as_uint(rot_s[lane]) : 0u));
-    const float scale = __fmul_rn(fmaxf(m, 1.0e-12f), 1.0f / 127.0f);
-    if (t == 0) scales[static_cast<size_t>(part) * M + row] = scale;
-    const float inv = __frcp_rn(scale);
-    uint32_t code[V];
-    bool ok = true;
+    for (int k = 0; k < R; ++k)
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-        const float q = __fmul_rn(v[j], inv);
-        const float r = __fadd_rn(q, 12582912.0f);
-        code[j] = __float_as_uint(r);
-        ok = ok && fabsf(__fsub_rn(q, __fsub_rn(r, 12582912.0f))) < 0.5f - 6.103515625e-05f;
-    }
-    if (!ok) {
-#pragma unroll
-        for (int j = 0; j < V; ++j) code[j] = static_cast<uint32_t>(__float2int_rn(__fdiv_rn(v[j], scale)));
-    }
-    int8_t* lr = low + static_cast<size_t>(row) * parts * group + static_cast<size_t>(part) * group + o0;
-    if (vec) {
-        uint32_t w[(V + 3) / 4];
-#pragma unroll
-        for (int i = 0; i < V / 4; ++i)
-            w[i] = __byte_perm(__byte_perm(code[4 * i], code[4 * i + 1], 0x0040),
-                               __byte_perm(code[4 * i + 2], code[4 * i + 3], 0x0040), 0x5410);
-        if constexpr (V == 8) *reinterpret_cast<uint2*>(lr) = make_uint2(w[0], w[1]);
-        else if constexpr (V == 4) *reinterpret_cast<uint32_t*>(lr) = w[0];
-        else *reinterpret_cast<uint16_t*>(lr) = static_cast<uint16_t>(__byte_perm(code[0], code[1], 0x0040));
-    } else {
-#pragma unroll
-        for (int j = 0; j < V; ++j) lr[j] = static_cast<int8_t>(code[j]);
-    }
+        for (int i = 0; i < V / 2; ++i) m = fmaxf(m, fmaxf(fabsf(f2_lo(p[k][i])), fabsf(f2_hi(p[k][i]))));
+    return m;
 }
 
 // Four codes (the low bytes of a, b, c, d) as one little-endian word.
@@ -453,25 +398,142 @@ REAX_DEVI uint32_t pack4_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t 
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
+// The codes float2int_rn(div_rn(v, scale)) of the thread's values, as bytes in the flat order k V + j.
+// The code of v is rint(q), q = v * inv with inv = rcp_rn(scale), rounded by adding and removing
+// 1.5 * 2^23 (exact for |q| < 2^22; the sum's low byte is the code mod 256).  q is within 2^-16 of
+// v / scale and fl(v / scale) within 2^-17, because |v / scale| <= 127 (1 + 2^-22): so when q is more
+// than 2^-14 away from a half-integer, rint of either is the same integer.  The check, in packed form:
+// t = e e - (1/4 - 2^-14), with e = q - rint(q), is negative when |e| < 0.5 - 2^-14, give or take far
+// less than the margin.  If ptxas fuses the packed product into the packed sums after it, the sum and e
+// come from the exact product v inv, which is within 2^-17 of v / scale too, and the argument holds
+// unchanged.  A thread with any other quotient (or a NaN, which fails the check) divides all its values.
+template <int V, int R>
+REAX_DEVI void rot_codes(const uint64_t (&p)[R][V / 2], float scale, uint32_t (&w)[(R * V + 3) / 4]) {
+    const float inv = __frcp_rn(scale);
+    const uint64_t inv2 = f2(inv, inv), magic2 = f2(12582912.0f, 12582912.0f);
+    const uint64_t lim2 = f2(-(0.25f - 6.103515625e-05f), -(0.25f - 6.103515625e-05f));
+    uint32_t pend0 = 0u, pend1 = 0u;      // the first two codes of a word still to be completed
+    bool ok = true;
+#pragma unroll
+    for (int k = 0; k < R; ++k)
+#pragma unroll
+        for (int i = 0; i < V / 2; ++i) {
+            const uint64_t q = mul2_rn(p[k][i], inv2);
+            const uint64_t r = add2_rn(q, magic2);
+            const uint64_t e = sub2_rn(q, sub2_rn(r, magic2));
+            const uint64_t tt = fma2_rn(e, e, lim2);
+            ok = ok && f2_lo(tt) < 0.f && f2_hi(tt) < 0.f;
+            const uint32_t c0 = __float_as_uint(f2_lo(r)), c1 = __float_as_uint(f2_hi(r));
+            const int f = k * V + 2 * i;   // flat index of c0 among the thread's codes
+            if (f % 4 == 0) pend0 = c0, pend1 = c1;
+            else w[f / 4] = pack4_low_bytes(pend0, pend1, c0, c1);
+        }
+    if (!ok) {
+#pragma unroll
+        for (int k = 0; k < R; ++k)
+#pragma unroll
+            for (int i = 0; i < V / 2; ++i) {
+                const uint32_t c0 = static_cast<uint32_t>(__float2int_rn(__fdiv_rn(f2_lo(p[k][i]), scale)));
+                const uint32_t c1 = static_cast<uint32_t>(__float2int_rn(__fdiv_rn(f2_hi(p[k][i]), scale)));
+                const int f = k * V + 2 * i;
+                if (f % 4 == 0) pend0 = c0, pend1 = c1;
+                else w[f / 4] = pack4_low_bytes(pend0, pend1, c0, c1);
+            }
+    }
+    if constexpr ((R * V) % 4 != 0) w[(R * V + 3) / 4 - 1] = pack4_low_bytes(pend0, pend1, 0u, 0u);
+}
+
+// The thread's codes at lr[(k T + t) V ...], one vector store per run (V-byte aligned codes).
+template <int V, int R>
+REAX_DEVI void rot_store(int8_t* lr, int t, int T, const uint32_t (&w)[(R * V + 3) / 4]) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+        int8_t* dst = lr + (k * T + t) * V;
+        if constexpr (V == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(w[2 * k], w[2 * k + 1]);
+        else if constexpr (V == 4) *reinterpret_cast<uint32_t*>(dst) = w[k];
+        else *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(w[k / 2] >> (16 * (k % 2)));
+    }
+}
+
+// One CTA of group / V threads per (row, part), V consecutive columns per thread (one run).  The
+// column sign is bit 16 of the hash, carried at bit 31 of the hash shifted left by 15 ((h << 15) is
+// linear in the column mod 2^32) and xor-ed into the float.  The group's maximum is one redux per warp,
+// one barrier and one redux over the warps' maxima.  vec (host-checked: 16-byte aligned x and centers,
+// K and chunk multiples of V, V-byte aligned codes) lets a thread load and store its run as vectors.
+template <int V>
+__global__ void __launch_bounds__(1024) quant_rotated_lanes_kernel(
+    const __nv_bfloat16* __restrict__ x, const float* __restrict__ centers, int8_t* __restrict__ low,
+    float* __restrict__ scales, int M, int K, int chunk, int parts, int group, int block, int vec) {
+    static_assert(V == 2 || V == 4 || V == 8, "two, four or eight columns per thread");
+    constexpr int W = V / 2;
+    constexpr uint32_t kHashStep = 1103515245u << 15;
+    extern __shared__ float rot_s[];   // 32 warp maxima, then the group when it has wider stages
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const int t = threadIdx.x, lane = t & 31, T = blockDim.x;
+    const int row = blockIdx.x, part = blockIdx.y;
+    const int o0 = t * V, c0 = part * chunk + o0;
+    const __nv_bfloat16* xr = x + static_cast<size_t>(row) * K;
+    uint64_t p[1][W];
+    if (vec && o0 < chunk && c0 < K) {
+        uint32_t xw[W];
+        float cv[V];
+        if constexpr (V == 8) {
+            *reinterpret_cast<uint4*>(xw) = __ldg(reinterpret_cast<const uint4*>(xr + c0));
+            *reinterpret_cast<float4*>(cv) = __ldg(reinterpret_cast<const float4*>(centers + c0));
+            *reinterpret_cast<float4*>(cv + 4) = __ldg(reinterpret_cast<const float4*>(centers + c0) + 1);
+        } else if constexpr (V == 4) {
+            *reinterpret_cast<uint2*>(xw) = __ldg(reinterpret_cast<const uint2*>(xr + c0));
+            *reinterpret_cast<float4*>(cv) = __ldg(reinterpret_cast<const float4*>(centers + c0));
+        } else {
+            xw[0] = __ldg(reinterpret_cast<const uint32_t*>(xr + c0));
+            *reinterpret_cast<float2*>(cv) = __ldg(reinterpret_cast<const float2*>(centers + c0));
+        }
+#pragma unroll
+        for (int i = 0; i < W; ++i) p[0][i] = sub2_rn(bf16x2_to_f2(xw[i]), f2(cv[2 * i], cv[2 * i + 1]));
+    } else {
+        float a[V];
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+            const int c = c0 + j;
+            a[j] = (o0 + j < chunk && c < K) ? __fsub_rn(__bfloat162float(xr[c]), __ldg(centers + c)) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < W; ++i) p[0][i] = f2(a[2 * i], a[2 * i + 1]);
+    }
+    const uint32_t hs0 = (static_cast<uint32_t>(c0) * 1103515245u + 12345u) << 15;
+#pragma unroll
+    for (int i = 0; i < W; ++i) {
+        const uint32_t h0 = hs0 + static_cast<uint32_t>(2 * i) * kHashStep;
+        const uint32_t h1 = hs0 + static_cast<uint32_t>(2 * i + 1) * kHashStep;
+        p[0][i] ^= (static_cast<uint64_t>(h1 & 0x80000000u) << 32) | (h0 & 0x80000000u);
+    }
+    rot_stages<V, 1>(p, t, T, block, rot_s + 32);
+    const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(rot_absmax<V, 1>(p)));
+    if (lane == 0) rot_s[t >> 5] = __uint_as_float(wm);
+    __syncthreads();
+    const float m = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < (T >> 5) ? __float_as_uint(rot_s[lane]) : 0u));
+    const float scale = __fmul_rn(fmaxf(m, 1.0e-12f), 1.0f / 127.0f);
+    if (t == 0) scales[static_cast<size_t>(part) * M + row] = scale;
+    uint32_t w[(V + 3) / 4];
+    rot_codes<V, 1>(p, scale, w);
+    int8_t* lr = low + static_cast<size_t>(row) * parts * group + static_cast<size_t>(part) * group;
+    if (vec) {
+        rot_store<V, 1>(lr, t, T, w);
+    } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) lr[o0 + j] = static_cast<int8_t>(w[j / 4] >> (8 * (j % 4)));
+    }
+}
+
 // The same quantizer for launches of many rows: a CTA of T = group / (V R) threads keeps one part's
 // column constants in registers and walks the rows blockIdx.x, blockIdx.x + gridDim.x, ..., with the
-// inputs of the next kRotAhead - 1 rows requested while it transforms the current one.  Thread t holds, for each run k < R, the V
-// consecutive columns o = k T V + t V + j.  Index bits below log2(V) are register bits and the next
-// five lane bits; a block wider than 32 V columns has its higher stages exchanged through shared memory
-// by index, two barriers each.  Column pairs travel as packed float32 pairs (add, sub and fma .rn.f32x2
-// round each lane as the scalar op does).
-//  - The centred, sign-flipped input of a valid column is fma(s, x, -s c) with s = +-1: s x - s c is
-//    s (x - c) exactly, so its one rounding gives s fl(x - c), the reference's value.  A column past the
-//    chunk or past K is +0; the reference negates some of those zeros, which changes no code and no
-//    scale (a zero's sign only reaches the sign of a zero sum, and |v| and rint(v / scale) are the same
-//    for both zeros).
-//  - The codes are those of quant_rotated_lanes_kernel with its check in packed form: t = e e -
-//    (1/4 - 2^-14) with e = q - n is negative when |e| < 0.5 - 2^-14, give or take far less than the
-//    check's margin.  If ptxas fuses the packed product into the packed sums after it, r and e come from
-//    the exact product v inv, which is within 2^-17 of v / scale too, and the argument is unchanged.  A
-//    thread with any other quotient (or a NaN, which fails the check) divides all its values.
-// Needs the vector conditions of quant_rotated_lanes_kernel (16-byte aligned x rows and centers, K and
-// chunk multiples of V, V-byte aligned codes).
+// inputs of the next kRotAhead - 1 rows requested while it transforms the current one.  The centred,
+// sign-flipped input of a valid column is fma(s, x, -s c) with s = +-1: s x - s c is s (x - c) exactly,
+// so its one rounding gives s fl(x - c), the reference's value.  A column past the chunk or past K is
+// +0; the reference negates some of those zeros, which changes no code and no scale (a zero's sign only
+// reaches the sign of a zero sum, and |v| and rint(v / scale) are the same for both zeros).  Needs the
+// vector conditions of quant_rotated_lanes_kernel.
 constexpr int kRotAhead = 3;   // rows of input a thread of quant_rotated_rows_kernel has requested
 
 template <int V, int R>
@@ -480,11 +542,9 @@ __global__ void __launch_bounds__(1024) quant_rotated_rows_kernel(
     float* __restrict__ scales, int M, int K, int chunk, int parts, int group, int block) {
     static_assert(V == 2 || V == 4 || V == 8, "two, four or eight columns per run");
     constexpr int W = V / 2;                  // packed pairs per run
-    constexpr int NW = (R * V + 3) / 4;       // code words per thread
     constexpr uint32_t kHashStep = 1103515245u << 15;
     extern __shared__ float rot_s[];          // two sets of 32 warp maxima, then the group for exchanges
     float* red = rot_s;
-    float* ex = rot_s + 64;
     const int t = threadIdx.x, lane = t & 31, T = blockDim.x, nw = T >> 5;
     const int part = blockIdx.y;
     // the column constants: s = +-1 (bit 16 of the hash, at bit 31 of the hash shifted left by 15) and -s c
@@ -562,114 +622,19 @@ __global__ void __launch_bounds__(1024) quant_rotated_rows_kernel(
 #pragma unroll
                 for (int i = 0; i < W; ++i) in[a][k][i] = in[a + 1][k][i];
         load_row(row + kRotAhead * stride, in[kRotAhead - 1]);
-        // index bit 0 (inside a pair; block >= 2), then the register bits between pairs
-#pragma unroll
-        for (int k = 0; k < R; ++k)
-#pragma unroll
-            for (int i = 0; i < W; ++i) {
-                const float a = f2_lo(p[k][i]), b = f2_hi(p[k][i]);
-                p[k][i] = f2(__fadd_rn(a, b), __fsub_rn(a, b));
-            }
-#pragma unroll
-        for (int dp = 1; dp < W; dp *= 2) {
-            if (2 * dp >= block) break;
-#pragma unroll
-            for (int k = 0; k < R; ++k)
-#pragma unroll
-                for (int i = 0; i < W; ++i) {
-                    if (i & dp) continue;
-                    const uint64_t a = p[k][i], b = p[k][i + dp];
-                    p[k][i] = add2_rn(a, b);
-                    p[k][i + dp] = sub2_rn(a, b);
-                }
-        }
-        // lane bits (index distance V dl): fma(+1, lo, hi) on the low lane, fma(-1, hi, lo) on the high one
-#pragma unroll
-        for (int dl = 1; dl < 32; dl *= 2) {
-            if (V * dl >= block) break;   // the same for the whole CTA
-            const float s = (lane & dl) ? -1.f : 1.f;
-            const uint64_t sg = f2(s, s);
-#pragma unroll
-            for (int k = 0; k < R; ++k)
-#pragma unroll
-                for (int i = 0; i < W; ++i) {
-                    const float a = __shfl_xor_sync(0xffffffffu, f2_lo(p[k][i]), dl);
-                    const float b = __shfl_xor_sync(0xffffffffu, f2_hi(p[k][i]), dl);
-                    p[k][i] = fma2_rn(sg, p[k][i], f2(a, b));
-                }
-        }
-        // wider stages (index distance D >= 32 V) through shared memory
-        for (int D = 32 * V; D < block; D *= 2) {
-#pragma unroll
-            for (int k = 0; k < R; ++k)
-#pragma unroll
-                for (int i = 0; i < W; ++i) *reinterpret_cast<uint64_t*>(ex + (k * T + t) * V + 2 * i) = p[k][i];
-            __syncthreads();
-#pragma unroll
-            for (int k = 0; k < R; ++k) {
-                const int o0 = (k * T + t) * V;
-                const float s = (o0 & D) ? -1.f : 1.f;
-                const uint64_t sg = f2(s, s);
-#pragma unroll
-                for (int i = 0; i < W; ++i)
-                    p[k][i] = fma2_rn(sg, p[k][i], *reinterpret_cast<const uint64_t*>(ex + (o0 ^ D) + 2 * i));
-            }
-            __syncthreads();
-        }
+        rot_stages<V, R>(p, t, T, block, rot_s + 64);
         // the group's maximum: one redux per warp, one barrier (the two sets of maxima alternate by row)
-        float m = 0.f;
-#pragma unroll
-        for (int k = 0; k < R; ++k)
-#pragma unroll
-            for (int i = 0; i < W; ++i) m = fmaxf(m, fmaxf(fabsf(f2_lo(p[k][i])), fabsf(f2_hi(p[k][i]))));
-        const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+        const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(rot_absmax<V, R>(p)));
         if (lane == 0) red[buf * 32 + (t >> 5)] = __uint_as_float(wm);
         __syncthreads();
-        m = __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[buf * 32 + lane]) : 0u));
+        const float m =
+            __uint_as_float(__reduce_max_sync(0xffffffffu, lane < nw ? __float_as_uint(red[buf * 32 + lane]) : 0u));
         buf ^= 1;
         const float scale = __fmul_rn(fmaxf(m, 1.0e-12f), 1.0f / 127.0f);
         if (t == 0) scales[static_cast<size_t>(part) * M + row] = scale;
-        const float inv = __frcp_rn(scale);
-        const uint64_t inv2 = f2(inv, inv), magic2 = f2(12582912.0f, 12582912.0f);
-        const uint64_t lim2 = f2(-(0.25f - 6.103515625e-05f), -(0.25f - 6.103515625e-05f));
-        uint32_t w[NW];
-        uint32_t pend0 = 0u, pend1 = 0u;      // the first two codes of a word still to be completed
-        bool ok = true;
-#pragma unroll
-        for (int k = 0; k < R; ++k)
-#pragma unroll
-            for (int i = 0; i < W; ++i) {
-                const uint64_t q = mul2_rn(p[k][i], inv2);
-                const uint64_t r = add2_rn(q, magic2);
-                const uint64_t e = sub2_rn(q, sub2_rn(r, magic2));
-                const uint64_t tt = fma2_rn(e, e, lim2);
-                ok = ok && f2_lo(tt) < 0.f && f2_hi(tt) < 0.f;
-                const uint32_t c0 = __float_as_uint(f2_lo(r)), c1 = __float_as_uint(f2_hi(r));
-                const int f = k * V + 2 * i;   // flat index of c0 among the thread's codes
-                if (f % 4 == 0) pend0 = c0, pend1 = c1;
-                else w[f / 4] = pack4_low_bytes(pend0, pend1, c0, c1);
-            }
-        if (!ok) {
-#pragma unroll
-            for (int k = 0; k < R; ++k)
-#pragma unroll
-                for (int i = 0; i < W; ++i) {
-                    const uint32_t c0 = static_cast<uint32_t>(__float2int_rn(__fdiv_rn(f2_lo(p[k][i]), scale)));
-                    const uint32_t c1 = static_cast<uint32_t>(__float2int_rn(__fdiv_rn(f2_hi(p[k][i]), scale)));
-                    const int f = k * V + 2 * i;
-                    if (f % 4 == 0) pend0 = c0, pend1 = c1;
-                    else w[f / 4] = pack4_low_bytes(pend0, pend1, c0, c1);
-                }
-        }
-        if constexpr ((R * V) % 4 != 0) w[NW - 1] = pack4_low_bytes(pend0, pend1, 0u, 0u);
-        int8_t* lr = low + static_cast<size_t>(row) * parts * group + static_cast<size_t>(part) * group;
-#pragma unroll
-        for (int k = 0; k < R; ++k) {
-            int8_t* dst = lr + (k * T + t) * V;
-            if constexpr (V == 8) *reinterpret_cast<uint2*>(dst) = make_uint2(w[2 * k], w[2 * k + 1]);
-            else if constexpr (V == 4) *reinterpret_cast<uint32_t*>(dst) = w[k];
-            else *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(w[k / 2] >> (16 * (k % 2)));
-        }
+        uint32_t w[(R * V + 3) / 4];
+        rot_codes<V, R>(p, scale, w);
+        rot_store<V, R>(low + static_cast<size_t>(row) * parts * group + static_cast<size_t>(part) * group, t, T, w);
     }
 }
 
