@@ -457,18 +457,23 @@ def run_down(args, world, rank, local):
         ms = timed(graphs, args.steps)
         clocks = sampler.stop()
         # dominant kernel (the grouped INT8 GEMM) and the quantizer, back to back per bucket
-        per_gemm, per_quant = [], []
+        # (the GEMM as the step runs it, weight stream started before its dependency wait, and once more
+        # as the plain reax_sliced_i8, which waits first)
+        per_gemm, per_gemm_plain, per_quant = [], [], []
         for x in xs:
             M = x.shape[0]
             low, sc = quantize_rotated(x, banks[0].centers, K // P, P, G, B)
             parts_buf = torch.empty(P, M, N, dtype=torch.bfloat16, device=dev)
             reps = 3 * copies
-            gg = graphs_of(lambda c: [sliced_i8(low, banks[r % copies].low_weight, None, None, sc, banks[r % copies].scales,
-                                                banks[r % copies].bias, parts_buf, G, 0, P) for r in range(reps)])
-            per_gemm.append((M, timed(gg, max(2, args.steps // reps)) * 1e-3 / reps))
+            for static, dst in ((True, per_gemm), (False, per_gemm_plain)):
+                gg = graphs_of(lambda c: [sliced_i8(low, banks[r % copies].low_weight, None, None, sc,
+                                                    banks[r % copies].scales, banks[r % copies].bias, parts_buf, G, 0,
+                                                    P, static_weights=static) for r in range(reps)])
+                dst.append((M, timed(gg, max(2, args.steps // reps)) * 1e-3 / reps))
+                del gg
             gq = graphs_of(lambda c: [quantize_rotated(x, banks[r % copies].centers, K // P, P, G, B) for r in range(reps)])
             per_quant.append((M, timed(gq, max(2, args.steps // reps)) * 1e-3 / reps))
-            del gg, gq
+            del gq
         # end to end with host buffers (inputs from pinned memory, outputs back), copies on side streams
         xs_host = [x.pin_memory() for x in xs_cpu]
         outs_host = [torch.empty((x.shape[0], N), dtype=torch.bfloat16).pin_memory() for x in xs_cpu]
@@ -522,6 +527,7 @@ def run_down(args, world, rank, local):
                 "traffic": ncu_traffic("down"),
                 "kernel": "grouped INT8 GEMM (tc_gemm_kernel, plain epilogue, one partial per group)",
                 "per_launch_us": {str(M): round(d * 1e6, 2) for M, d in per_gemm},
+                "per_launch_us_plain": {str(M): round(d * 1e6, 2) for M, d in per_gemm_plain},
                 "quantizer_per_launch_us": {str(M): round(d * 1e6, 2) for M, d in per_quant}}
     cpu = None
     if not args.no_cpu_baseline:

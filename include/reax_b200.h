@@ -188,6 +188,17 @@ REAX_API int reax_sliced_i8(const int8_t* A, const int8_t* W, const void* AH, co
                    const float* sw, const float* bias, void* partials, int M, int N, int G, int HP, int P,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- a11 for weights that the preceding kernel does not write --------------------------------------
+ * No counterpart in the reference: reax_sliced_i8 with the same arguments and requirements, for a
+ * caller that guarantees that the kernel launched just before this one on the stream does not write W
+ * or WH (the usual case: banks are written once and then only read, and the kernel before the
+ * projection is its quantizer).  The GEMM then requests its first weight tiles before it waits for
+ * that kernel, so the weight stream starts under the tail of the previous launch.  A, AH, sa, sw and
+ * bias are still read only after the wait. */
+REAX_API int reax_sliced_i8_static(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa,
+                                   const float* sw, const float* bias, void* partials, int M, int N, int G, int HP,
+                                   int P, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- failure detection -------------------------------------------------------------------------------
  * Runs one kernel that waits on a barrier nothing arrives on, bounded by timeout_ns, and ORs
  * REAX_STATUS_SELFTEST into the workspace status word when the wait expires. */

@@ -49,6 +49,7 @@ SIGNATURES = {
     "reax_gate_up_bf16": ([_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_bf16_partials": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_sliced_i8": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
+    "reax_sliced_i8_static": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_selftest_wait": ([_P, _ULL, _P], _I),
 }
 

@@ -834,9 +834,11 @@ int reax_bf16_partials(const void* x, const void* w, const int32_t* split, void*
     return launch_tc(reax::kEpiPlain, p, grid, s);
 }
 
-int reax_sliced_i8(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa, const float* sw,
-                   const float* bias, void* partials, int M, int N, int G, int HP, int P, void* workspace,
-                   size_t workspace_bytes, void* stream) {
+namespace {
+
+int sliced_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa, const float* sw,
+                     const float* bias, void* partials, int M, int N, int G, int HP, int P, void* workspace,
+                     size_t workspace_bytes, void* stream, int early_b) {
     if (M < 0 || N <= 0 || G <= 0 || HP < 0 || P < 1)
         return fail(REAX_ERR_INVALID, "sliced_i8: bad sizes M=%d N=%d G=%d HP=%d P=%d", M, N, G, HP, P);
     if (G % 128 != 0 || HP % 64 != 0 || N % 256 != 0)
@@ -895,9 +897,26 @@ int reax_sliced_i8(const int8_t* A, const int8_t* W, const void* AH, const void*
     p.ws_partials = ws.partials;
     p.ws_counters = ws.counters;
     p.status = ws.status;
+    p.early_b = early_b;
     int grid = 0;
     plan_schedule(p, info->sms, false, &grid);
     return launch_tc(reax::kEpiPlain, p, grid, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace
+
+int reax_sliced_i8(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa, const float* sw,
+                   const float* bias, void* partials, int M, int N, int G, int HP, int P, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+    return sliced_i8_launch(A, W, AH, WH, sa, sw, bias, partials, M, N, G, HP, P, workspace, workspace_bytes, stream,
+                            0);
+}
+
+int reax_sliced_i8_static(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa,
+                          const float* sw, const float* bias, void* partials, int M, int N, int G, int HP, int P,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+    return sliced_i8_launch(A, W, AH, WH, sa, sw, bias, partials, M, N, G, HP, P, workspace, workspace_bytes, stream,
+                            1);
 }
 
 int reax_selftest_wait(void* workspace, unsigned long long timeout_ns, void* stream) {

@@ -28,8 +28,12 @@ def _next_pow2(n: int) -> int:
     return 1 << max(0, int(n) - 1).bit_length()
 
 
-def sliced_i8(low, w, high, wh, scales, sw, bias, partials, group, hp, parts):
-    """bf16 partials [P, M, N] of a grouped INT8 projection on the current stream."""
+def sliced_i8(low, w, high, wh, scales, sw, bias, partials, group, hp, parts, static_weights=False):
+    """bf16 partials [P, M, N] of a grouped INT8 projection on the current stream.
+
+    ``static_weights=True`` promises that the kernel launched just before this one on the stream does not
+    write ``w`` or ``wh``, so the GEMM may request its first weight tiles before it waits for that kernel
+    (``reax_sliced_i8_static``)."""
     m, n = low.shape[0], w.shape[0]
     _native.require_cuda(low, w, scales, sw, bias, partials)
     for t in (low, w, high, wh, scales, sw, bias, partials):
@@ -37,7 +41,9 @@ def sliced_i8(low, w, high, wh, scales, sw, bias, partials, group, hp, parts):
             raise RuntimeError("sliced: operands must be contiguous")
     with torch.cuda.device(low.device):
         ws = _native.workspace(low.device)
-        _native.check(_native.load().reax_sliced_i8(
+        lib = _native.load()
+        entry = lib.reax_sliced_i8_static if static_weights else lib.reax_sliced_i8
+        _native.check(entry(
             low.data_ptr(), w.data_ptr(), _native.ptr(high) if hp else None, _native.ptr(wh) if hp else None,
             scales.data_ptr(), sw.data_ptr(), bias.data_ptr(), partials.data_ptr(), m, n, int(group), int(hp),
             int(parts), ws.data_ptr(), ws.numel(), _native.stream_handle(low.device)))
@@ -61,7 +67,9 @@ class Native(NativeInt8):
         partials = torch.empty((p.parts, m, n), device=x.device, dtype=x.dtype)
         bm, sm, bn, threads = CONFIGS[name]
         assert n % bn == 0
-        sliced_i8(low, p.low_weight, high, p.high_weight, scales, p.scales, p.bias, partials, p.group, p.hp, p.parts)
+        # the kernel just before the GEMM on the stream is prepare's quantizer, which writes no weights
+        sliced_i8(low, p.low_weight, high, p.high_weight, scales, p.scales, p.bias, partials, p.group, p.hp, p.parts,
+                  static_weights=True)
         if p.parts == 1:
             return partials[0]
         out = torch.empty((m, n), device=x.device, dtype=x.dtype)

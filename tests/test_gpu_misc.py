@@ -114,6 +114,38 @@ def test_sliced_projection(P, G, HP, M, N):
         assert ok.all(), rep
 
 
+@pytest.mark.parametrize("P,G,HP,M,N", [(4, 2304, 0, 1, 2560), (4, 2304, 0, 64, 2560), (2, 512, 64, 130, 768)])
+def test_sliced_static_entry_back_to_back(P, G, HP, M, N):
+    """reax_sliced_i8_static launched back to back (each launch streams its weights under the previous
+    one's tail, over rotating banks) gives the bits of reax_sliced_i8 with no expired wait."""
+    from reax_engine_runtime_v3_b200 import _native
+    from reax_engine_runtime_v3_b200.reaxv2.sliced import sliced_i8
+    g = H.gen(7 * M + P * G + HP + N)
+    dev = torch.device("cuda")
+    low = torch.randint(-127, 128, (M, P * G), generator=g, dtype=torch.int32).to(torch.int8).to(dev)
+    high = (torch.randn(M, P * HP, generator=g)).to(torch.bfloat16).to(dev)
+    sa = (1e-3 + 9e-3 * torch.rand(P, M, generator=g)).to(dev)
+    banks = [dict(w=torch.randint(-127, 128, (N, P * G), generator=g, dtype=torch.int32).to(torch.int8).to(dev),
+                  wh=(torch.randn(N, P * HP, generator=g) * 0.02).to(torch.bfloat16).to(dev),
+                  sw=(1e-3 + 9e-3 * torch.rand(P, N, generator=g)).to(dev),
+                  bias=(torch.randn(P, N, generator=g) * 0.05).to(dev)) for _ in range(2)]
+
+    def run(b, static):
+        out = torch.empty(P, M, N, dtype=torch.bfloat16, device=dev)
+        return sliced_i8(low, b["w"], high, b["wh"], sa, b["sw"], b["bias"], out, G, HP, P, static_weights=static)
+
+    ws = _native.workspace(dev)
+    _native.clear_status(ws)
+    outs = [run(b, True) for b in banks * 4]
+    torch.cuda.synchronize()
+    assert _native.read_status(ws) == 0
+    for i, b in enumerate(banks):
+        plain = run(b, False)
+        torch.cuda.synchronize()
+        for out in outs[i::2]:
+            assert torch.equal(out.view(torch.int16), plain.view(torch.int16))
+
+
 def test_split_gated_projection_out_path():
     from reax_engine_runtime_v3_b200.runtime.split_gated_projection import project_split
     from reax_engine_runtime_v3_b200.reaxv2.sliced import Native
