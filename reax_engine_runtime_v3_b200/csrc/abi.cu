@@ -583,8 +583,8 @@ int reax_quant_rotated(const void* x, const float* centers, int8_t* low, float* 
                                block);
         return e == cudaSuccess ? REAX_OK : cuda_fail(e, "quant_rotated launch");
     }
-    const auto aligned = [](const void* p, int bytes) { return reinterpret_cast<uintptr_t>(p) % bytes == 0; };
-    const bool vec = K % V == 0 && chunk % V == 0 && aligned(x, 16) && aligned(centers, 16) && aligned(low, V);
+    const bool vec = K % V == 0 && chunk % V == 0 && aligned(x, 16) && aligned(centers, 16) &&
+                     aligned(low, static_cast<size_t>(V));
     // Many rows of two-column runs (groups of an odd multiple of 64 columns): persistent CTAs of
     // group / (2 R) threads, each walking rows of one part, three runs per thread when the group is a
     // multiple of 192 columns, so that a thread has six values.  Wider runs measured faster with one CTA
