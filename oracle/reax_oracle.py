@@ -232,13 +232,51 @@ def swiglu_bits(g_bits: np.ndarray, u_bits: np.ndarray, table: np.ndarray | None
 def gate_up_values(a, w, ah_bits, wh_bits, sa, sw, bias):
     """float32 [M, N2] gate|up values before bf16 rounding (native_hybrid8.cu:9-26).
 
-    INT8 part exact (dequant as :23-24).  The BF16 outlier part (:26, accumulated by mma.sync into
-    the dequantized registers) is restated as one float32 add of the float32-rounded dot product.
+    INT8 part exact (dequant as :23-24).  The BF16 outlier part (:26) is accumulated by mma.sync
+    m16n8k16 into the registers that hold the dequantized values, 16 columns per instruction in
+    ascending order (hybrid8_tiles.cuh:454-550): restated as one float32 add per 16-column block of
+    that block's dot product (computed in float64, exact for these products and sums).  The tensor
+    cores' own rounding inside a block is not restated, so this models the association, not the bits.
     """
     v = dequant(int_gemm(a, w), sa, sw, bias)
     if ah_bits is not None and np.asarray(ah_bits).shape[1] > 0:
-        v = (v + bf16_gemm_f32(np.asarray(ah_bits), np.asarray(wh_bits))).astype(F32)
+        v = add_bf16_blocks(v, np.asarray(ah_bits), np.asarray(wh_bits))
     return v
+
+
+def gate_up_ill_conditioned(a, w, ah_bits, wh_bits, sa, sw, bias, slack: float = 2.0 ** -19) -> np.ndarray:
+    """bool [M, N2 // 2]: outputs whose gate or up value is small against the magnitudes summed into it
+    (|dequant| + sum |ah * wh| over the BF16 columns), so that float32 accumulation errors of ``slack``
+    times that magnitude exceed half a bf16 ulp of the value.  Such values can round differently when
+    the order or the rounding of the accumulation differs (tensor cores vs exact block sums)."""
+    v = gate_up_values(a, w, ah_bits, wh_bits, sa, sw, bias).astype(np.float64)
+    mag = np.abs(dequant(int_gemm(a, w), sa, sw, bias).astype(np.float64))
+    if ah_bits is not None and np.asarray(ah_bits).shape[1] > 0:
+        mag = mag + np.abs(bf16_to_f32(np.asarray(ah_bits)).astype(np.float64)) @ \
+            np.abs(bf16_to_f32(np.asarray(wh_bits)).astype(np.float64)).T
+    half_ulp = np.maximum(np.abs(v), 2.0 ** -126) * 2.0 ** -9        # half a bf16 ulp (8 significand bits)
+    bad = slack * mag > half_ulp
+    H = v.shape[1] // 2
+    return bad[:, :H] | bad[:, H:]
+
+
+def add_bf16_blocks(v: np.ndarray, ah_bits: np.ndarray, wh_bits: np.ndarray, block: int = 16) -> np.ndarray:
+    """v (float32 [M, N]) + the BF16 columns' products, one float32 rounding per ``block`` columns in
+    ascending order (the k-chain of the reference's mma.sync.m16n8k16 accumulation)."""
+    a = bf16_to_f32(ah_bits).astype(np.float64)
+    w = bf16_to_f32(wh_bits).astype(np.float64)
+    v = np.asarray(v, F32).copy()
+    for k0 in range(0, a.shape[1], block):
+        v = (v.astype(np.float64) + a[:, k0:k0 + block] @ w[:, k0:k0 + block].T).astype(F32)
+    return v
+
+
+def gate_up_pre_bits(a, w, ah_bits, wh_bits, sa, sw, bias):
+    """(g, u) uint16 bf16 [M, N2 // 2]: the gate and up values as the SwiGLU receives them
+    (hybrid8_tiles.cuh:694-710 rounds each to bf16 first)."""
+    v = gate_up_values(a, w, ah_bits, wh_bits, sa, sw, bias)
+    H = v.shape[1] // 2
+    return f32_to_bf16(v[:, :H]), f32_to_bf16(v[:, H:])
 
 
 def gate_up_product(a, w, ah_bits, wh_bits, sa, sw, bias, table=None):
@@ -284,7 +322,7 @@ def sliced_partials(low, w, high_bits, wh_bits, scales, sw, bias, group, hp, par
         v = dequant(int_gemm(low[:, k0:k1], w[:, k0:k1]), scales[z], sw[z], bias[z])      # :11-27
         if hp > 0:
             h0, h1 = z * hp, (z + 1) * hp
-            v = (v + bf16_gemm_f32(high_bits[:, h0:h1], wh_bits[:, h0:h1])).astype(F32)  # :28-30
+            v = add_bf16_blocks(v, high_bits[:, h0:h1], wh_bits[:, h0:h1])  # :28-30
         out[z] = f32_to_bf16(v)                                                          # :31
     return out
 
@@ -434,3 +472,42 @@ def ulp_distance_bf16(a_bits: np.ndarray, b_bits: np.ndarray) -> np.ndarray:
         mag = b & 0x7FFF
         return np.where(b & 0x8000, -mag, mag)
     return np.abs(key(a_bits) - key(b_bits))
+
+
+# ----------------------------------------------------------------------------- a13: offline bank construction
+
+
+def build_bank(weight_bits, count, col_sum, col_square, col_max, protected):
+    """Restates ``bank(weight, stats, protected)``
+    (private/snapshots/model-exact-addressed-projections-full-r5/earlier_gate_up_screen.py:17-33) in numpy.
+
+    weight_bits uint16 (bf16) [N2, K]; count rows; col_sum, col_square float64 [K] running sums of the
+    activations and their squares; col_max float32 [K] running max |activation|.  Returns a namespace
+    with the bank fields (low/high columns int32, low_weight int8, high_weight uint16 bits, smoothing,
+    centers, scales, bias float32).
+    """
+    from types import SimpleNamespace
+    w = bf16_to_f32(np.asarray(weight_bits, np.uint16))                                # :19 weight.float()
+    mean = (np.asarray(col_sum, np.float64) / count).astype(F32)                       # :18
+    var = np.asarray(col_square, np.float64) / count - mean.astype(np.float64) ** 2    # :19
+    energy = np.sqrt(np.maximum(var, 1e-12).astype(F32))
+    norms = np.sqrt((w.astype(np.float64) ** 2).sum(0).astype(F32))                    # float32 column norms
+    importance = (energy * norms).astype(F32)
+    order = np.argsort(-importance, kind="stable")
+    high = np.sort(order[:protected])                                                  # :20
+    keep = np.ones(w.shape[1], bool)
+    keep[high] = False
+    low = np.nonzero(keep)[0]                                                          # :21-22
+    values = w[:, low]
+    centers = mean[low]                                                                # :23
+    amax = (np.asarray(col_max, F32)[low] + np.abs(centers)).astype(F32)
+    ratio = np.sqrt((np.maximum(amax, F32(1e-8)) / np.maximum(np.abs(values).max(0), F32(1e-8))).astype(F32))  # :24
+    smoothing = np.exp2(np.clip(np.round(np.log2(ratio)), -8, 8)).astype(F32)          # :25
+    scaled = (values * smoothing[None, :]).astype(F32)                                 # :26
+    scales = (np.maximum(np.abs(scaled).max(1), F32(1e-12)) / F32(127.0)).astype(F32)
+    codes = np.clip(np.round((scaled / scales[:, None]).astype(F32)), -127, 127).astype(np.int8)   # :27
+    bias = (values.astype(np.float64) @ centers.astype(np.float64)).astype(F32)        # :28
+    return SimpleNamespace(width=w.shape[1], centered=True, low_columns=low.astype(np.int32),
+                           high_columns=high.astype(np.int32), low_weight=codes,
+                           high_weight=np.asarray(weight_bits, np.uint16)[:, high], smoothing=smoothing,
+                           centers=centers, scales=scales, bias=bias)

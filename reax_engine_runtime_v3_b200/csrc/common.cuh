@@ -15,8 +15,10 @@
 namespace reax {
 
 // ------------------------------------------------------------------------------------------------ status words
-// Bits OR-ed into the caller's device status word when a bounded wait gives up.  The host reads it
-// with reax_read_status(); a kernel that sets one of these has returned early and its output is invalid.
+// Bits OR-ed into the device status word (word 0 of the caller's workspace, or of the allocation-free
+// entry's static scratch) when a bounded wait gives up.  The host reads the workspace word directly and
+// the scratch word with reax_noalloc_status(); a kernel that sets one of these has returned early and
+// its output is invalid.
 enum : uint32_t {
     kStatusTimeoutFull = 1u << 0,      // MMA issuer waited too long for a TMA stage
     kStatusTimeoutEmpty = 1u << 1,     // producer waited too long for a free stage
@@ -253,6 +255,22 @@ REAX_DEVI void tmem_ld2_x16_sync(uint32_t ta, uint32_t tb, uint32_t (&a)[16], ui
         : "r"(ta), "r"(tb)
         : "memory");
 }
+
+// Store 32 consecutive 32-bit columns of this warp's 32 lanes: TMEM[lane base + t][column + i] <- register
+// i of lane t.  tmem_wait_st() makes them complete before the thread goes on (e.g. to signal the MMA
+// issuer, after tc_fence_before()).
+REAX_DEVI void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+REAX_DEVI void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Gate and up accumulators of 2 * PAIRS token columns (8, 16 or 32) with one wait.
 template <int PAIRS>

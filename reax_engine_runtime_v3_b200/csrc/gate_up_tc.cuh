@@ -424,7 +424,10 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     uint64_t* acc_full = empty + kMaxStages;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    // ADD_F: the epilogue has written a tile's dequantized values into the float32 region (one arrival
+    // per epilogue warp), so the MMA issuer may add the BF16 columns' products on top of them
+    uint64_t* deq_ready = drain + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(deq_ready + 1);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     int* last_flag = abort_flag + 1;
     // pipeline stages and the boxes inside them
@@ -452,6 +455,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             mbar_init(&acc_empty[b], EPI_WARPS);
         }
         mbar_init(drain, 1);
+        mbar_init(deq_ready, EPI_WARPS);
         *abort_flag = 0;
         *last_flag = 0;
         fence_mbar_init();
@@ -589,15 +593,22 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             uint32_t phase = 0;
             int buf = 0;
             uint32_t acc_phase = 0;
+            uint32_t deq_phase = 0;
             Cursor cur = cursor_init(p);
             Segment seg;
             bool ok = true;
             while (ok && cursor_next(p, split, cur, seg)) {
-                if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1, p.timeout_ns, vabort)) {
-                    if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutAccEmpty);
-                    break;
+                // ADD_F: the INT8 region is free once the epilogue has dequantized the previous tile out of
+                // it (the deq_ready wait before that tile's BF16 MMAs), so the next tile's INT8 MMAs run
+                // under the previous tile's BF16 MMAs and epilogue; the float32 region is reused only after
+                // the next deq_ready, which the epilogue signals after it has read that region.
+                if constexpr (!ADD_F) {
+                    if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1, p.timeout_ns, vabort)) {
+                        if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutAccEmpty);
+                        break;
+                    }
+                    tc_fence_after();
                 }
-                tc_fence_after();
                 const uint32_t d_int = tmem_base + buf * kBN;
                 const uint32_t d_f32 = (MODE == 1) ? tmem_base + buf * kBN : tmem_base + kBN;
                 const int first_f = max(seg.k0, p.kb_int);
@@ -623,9 +634,24 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             }
                         }
                     } else {
+                        if constexpr (ADD_F) {
+                            // The BF16 columns add into the dequantized values, 16 columns per MMA in
+                            // ascending order, as the reference's mma.sync chain adds them into its
+                            // dequantized registers (native_hybrid8.cu:26, hybrid8_tiles.cuh:454-550):
+                            // wait until the epilogue has stored those values in the float32 region.
+                            if (kb == p.kb_int) {
+                                if (!mbar_wait_bounded(deq_ready, deq_phase, p.timeout_ns, vabort)) {
+                                    if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutAccEmpty);
+                                    ok = false;
+                                    break;
+                                }
+                                deq_phase ^= 1;
+                                tc_fence_after();
+                            }
+                        }
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
-                            const uint32_t acc = (kb > first_f || k > 0) ? 1u : 0u;
+                            const uint32_t acc = (ADD_F || kb > first_f || k > 0) ? 1u : 0u;
                             if constexpr (SWAP) {
                                 umma_f16(d_f32, bd + 2 * k, ad + 2 * k, idesc_f16, acc);
                                 umma_f16(d_f32 + p.n_tok, bd_up + 2 * k, ad + 2 * k, idesc_f16, acc);
@@ -635,13 +661,15 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         }
                     }
                     umma_commit(&empty[stage]);
+                    // ADD_F: the INT8 accumulators of the tile are complete
+                    if (ADD_F && kb == p.kb_int - 1) umma_commit(&acc_full[0]);
                     if (++stage == ns) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (!ok) break;
-                umma_commit(&acc_full[buf]);
+                umma_commit(&acc_full[ADD_F ? 1 : buf]);
                 if (p.acc_bufs == 2) {
                     buf ^= 1;
                     if (buf == 0) acc_phase ^= 1;
@@ -935,23 +963,55 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     finish = publish_partial<EPI_WARPS, 32>(p, seg, st, t_int, c_lo, c_hi, up_off, r_tile, row_ok,
                                                             last_flag);
                 }
+                constexpr bool add_f = (MODE == 0 && ADD_F);
+                const uint64_t sa2 = f2(sa_row, sa_row);
+                if constexpr (add_f) {
+                    // Dequantize the INT8 accumulators into the float32 region, where the MMA issuer then
+                    // adds the BF16 columns' products on top (tiles with BF16 columns are never split).
+                    // Rows past the tile's rows and columns past c_end get values that are never stored.
+                    for (int cc = c_lo; cc < c_hi; cc += 32) {
+                        if (cc >= c_end) break;   // the same for the whole CTA
+                        for (int h = 0; h < (EPI == kEpiSwiglu ? 2 : 1); ++h) {
+                            const int col = cc + h * up_off;   // TMEM column; its scales sit at s_sw[cc + h * kBN / 2]
+                            const int sc = cc + h * (kBN / 2);
+                            uint32_t a[32];
+                            tmem_ld_x32_sync(t_int + col, a);
+#pragma unroll
+                            for (int i = 0; i < 32; i += 2) {
+                                const int si = (EPI == kEpiSwiglu ? sc : col) + i;
+                                const uint64_t v = dequant2(a[i], a[i + 1], sa2, *reinterpret_cast<const uint64_t*>(s_sw + si),
+                                                            *reinterpret_cast<const uint64_t*>(s_bias + si));
+                                a[i] = static_cast<uint32_t>(v);
+                                a[i + 1] = static_cast<uint32_t>(v >> 32);
+                            }
+                            tmem_st_x32(t_f32 + col, a);
+                        }
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(deq_ready);
+                    if (!mbar_wait_bounded(&acc_full[1], acc_phase, p.timeout_ns, nullptr)) {
+                        raise_error(p, abort_flag, kStatusTimeoutAccFull);
+                        break;
+                    }
+                    tc_fence_after();
+                }
                 if (finish) {
                     const int4* contrib[kMaxContrib];
                     const int n_contrib = whole ? 0 : contributors(p, st, contrib);
-                    constexpr bool add_f = (MODE == 0 && ADD_F);
-                    const uint64_t sa2 = f2(sa_row, sa_row);
+                    // float32 values to round: BF16-only accumulators, or the dequantized values with the
+                    // BF16 columns added (ADD_F)
+                    constexpr bool f32_vals = (MODE == 1 || add_f);
+                    const uint32_t t_rd = add_f ? t_f32 : t_acc;
                     for (int cc = c_lo; cc < c_hi; cc += 32) {
                         if (cc >= c_end) break;   // the same for the whole CTA
                         uint32_t g[32];
                         uint32_t u[32];
-                        uint32_t fg[32];
-                        uint32_t fu[32];
                         if constexpr (EPI == kEpiSwiglu) {
-                            tmem_ld2_x32_sync(t_acc + cc, t_acc + up_off + cc, g, u);
-                            if constexpr (add_f) tmem_ld2_x32_sync(t_f32 + cc, t_f32 + up_off + cc, fg, fu);
+                            tmem_ld2_x32_sync(t_rd + cc, t_rd + up_off + cc, g, u);
                         } else {
-                            tmem_ld_x32_sync(t_acc + cc, g);
-                            if constexpr (add_f) tmem_ld_x32_sync(t_f32 + cc, fg);
+                            tmem_ld_x32_sync(t_rd + cc, g);
                         }
                         // whole warps outside the tile's rows skip; the others stay converged for the SiLU's
                         // warp vote, and only their stores and partial sums are per row
@@ -968,17 +1028,13 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 #pragma unroll
                             for (int i = 0; i < 32; i += 2) {
                                 uint64_t vg, vu;
-                                if constexpr (MODE == 0) {
+                                if constexpr (!f32_vals) {
                                     const uint64_t swg = *reinterpret_cast<const uint64_t*>(s_sw + cc + i);
                                     const uint64_t swu = *reinterpret_cast<const uint64_t*>(s_sw + kBN / 2 + cc + i);
                                     const uint64_t bgv = *reinterpret_cast<const uint64_t*>(s_bias + cc + i);
                                     const uint64_t buv = *reinterpret_cast<const uint64_t*>(s_bias + kBN / 2 + cc + i);
                                     vg = dequant2(g[i], g[i + 1], sa2, swg, bgv);
                                     vu = dequant2(u[i], u[i + 1], sa2, swu, buv);
-                                    if constexpr (add_f) {
-                                        vg = add2_rn(vg, f2(__uint_as_float(fg[i]), __uint_as_float(fg[i + 1])));
-                                        vu = add2_rn(vu, f2(__uint_as_float(fu[i]), __uint_as_float(fu[i + 1])));
-                                    }
                                 } else {
                                     vg = f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1]));
                                     vu = f2(__uint_as_float(u[i]), __uint_as_float(u[i + 1]));
@@ -992,11 +1048,10 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 #pragma unroll
                             for (int i = 0; i < 32; i += 2) {
                                 uint64_t v;
-                                if constexpr (MODE == 0) {
+                                if constexpr (!f32_vals) {
                                     const uint64_t s2 = *reinterpret_cast<const uint64_t*>(s_sw + cc + i);
                                     const uint64_t b2 = *reinterpret_cast<const uint64_t*>(s_bias + cc + i);
                                     v = dequant2(g[i], g[i + 1], sa2, s2, b2);
-                                    if constexpr (add_f) v = add2_rn(v, f2(__uint_as_float(fg[i]), __uint_as_float(fg[i + 1])));
                                 } else {
                                     v = f2(__uint_as_float(g[i]), __uint_as_float(g[i + 1]));
                                 }
