@@ -154,10 +154,21 @@ REAX_API int reax_project_i8(const void* x, const int32_t* low_columns, const in
  * The first call on a device resolves the array's device address (cudaGetSymbolAddress) and should
  * come before any stream capture.  All calls share the array and each call clears its status word
  * and counters, so calls that overlap on the GPU (other streams, other threads) race: serialize them.
+ * A bounded wait that expires inside the kernel is recorded in the array's status word (the
+ * REAX_STATUS_* bits below; the output of that call is then invalid): read it with
+ * reax_noalloc_status() before the next call clears it.
  * Arguments and requirements as reax_gate_up_i8, without workspace / workspace_bytes. */
 REAX_API int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, const void* WH,
                                      const float* sa, const float* sw, const float* bias, void* out, int M, int N2,
                                      int KL, int KH, int ldo, void* stream);
+
+/* Status word of reax_gate_up_i8_noalloc's static scratch on the current device, after the work queued
+ * on `stream` so far (this call synchronizes `stream`, so it is not for use inside stream capture):
+ * 0, or the REAX_STATUS_* bits of the last allocation-free call whose bounded wait expired.  The word
+ * is shared by every allocation-free call on the device; each such call clears it when it starts, and
+ * `clear` != 0 clears it here after reading.  No counterpart in the reference (the allocation-free
+ * entry point has none). */
+REAX_API int reax_noalloc_status(unsigned* status, int clear, void* stream);
 
 /* ---- a12 (fused): BF16-weight gate/up GEMM + SwiGLU, unsplit plan ------------------------------------
  * The mixed-origin BF16 projection with parts = 1 on both origins (runtime/mixed_origin_bf16.py:19-48:
@@ -201,7 +212,8 @@ REAX_API int reax_sliced_i8_static(const int8_t* A, const int8_t* W, const void*
 
 /* ---- failure detection -------------------------------------------------------------------------------
  * Runs one kernel that waits on a barrier nothing arrives on, bounded by timeout_ns, and ORs
- * REAX_STATUS_SELFTEST into the workspace status word when the wait expires. */
+ * REAX_STATUS_SELFTEST into the status word at `workspace` (a GEMM workspace, or NULL for the status word
+ * of reax_gate_up_i8_noalloc's static scratch on the current device) when the wait expires. */
 REAX_API int reax_selftest_wait(void* workspace, unsigned long long timeout_ns, void* stream);
 
 #ifdef __cplusplus

@@ -51,6 +51,7 @@ SIGNATURES = {
     "reax_sliced_i8": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_sliced_i8_static": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_selftest_wait": ([_P, _ULL, _P], _I),
+    "reax_noalloc_status": ([C.POINTER(C.c_uint), _I, _P], _I),
 }
 
 _lib = None
@@ -130,6 +131,14 @@ def workspace(device: torch.device) -> torch.Tensor:
 def read_status(ws: torch.Tensor) -> int:
     """Device status word of a workspace (synchronizes); non-zero means a bounded wait expired."""
     return int(ws[:4].view(torch.int32).item())
+
+
+def noalloc_status(clear: bool = False) -> int:
+    """Status word of the allocation-free entry point's static scratch on the current device, after the
+    current stream's work (synchronizes that stream)."""
+    v = C.c_uint(0)
+    check(load().reax_noalloc_status(C.byref(v), 1 if clear else 0, stream_handle()))
+    return int(v.value)
 
 
 def clear_status(ws: torch.Tensor) -> None:

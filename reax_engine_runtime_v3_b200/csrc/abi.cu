@@ -417,51 +417,49 @@ int noalloc_scratch(int dev, void** out) {
     return REAX_OK;
 }
 
-// reax_gate_up_i8 with the option of requesting the first weight tiles before the dependency wait.
-int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa, const float* sw,
-                      const float* bias, void* out, int M, int N2, int KL, int KH, int ldo, void* workspace,
-                      size_t workspace_bytes, void* stream, int early_b) {
+// Argument checks shared by the INT8 gate/up entry points (the reference's asserts, reaxv2/gate_up.py:14,
+// plus the kernels' alignment needs).  *empty: M == 0, nothing to launch.
+int check_gate_up_args(const char* who, const int8_t* A, const int8_t* W, const void* AH, const void* WH,
+                       const float* sa, const float* sw, const float* bias, const void* out, int M, int N2, int KL,
+                       int KH, int ldo, bool* empty) {
+    *empty = false;
     if (M < 0 || N2 <= 0 || KL < 0 || KH < 0 || KL + KH == 0)
-        return fail(REAX_ERR_INVALID, "gate_up_i8: bad sizes M=%d N2=%d KL=%d KH=%d", M, N2, KL, KH);
+        return fail(REAX_ERR_INVALID, "%s: bad sizes M=%d N2=%d KL=%d KH=%d", who, M, N2, KL, KH);
     if (KL % 128 != 0 || KH % 64 != 0 || N2 % 256 != 0)
-        return fail(REAX_ERR_INVALID, "gate_up_i8: needs KL %% 128 == 0, KH %% 64 == 0, N2 %% 256 == 0 (KL=%d KH=%d N2=%d)",
-                    KL, KH, N2);
-    if (ldo < N2 / 2 || ldo % 8 != 0) return fail(REAX_ERR_INVALID, "gate_up_i8: ldo=%d (needs >= N2/2, %% 8 == 0)", ldo);
-    if (KL == 0) return fail(REAX_ERR_INVALID, "gate_up_i8: KL must be > 0 (the INT8 part of the bank is empty)");
-    if (M == 0) return REAX_OK;
-    if (!out || !sw || !bias || (KL && (!A || !W || !sa)) || (KH && (!AH || !WH)))
-        return fail(REAX_ERR_INVALID, "gate_up_i8: NULL pointer argument");
+        return fail(REAX_ERR_INVALID, "%s: needs KL %% 128 == 0, KH %% 64 == 0, N2 %% 256 == 0 (KL=%d KH=%d N2=%d)",
+                    who, KL, KH, N2);
+    if (ldo < N2 / 2 || ldo % 8 != 0) return fail(REAX_ERR_INVALID, "%s: ldo=%d (needs >= N2/2, %% 8 == 0)", who, ldo);
+    if (KL == 0) return fail(REAX_ERR_INVALID, "%s: KL must be > 0 (the INT8 part of the bank is empty)", who);
+    if (M == 0) {
+        *empty = true;
+        return REAX_OK;
+    }
+    if (!out || !sw || !bias || !A || !W || !sa || (KH && (!AH || !WH)))
+        return fail(REAX_ERR_INVALID, "%s: NULL pointer argument", who);
     if (!aligned(A, 16) || !aligned(W, 16) || !aligned(AH, 16) || !aligned(WH, 16) || !aligned(sw, 16) ||
         !aligned(bias, 16) || !aligned(out, 16))
-        return fail(REAX_ERR_ALIGN, "gate_up_i8: operands, sw, bias and out must be 16-byte aligned");
-    int dev;
-    DeviceInfo* info;
-    int rc = current_device(&dev, &info);
-    if (rc != REAX_OK) return rc;
-    Workspace ws;
-    if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
+        return fail(REAX_ERR_ALIGN, "%s: operands, sw, bias and out must be 16-byte aligned", who);
+    return REAX_OK;
+}
 
-    reax::TcParams p;
+// Tile plan, tensor maps and operands of an INT8 gate/up launch (everything but the scratch pointers,
+// early_b and the schedule), shared by the workspace and the allocation-free entry points so that both
+// run the same kernel on the same plan.  *split_ok: whether the plan may split tiles by K.
+int fill_gate_up_params(reax::TcParams& p, int sms, const int8_t* A, const int8_t* W, const void* AH, const void* WH,
+                        const float* sa, const float* sw, const float* bias, void* out, int M, int N2, int KL, int KH,
+                        int ldo, bool* split_ok) {
     init_params(p);
     // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
-    bool split_ok = false;
-    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, info->sms, &split_ok);
-    if (KL) {
-        if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
-            return rc;
-        if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, p.tile_rows)) !=
-            REAX_OK)
-            return rc;
-    }
+    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, sms, split_ok);
+    int rc;
+    if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
+        return rc;
+    if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, p.tile_rows)) != REAX_OK) return rc;
     if (KH) {
         if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH, p.a_rows)) != REAX_OK) return rc;
-        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH, p.tile_rows)) != REAX_OK) return rc;
-    }
-    if (!KL) {
-        p.tm_a = p.tm_ah;
-        p.tm_b = p.tm_bh;
-    }
-    if (!KH) {
+        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH, p.tile_rows)) != REAX_OK)
+            return rc;
+    } else {
         p.tm_ah = p.tm_a;
         p.tm_bh = p.tm_b;
     }
@@ -479,10 +477,30 @@ int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const vo
     p.tiles = p.m_tiles * p.n_tiles;
     p.mode = 0;
     p.acc_bufs = KH ? 1 : 2;
+    p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
+    return REAX_OK;
+}
+
+// reax_gate_up_i8 with the option of requesting the first weight tiles before the dependency wait.
+int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa, const float* sw,
+                      const float* bias, void* out, int M, int N2, int KL, int KH, int ldo, void* workspace,
+                      size_t workspace_bytes, void* stream, int early_b) {
+    bool empty = false;
+    int rc = check_gate_up_args("gate_up_i8", A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &empty);
+    if (rc != REAX_OK || empty) return rc;
+    int dev;
+    DeviceInfo* info;
+    if ((rc = current_device(&dev, &info)) != REAX_OK) return rc;
+    Workspace ws;
+    if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
+    reax::TcParams p;
+    bool split_ok = false;
+    if ((rc = fill_gate_up_params(p, info->sms, A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &split_ok)) !=
+        REAX_OK)
+        return rc;
     p.ws_partials = ws.partials;
     p.ws_counters = ws.counters;
     p.status = ws.status;
-    p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
     p.early_b = early_b;
     int grid = 0;
     plan_schedule(p, info->sms, split_ok, &grid);
@@ -920,11 +938,13 @@ int reax_sliced_i8_static(const int8_t* A, const int8_t* W, const void* AH, cons
 }
 
 int reax_selftest_wait(void* workspace, unsigned long long timeout_ns, void* stream) {
-    if (!workspace || !aligned(workspace, 256)) return fail(REAX_ERR_WORKSPACE, "selftest_wait: bad workspace");
+    if (workspace && !aligned(workspace, 256)) return fail(REAX_ERR_WORKSPACE, "selftest_wait: bad workspace");
     int dev;
     DeviceInfo* info;
     int rc = current_device(&dev, &info);
     if (rc != REAX_OK) return rc;
+    // NULL: the allocation-free entry point's status word, so that its reporting path can be exercised
+    if (!workspace && (rc = noalloc_scratch(dev, &workspace)) != REAX_OK) return rc;
     return launch_plain("selftest_wait launch", reax::selftest_wait_kernel, dim3(1), dim3(32),
                         static_cast<cudaStream_t>(stream), static_cast<unsigned*>(workspace), timeout_ns);
 }
@@ -932,68 +952,25 @@ int reax_selftest_wait(void* workspace, unsigned long long timeout_ns, void* str
 int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, const void* WH, const float* sa,
                             const float* sw, const float* bias, void* out, int M, int N2, int KL, int KH, int ldo,
                             void* stream) {
-    if (M < 0 || N2 <= 0 || KL < 0 || KH < 0 || KL + KH == 0)
-        return fail(REAX_ERR_INVALID, "gate_up_i8_noalloc: bad sizes M=%d N2=%d KL=%d KH=%d", M, N2, KL, KH);
-    if (KL % 128 != 0 || KH % 64 != 0 || N2 % 256 != 0)
-        return fail(REAX_ERR_INVALID,
-                    "gate_up_i8_noalloc: needs KL %% 128 == 0, KH %% 64 == 0, N2 %% 256 == 0 (KL=%d KH=%d N2=%d)", KL,
-                    KH, N2);
-    if (ldo < N2 / 2 || ldo % 8 != 0)
-        return fail(REAX_ERR_INVALID, "gate_up_i8_noalloc: ldo=%d (needs >= N2/2, %% 8 == 0)", ldo);
-    if (KL == 0) return fail(REAX_ERR_INVALID, "gate_up_i8_noalloc: KL must be > 0");
-    if (M == 0) return REAX_OK;
-    if (!out || !sw || !bias || !A || !W || !sa || (KH && (!AH || !WH)))
-        return fail(REAX_ERR_INVALID, "gate_up_i8_noalloc: NULL pointer argument");
-    if (!aligned(A, 16) || !aligned(W, 16) || !aligned(AH, 16) || !aligned(WH, 16) || !aligned(sw, 16) ||
-        !aligned(bias, 16) || !aligned(out, 16))
-        return fail(REAX_ERR_ALIGN, "gate_up_i8_noalloc: operands, sw, bias and out must be 16-byte aligned");
+    bool empty = false;
+    int rc = check_gate_up_args("gate_up_i8_noalloc", A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &empty);
+    if (rc != REAX_OK || empty) return rc;
     int dev;
     DeviceInfo* info;
-    int rc = current_device(&dev, &info);
-    if (rc != REAX_OK) return rc;
+    if ((rc = current_device(&dev, &info)) != REAX_OK) return rc;
     void* scratch = nullptr;
     if ((rc = noalloc_scratch(dev, &scratch)) != REAX_OK) return rc;
-
     reax::TcParams p;
-    init_params(p);
     bool split_ok = false;
-    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, info->sms, &split_ok);
-    if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
+    if ((rc = fill_gate_up_params(p, info->sms, A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &split_ok)) !=
+        REAX_OK)
         return rc;
-    if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, p.tile_rows)) != REAX_OK)
-        return rc;
-    if (KH) {
-        if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH, p.a_rows)) != REAX_OK) return rc;
-        if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH, p.tile_rows)) != REAX_OK) return rc;
-    } else {
-        p.tm_ah = p.tm_a;
-        p.tm_bh = p.tm_b;
-    }
-    p.sa = sa;
-    p.sw = sw;
-    p.bias = bias;
-    p.out = static_cast<__nv_bfloat16*>(out);
-    p.M = M;
-    p.H = N2 / 2;
-    p.ldo = ldo;
-    p.kb_int = KL / 128;
-    p.kb_f16 = KH / 64;
-    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
-    p.n_tiles = (N2 / 2 + p.tile_rows - 1) / p.tile_rows;
-    p.tiles = p.m_tiles * p.n_tiles;
-    p.mode = 0;
-    p.acc_bufs = KH ? 1 : 2;
-    p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
     // Whole-tile plans need no partials; a plan that splits tiles is re-planned for at most
     // kNoAllocMaxCtas CTAs, whose partials the static scratch holds.
     int grid = 0;
     plan_schedule(p, info->sms, split_ok, &grid);
-    int ctas = grid;
-    if (p.sk_iters > 0 && grid > kNoAllocMaxCtas) {
-        plan_schedule(p, kNoAllocMaxCtas, true, &grid);
-        ctas = grid;
-    }
-    const int slots = p.sk_iters > 0 ? ctas : 0;
+    if (p.sk_iters > 0 && grid > kNoAllocMaxCtas) plan_schedule(p, kNoAllocMaxCtas, true, &grid);
+    const int slots = p.sk_iters > 0 ? grid : 0;
     const size_t counter_bytes = ((static_cast<size_t>(2 * (slots > 0 ? slots : 1)) * sizeof(int)) + 255) / 256 * 256;
     const size_t need = kStatusBytes + counter_bytes + static_cast<size_t>(slots) * 2 * reax::kSlotInts * sizeof(int);
     if (need > kNoAllocScratchBytes)
@@ -1008,6 +985,21 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     const cudaError_t e = cudaMemsetAsync(scratch, 0, kStatusBytes + counter_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "gate_up_i8_noalloc: clearing the scratch");
     return launch_tc(reax::kEpiSwiglu, p, grid, s);
+}
+
+int reax_noalloc_status(unsigned* status, int clear, void* stream) {
+    if (!status) return fail(REAX_ERR_INVALID, "noalloc_status: NULL status pointer");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    void* scratch = nullptr;
+    if ((rc = noalloc_scratch(dev, &scratch)) != REAX_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(status, scratch, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess && clear) e = cudaMemsetAsync(scratch, 0, sizeof(unsigned), s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? REAX_OK : cuda_fail(e, "noalloc_status");
 }
 
 }  // extern "C"
