@@ -13,9 +13,15 @@ replayed.  Timing: W warm-up steps, then exactly K graph replays between barrier
 CUDA events on the launching stream, max over ranks.  Three copies of
 the weights rotate between steps (3 x 117 MB > 126 MB L2), so no step finds its weights in L2.
 
+The one-GPU cfg2 line also carries two records outside ``value``: ``prefill`` (the
+INT8-TOPS half of the metric, through the same public API, with the GEMM's TOP/s against a live
+``torch._int_mm`` measurement, twice the measured bf16 peak and the 4.5 POP/s datasheet figure) and
+``ref_kernel`` (the reference's own GPU implementation, its Triton quantizer and its native_hybrid8
+kernel built from source, timed per call on the same buckets and weights, next to ours).
+
 ``--impl reference`` times the reference arithmetic of the path on the host cores (the reference
 ships no CPU implementation of it; the timed code is the oracle's restatement, ``oracle/``), on
-rank 0 only, on a bounded sample of the same workload.
+rank 0 only: every bucket, every output column, one pass per step.
 """
 from __future__ import annotations
 
@@ -67,6 +73,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--measure-int8-peak", action="store_true", help="print torch._int_mm int8 throughput and exit")
+    ap.add_argument("--no-side-records", action="store_true",
+                    help="skip the prefill and reference-kernel records of the one-GPU cfg2 line")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     return a
@@ -255,46 +263,60 @@ def barrier(world):
 
 
 # -------------------------------------------------------------------------------------------------- CPU legs
-def cpu_run(name: str, budget_s: float = 12.0):
-    """Time the oracle's restatement of the path on the host cores over a bounded sample of the
-    workload (all buckets, a slice of the output columns); returns tokens/s scaled to full width."""
-    from oracle import reax_oracle as ro
-    buckets, K, H, kind, srange, _ = WORKLOADS[name]
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    g = np.random.default_rng(7)
-    cols = min(H, 1024)
-    if srange is None:
-        w = (g.standard_normal((2 * cols, K)) * 0.02).astype(np.float32)
-        wb = ro.f32_to_bf16(w)
-    else:
-        w = g.integers(-127, 128, (2 * cols, K), dtype=np.int8)
-        sw = (1e-3 + 9e-3 * g.random(2 * cols)).astype(np.float32)
-        from types import SimpleNamespace
-        bank = SimpleNamespace(low_columns=np.arange(K), high_columns=np.zeros(0, np.int64), smoothing=np.ones(K, np.float32),
-                               centers=np.zeros(K, np.float32), centered=False, low_weight=w,
-                               high_weight=np.zeros((2 * cols, 0), np.uint16), scales=sw, bias=np.zeros(2 * cols, np.float32))
-    xs = [ro.f32_to_bf16(g.standard_normal((M, K)).astype(np.float32)) for M in buckets]
-    # cap rows so one pass stays bounded on the biggest prefill buckets
-    max_rows = 512
-    xs = [x[:max_rows] for x in xs]
-    tokens = sum(len(x) for x in xs)
-    t0 = time.perf_counter()
-    passes = 0
-    while True:
-        for x in xs:
-            if srange is None:
-                ro.gate_up_bf16(x, wb, 0, dict(parts=1, chunk=K), dict(parts=1, chunk=K))
+class CpuSample:
+    """The oracle's restatement of the path (the reference ships no CPU implementation of it) on the
+    host cores: every bucket of the workload, all output columns, rows capped at 512 per bucket on the
+    prefill buckets.  One pass = one step of that sample."""
+
+    MAX_ROWS = 512
+
+    def __init__(self, name: str):
+        from oracle import reax_oracle as ro
+        self.ro = ro
+        buckets, K, H, kind, srange, _ = WORKLOADS[name]
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        g = np.random.default_rng(7)
+        self.int8 = srange is not None
+        self.K = K
+        if self.int8:
+            from types import SimpleNamespace
+            w = g.integers(-127, 128, (2 * H, K), dtype=np.int8)
+            sw = (1e-3 + 9e-3 * g.random(2 * H)).astype(np.float32)
+            self.bank = SimpleNamespace(low_columns=np.arange(K), high_columns=np.zeros(0, np.int64),
+                                        smoothing=np.ones(K, np.float32), centers=np.zeros(K, np.float32),
+                                        centered=False, low_weight=w, high_weight=np.zeros((2 * H, 0), np.uint16),
+                                        scales=sw, bias=np.zeros(2 * H, np.float32))
+        else:
+            self.wb = ro.f32_to_bf16((g.standard_normal((2 * H, K)) * 0.02).astype(np.float32))
+        self.xs = [ro.f32_to_bf16(g.standard_normal((min(M, self.MAX_ROWS), K)).astype(np.float32)) for M in buckets]
+        self.tokens = sum(len(x) for x in self.xs)
+        self.H = H
+
+    def one_pass(self) -> float:
+        t0 = time.perf_counter()
+        for x in self.xs:
+            if self.int8:
+                self.ro.gate_up_project(x, self.bank)
             else:
-                ro.gate_up_project(x, bank)
+                self.ro.gate_up_bf16(x, self.wb, 0, dict(parts=1, chunk=self.K), dict(parts=1, chunk=self.K))
+        return time.perf_counter() - t0
+
+    def describe(self, passes: int, seconds: float) -> str:
+        return (f"{passes} passes over buckets {[len(x) for x in self.xs]} rows x all {self.H} output columns, "
+                f"{seconds:.1f} s")
+
+
+def cpu_run(name: str, budget_s: float = 12.0):
+    """Tokens/s of the CPU port over a bounded sample of the workload (CpuSample), as many passes as fit
+    in the budget (at most 50)."""
+    sample = CpuSample(name)
+    sample.one_pass()                      # first-touch of the weights
+    passes, total = 0, 0.0
+    while total < budget_s and passes < 50:
+        total += sample.one_pass()
         passes += 1
-        if time.perf_counter() - t0 > budget_s or passes >= 50:
-            break
-    dt = time.perf_counter() - t0
-    tok_s = tokens * passes / dt * (cols / H)
-    sample = (f"{passes} passes over buckets {list(len(x) for x in xs)} rows x {cols}/{H} output columns "
-              f"(scaled to full width), {dt:.1f} s")
-    return tok_s, threads, sample
+    return sample.tokens * passes / total, sample.threads, sample.describe(passes, total)
 
 
 def run_reference(args, world, rank):
@@ -303,21 +325,20 @@ def run_reference(args, world, rank):
     if args.workload == "down":
         return run_down_reference(args)
     buckets, K, H, kind, srange, desc = WORKLOADS[args.workload]
-    times = []
-    tok_s = None
-    threads = os.cpu_count() or 1
-    sample = ""
-    for i in range(args.warmup + args.steps):
-        budget = 1.5 if args.steps > 20 else 4.0
-        v, threads, sample = cpu_run(args.workload, budget_s=budget)
-        if i >= args.warmup:
-            times.append(v)
-    tok_s = statistics.median(times)
+    sample = CpuSample(args.workload)
+    for _ in range(args.warmup):
+        sample.one_pass()
+    times = [sample.one_pass() for _ in range(args.steps)]
+    ms = statistics.median(times) * 1e3
+    tok_s = sample.tokens / (ms * 1e-3)
+    desc_sample = sample.describe(args.steps, sum(times)) + " (median pass is the step)"
     line = {"impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sum(buckets) / tok_s * 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "s8" if srange else "bf16",
-            "data": "synthetic", "config": {"workload": desc, "parallelism": "host cores"},
-            "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "data": "synthetic", "config": {"workload": desc, "parallelism": "host cores",
+                                            "tokens_per_step": sample.tokens},
+            "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": sample.threads, "kind": "port",
+                             "sample": desc_sample},
             "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -550,6 +571,120 @@ def run_down(args, world, rank, local):
     return 0
 
 
+# ------------------------------------------------------------------------------ side records of the cfg2 line
+def graph_time(fn, reps, n_rep, cap):
+    """Seconds per call of fn(0), ..., fn(reps - 1) captured back to back in one CUDA graph on stream
+    `cap` and replayed n_rep times (CUDA events on `cap`).  Call with `cap` current."""
+    fn(0)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=cap):
+        for r in range(reps):
+            fn(r)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(cap)
+    for _ in range(n_rep):
+        g.replay()
+    e1.record(cap)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e-3 / (n_rep * reps)
+
+
+def int_mm_tops(n=8192, tries=5):
+    """Dense INT8 tensor throughput on this GPU now: torch._int_mm at n^3, best of `tries` (CUDA events)."""
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t()
+    for _ in range(2):
+        torch._int_mm(a, b)
+    best = None
+    for _ in range(tries):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) * 1e-3
+        best = t if best is None else min(best, t)
+    del a, b
+    return 2 * n ** 3 / best / 1e12
+
+
+def prefill_record(banks, dev, cap, steps):
+    """BASELINE config 3 (the INT8-TOPS half of the metric) through the public API, on the cfg2 weight
+    copies (same K, H and weight distribution): X bf16 [4096, 4096] ~ N(0,1).  Per call of
+    gate_up.Native.project (quantize + gate/up), per GEMM launch and per quantizer launch, with the GEMM's
+    TOP/s against three denominators."""
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native, gate_up_i8, quantize_rows
+    _, K, H, _, _, desc = WORKLOADS["cfg3"]
+    M = 4096
+    gx = torch.Generator().manual_seed(20261201)
+    x = torch.randn(M, K, generator=gx).to(torch.bfloat16).to(dev)
+    nat = Native(None)
+    copies = len(banks)
+    n_rep = max(3, steps // copies)
+    with torch.cuda.stream(cap):
+        call = graph_time(lambda r: nat.project(x, banks[r % copies], "hybrid8_b128n256_s64n256"), copies, n_rep, cap)
+        low, high, sc = quantize_rows(x, banks[0])
+        gemm = graph_time(lambda r: gate_up_i8(low, banks[r % copies].low_weight, high, banks[r % copies].high_weight,
+                                               sc, banks[r % copies].scales, banks[r % copies].bias,
+                                               static_weights=True), copies, n_rep, cap)
+        quant = graph_time(lambda r: quantize_rows(x, banks[r % copies]), copies, n_rep, cap)
+    ops = gemm_ops(M, K, H)
+    tops = ops / gemm / 1e12
+    live = int_mm_tops()
+    peaks, kind = measured_peaks()
+    return {"workload": desc, "tokens_per_s": M / call, "call_us": call * 1e6, "gemm_us": gemm * 1e6,
+            "quant_us": quant * 1e6, "gemm_tops": tops, "call_tops": ops / call / 1e12,
+            "frac": {"torch_int_mm_live": tops / live, "twice_bf16_burst": tops / (2 * peaks["bf16_tflops"]),
+                     "datasheet_dense_int8": tops / 4500.0},
+            "denominators_tops": {"torch_int_mm_live": live, "twice_bf16_burst": 2 * peaks["bf16_tflops"],
+                                  "datasheet_dense_int8": 4500.0},
+            "how": "CUDA graphs of back-to-back calls over the 3 rotating weight copies; GEMM as "
+                   "reax_gate_up_i8_static on pre-quantized codes; torch._int_mm 8192^3 best of 5 measured in this run"}
+
+
+def ref_kernel_record(banks, xs, dev, cap, steps):
+    """The reference's own implementation of the path on this GPU, as reaxv2.gate_up.Native.project runs
+    it (reaxv2/gate_up.py:29-37): its Triton _prepare, compiled ahead of time from the unmodified source,
+    then its native_hybrid8 kernel (kernel-source/legacy-v2/src/native_hybrid8.cu, built from source for
+    sm_100a), the best hybrid8_* configuration per bucket, against ours on the same inputs, weights and
+    L2 rotation.  Both are timed per call (serially), outside `value`; outputs are compared once."""
+    from oracle import ref_gpu
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native
+    name0 = ref_gpu.TritonQuantizer.prepare_name(4096, 4096, 0, False)
+    if not (ref_gpu.available("native_hybrid8.cubin") and ref_gpu.TritonQuantizer.available(name0)):
+        return {"unavailable": "reference kernels not built into oracle/_ref (oracle/build_ref.py)"}
+    hy, tq = ref_gpu.Hybrid8(), ref_gpu.TritonQuantizer()
+    nat = Native(None)
+    copies = len(banks)
+    n_rep = max(3, steps // copies)
+
+    def ref_project(x, b, name):
+        low, high, sc = tq.prepare(x, b.low_columns, b.high_columns, b.smoothing, b.centers, b.centered)
+        return hy.product(low, b.low_weight, high, b.high_weight, sc, b.scales, b.bias, name)
+
+    rec = {}
+    with torch.cuda.stream(cap):
+        for x in xs:
+            M = x.shape[0]
+            best = None
+            for name in ref_gpu.HYBRID:
+                t = graph_time(lambda r: ref_project(x, banks[r % copies], name), copies, n_rep, cap)
+                if best is None or t < best[0]:
+                    best = (t, name)
+            ours = graph_time(lambda r: nat.project(x, banks[r % copies], "hybrid8_b128n256_s64n256"), copies, n_rep, cap)
+            same = torch.equal(ref_project(x, banks[0], best[1]).view(torch.int16),
+                               nat.project(x, banks[0], "hybrid8_b128n256_s64n256").view(torch.int16))
+            rec[str(M)] = {"ref_us": round(best[0] * 1e6, 2), "ref_config": best[1], "ours_us": round(ours * 1e6, 2),
+                           "speedup": best[0] / ours, "outputs_bit_identical": same}
+    return {"per_bucket": rec, "how": "CUDA graphs of back-to-back calls over the 3 rotating weight copies, "
+                                      "quantize + gate/up per call, best reference hybrid8_* config per bucket"}
+
+
 # -------------------------------------------------------------------------------------------------- GPU leg
 def main():
     args = parse()
@@ -721,6 +856,16 @@ def main():
     if per_bucket_plain:
         roofline["per_launch_us_plain"] = {str(M): round(d * 1e6, 2) for M, d in per_bucket_plain}
 
+    # Side records of the one-GPU default line (outside `value`): the prefill half of the metric (cfg3)
+    # and the reference's own GPU implementation on the same buckets.
+    prefill = ref_kernel = None
+    if world == 1 and args.workload == DEFAULT_WORKLOAD and int8 and not args.no_side_records:
+        prefill = prefill_record(banks, dev, cap, args.steps)
+        gx = torch.Generator().manual_seed(20261201)
+        x3 = torch.randn(4096, K, generator=gx).to(torch.bfloat16).to(dev)
+        ref_kernel = ref_kernel_record(banks, xs + [x3], dev, cap, args.steps)
+        del x3
+
     # end to end through the public API with host buffers: every step copies each bucket's input from
     # pinned host memory, runs the path and reads every output back to pinned host memory, all inside the
     # replayed graph.  The compute runs on the step's two lanes; the copies run on two more streams, so a
@@ -854,7 +999,7 @@ def main():
                            "l2": f"{copies} rotating weight copies ({copies * 2 * h * K * (1 if int8 else 2) / 1e6:.0f} MB > 126 MB L2), "
                                  "a different copy on consecutive calls"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
-                "allgather": allgather,
+                "allgather": allgather, "prefill": prefill, "ref_kernel": ref_kernel,
                 "device_status": status, "timing": "CUDA-graph replay of the captured step",
                 "eager_ms_per_step": eager_ms}
         print(json.dumps(line), flush=True)
