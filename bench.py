@@ -73,6 +73,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--measure-int8-peak", action="store_true", help="print torch._int_mm int8 throughput and exit")
+    ap.add_argument("--lane-sms", choices=("whole", "half"), default="half",
+                    help="SMs each of the two lanes' GEMMs are planned for (reax_set_stream_sms): half each "
+                         "(the lanes' grids run side by side) or the whole GPU each")
+    ap.add_argument("--emulate-shard", type=int, default=1,
+                    help="one GPU runs rank 0's H shard of an N-way job (a diagnostic of per-rank latency)")
     ap.add_argument("--no-side-records", action="store_true",
                     help="skip the prefill and reference-kernel records of the one-GPU cfg2 line")
     a = ap.parse_args()
@@ -222,10 +227,10 @@ def deal_lanes(buckets):
     return lanes, {j: 2 * k + l for l, ln in enumerate(lanes) for k, j in enumerate(ln)}
 
 
-def lane_runner(lanes, dev):
+def lane_runner(lanes, dev, side=None):
     """run(work): work(j) for every bucket, lane 0 on the current stream and lane 1 on a side stream
     forked from and joined to it (inside a graph capture too)."""
-    side = torch.cuda.Stream(dev)
+    side = side if side is not None else torch.cuda.Stream(dev)
 
     def run(work):
         main = torch.cuda.current_stream(dev)
@@ -239,6 +244,28 @@ def lane_runner(lanes, dev):
             main.wait_stream(side)
         return outs
     return run
+
+
+class LaneShares:
+    """With two lanes and ``--lane-sms half``: each lane's GEMMs are planned for half of the SMs
+    (reax_set_stream_sms), so the two lanes' persistent grids run side by side; used around the
+    capture of the step graphs, which keep the plans they were captured with."""
+
+    def __init__(self, streams, dev, enabled):
+        self.streams = streams if enabled and len(streams) > 1 else []
+        self.sms = torch.cuda.get_device_properties(dev).multi_processor_count
+
+    def __enter__(self):
+        from reax_engine_runtime_v3_b200 import _native
+        for i, st in enumerate(self.streams):
+            _native.set_stream_sms(st, self.sms // 2 if i == 0 else self.sms - self.sms // 2)
+        return self
+
+    def __exit__(self, *exc):
+        from reax_engine_runtime_v3_b200 import _native
+        for st in self.streams:
+            _native.set_stream_sms(st, 0)
+        return False
 
 
 def dist_env():
@@ -711,7 +738,8 @@ def main():
     buckets, K, H, kind, srange, desc = WORKLOADS[args.workload]
     int8 = srange is not None
     copies = 3
-    xs_cpu, banks, h = make_inputs(args.workload, rank, world, copies)
+    shard_world = args.emulate_shard if world == 1 and args.emulate_shard > 1 else world
+    xs_cpu, banks, h = make_inputs(args.workload, rank, shard_world, copies)
     dev = torch.device("cuda", local)
     xs = [x.to(dev) for x in xs_cpu]
     gate_up = Native(None)
@@ -722,7 +750,8 @@ def main():
     # at the same time, always read different weight copies.
     order = sorted(range(len(buckets)), key=lambda j: -buckets[j])
     lanes, slot_of = deal_lanes(buckets)
-    run_lanes = lane_runner(lanes, dev)
+    side = torch.cuda.Stream(dev)
+    run_lanes = lane_runner(lanes, dev, side)
 
     def bank_of(i, j):
         return banks[(4 * i + slot_of[j]) % copies]
@@ -741,7 +770,8 @@ def main():
     # inside a graph.
     cap = torch.cuda.Stream(dev)
     cap.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(cap):
+    shares = LaneShares([cap, side], dev, args.lane_sms == "half" and len(lanes) > 1)
+    with torch.cuda.stream(cap), shares:
         for i in range(args.warmup):
             step(i)
         torch.cuda.synchronize()
@@ -859,7 +889,7 @@ def main():
     # Side records of the one-GPU default line (outside `value`): the prefill half of the metric (cfg3)
     # and the reference's own GPU implementation on the same buckets.
     prefill = ref_kernel = None
-    if world == 1 and args.workload == DEFAULT_WORKLOAD and int8 and not args.no_side_records:
+    if world == 1 and shard_world == 1 and args.workload == DEFAULT_WORKLOAD and int8 and not args.no_side_records:
         prefill = prefill_record(banks, dev, cap, args.steps)
         gx = torch.Generator().manual_seed(20261201)
         x3 = torch.randn(4096, K, generator=gx).to(torch.bfloat16).to(dev)
@@ -918,7 +948,7 @@ def main():
             main.wait_stream(s_in)
             main.wait_stream(s_out)
             return outs
-        with torch.cuda.stream(cap):
+        with torch.cuda.stream(cap), shares:
             e2e_step(0)
             torch.cuda.synchronize()
             egraphs = []
@@ -994,8 +1024,11 @@ def main():
                 "scaling": "strong" if world > 1 else "strong", "vs_baseline": None, "dtype": "s8" if int8 else "bf16",
                 "data": "synthetic (seeded N(0,1) or Student-t activations, uniform int8 / N(0,0.02) bf16 weights)",
                 "config": {"workload": desc, "tokens_per_step": tokens, "K": K, "H": H, "H_per_gpu": h,
-                           "parallelism": f"H-shard x{world}" if world > 1 else "1 GPU",
+                           "parallelism": f"H-shard x{world}" if world > 1 else (
+                               f"rank 0 of an H-shard x{shard_world}, alone on one GPU (its tokens/s, not the job's)"
+                               if shard_world > 1 else "1 GPU"),
                            "lanes": [[buckets[j] for j in ln] for ln in lanes],
+                           "lane_sms": [shares.sms // 2, shares.sms - shares.sms // 2] if shares.streams else "whole GPU",
                            "l2": f"{copies} rotating weight copies ({copies * 2 * h * K * (1 if int8 else 2) / 1e6:.0f} MB > 126 MB L2), "
                                  "a different copy on consecutive calls"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,

@@ -54,6 +54,13 @@ REAX_API const char* reax_last_error(void);
  * workspace may not be used by two launches that can run at the same time (use one per stream). */
 REAX_API size_t reax_workspace_bytes(int device);
 
+/* SM share of the GEMM launches on `stream`: their tile plans and grids use at most `sms` SMs (0 removes
+ * the share: the whole GPU).  For callers that run several lanes at once (streams whose launches
+ * overlap, as the reference's two serving lanes do: runtime/bootstrap.py:29, vendor/s1eng/s1eng/kprio.py):
+ * each lane's persistent grid then fits beside the other's instead of queueing for the whole GPU.
+ * At most 64 streams hold a share.  No counterpart in the reference, whose kernels take fixed grids. */
+REAX_API int reax_set_stream_sms(void* stream, int sms);
+
 /* Default bound (nanoseconds) of every device-side wait; reax_set_wait_timeout_ns() changes it for
  * later launches from any thread (0 restores the default of 2 s). */
 REAX_API void reax_set_wait_timeout_ns(unsigned long long ns);

@@ -52,6 +52,7 @@ SIGNATURES = {
     "reax_sliced_i8_static": ([_P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P], _I),
     "reax_selftest_wait": ([_P, _ULL, _P], _I),
     "reax_noalloc_status": ([C.POINTER(C.c_uint), _I, _P], _I),
+    "reax_set_stream_sms": ([_P, _I], _I),
 }
 
 _lib = None
@@ -139,6 +140,11 @@ def noalloc_status(clear: bool = False) -> int:
     v = C.c_uint(0)
     check(load().reax_noalloc_status(C.byref(v), 1 if clear else 0, stream_handle()))
     return int(v.value)
+
+
+def set_stream_sms(stream: torch.cuda.Stream, sms: int) -> None:
+    """Give the GEMM launches on `stream` a share of `sms` SMs (0: the whole GPU); see reax_set_stream_sms."""
+    check(load().reax_set_stream_sms(stream.cuda_stream, int(sms)))
 
 
 def clear_status(ws: torch.Tensor) -> None:

@@ -54,14 +54,25 @@ struct DeviceInfo {
     int sms = 0;
     int major = 0, minor = 0;
     bool smem_set = false;
+    bool stream_smem_set = false;
+    int pair_clusters = 0;   // CTA pairs of the pair GEMM that can be resident at once (GPC layout permitting)
 };
+// Shared memory the many-rows quantizer may use per CTA (one CTA per SM), and the rows from which it runs.
+constexpr size_t kQuantStreamSmemMax = 227 * 1024;
+constexpr int kQuantStreamMinRows = 1 << 30;   // off until it measures faster than the 128-thread rows kernel
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mutex;
 
 // The kernel variants: (epilogue, mode, BF16 columns added to INT8 accumulators).
 enum Variant : int {
-    kSwigluI8 = 0, kSwigluI8F, kSwigluBf16, kPlainI8, kPlainI8F, kPlainBf16, kSwapI8, kSwapBf16, kVariants
+    kSwigluI8 = 0, kSwigluI8F, kSwigluBf16, kPlainI8, kPlainI8F, kPlainBf16, kSwapI8, kSwapBf16, kPairI8, kVariants
 };
+
+// Token rows from which an INT8 gate/up launch without BF16 columns takes CTA-pair tiles (256 token rows x
+// 128 gate + 128 up columns per pair, tcgen05 cta_group::2).
+constexpr int kPairMinRows = 1 << 30;   // CTA-pair tiles: off until they measure faster
+// Stages of a pair's ring: [half of B | A box] of 32 KiB each in the same pool as four 48 KiB stages.
+constexpr int kPairStages = 6;
 
 // Activation rows up to which the gate/up kernels use weight-major (swap) tiles.
 constexpr int kSwapMaxRows = reax::kSwapMaxTok;
@@ -76,11 +87,14 @@ void* tc_kernel_ptr(int v) {
         case kPlainI8F: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiPlain, 0, true, false>);
         case kPlainBf16: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiPlain, 1, false, false>);
         case kSwapI8: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 0, false, true>);
+        case kPairI8:
+            return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 0, false, false, true>);
         default: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 1, false, true>);
     }
 }
 
 int variant_of(int epi, const reax::TcParams& p) {
+    if (p.cta_shift == 1) return kPairI8;
     if (p.n_tok > 0) return p.mode == 1 ? kSwapBf16 : kSwapI8;
     if (epi == reax::kEpiSwiglu) return p.mode == 1 ? kSwigluBf16 : (p.kb_f16 > 0 ? kSwigluI8F : kSwigluI8);
     return p.mode == 1 ? kPlainBf16 : (p.kb_f16 > 0 ? kPlainI8F : kPlainI8);
@@ -131,11 +145,49 @@ int current_device(int* dev_out, DeviceInfo** info_out) {
                 return fail(REAX_ERR_DEVICE, "tcgen05 kernel variant %d compiled to %d registers per thread, which "
                             "cannot cover the %d/%d register split", v, fa.numRegs, reax::kCtlRegs, reax::kEpiRegs);
         }
+        // A persistent grid of CTA pairs must fit in one wave: not every GPC may host clusters of two on all
+        // its SMs, so ask how many pairs can be resident rather than assuming SMs / 2.
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
+        cfg.blockDim = dim3(reax::kCtlThreads + 32 * kEpiWarps, 1, 1);
+        cfg.dynamicSmemBytes = tc_smem_bytes();
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if ((e = cudaOccupancyMaxActiveClusters(&clusters, tc_kernel_ptr(kPairI8), &cfg)) != cudaSuccess)
+            return cuda_fail(e, "cudaOccupancyMaxActiveClusters(pair GEMM)");
+        d.pair_clusters = clusters;
         d.smem_set = true;
     }
     *dev_out = dev;
     *info_out = &d;
     return REAX_OK;
+}
+
+// ------------------------------------------------------------------------------------------ per-stream SM share
+// A caller that runs several lanes at once (streams whose launches overlap) can give each lane's GEMMs a
+// share of the SMs (reax_set_stream_sms): the planner then sizes tiles and grids for that many SMs, so the
+// lanes' persistent grids sit side by side instead of queueing for the whole GPU.
+constexpr int kMaxStreamShares = 64;
+struct StreamShare {
+    void* stream;
+    int sms;
+};
+StreamShare g_shares[kMaxStreamShares];
+int g_n_shares = 0;
+std::mutex g_share_mutex;
+
+// SMs the GEMM plans of `stream` may use on a device of `sms` SMs.
+int stream_sms(void* stream, int sms) {
+    std::lock_guard<std::mutex> lock(g_share_mutex);
+    for (int i = 0; i < g_n_shares; ++i)
+        if (g_shares[i].stream == stream) return std::min(sms, g_shares[i].sms);
+    return sms;
 }
 
 // ------------------------------------------------------------------------------------------------ tensor maps
@@ -320,11 +372,18 @@ int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
     cfg.blockDim = dim3(reax::kCtlThreads + 32 * kEpiWarps, 1, 1);
     cfg.dynamicSmemBytes = tc_smem_bytes();
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (p.cta_shift == 1) {   // CTA pairs: clusters of two
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 2;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+    }
     void* args[1] = {const_cast<reax::TcParams*>(&p)};
     cudaError_t e = cudaLaunchKernelExC(&cfg, tc_kernel_ptr(variant_of(epi, p)), args);
     if (e != cudaSuccess) return cuda_fail(e, "tcgen05 GEMM launch");
@@ -445,12 +504,24 @@ int check_gate_up_args(const char* who, const int8_t* A, const int8_t* W, const 
 // Tile plan, tensor maps and operands of an INT8 gate/up launch (everything but the scratch pointers,
 // early_b and the schedule), shared by the workspace and the allocation-free entry points so that both
 // run the same kernel on the same plan.  *split_ok: whether the plan may split tiles by K.
-int fill_gate_up_params(reax::TcParams& p, int sms, const int8_t* A, const int8_t* W, const void* AH, const void* WH,
-                        const float* sa, const float* sw, const float* bias, void* out, int M, int N2, int KL, int KH,
-                        int ldo, bool* split_ok) {
+int fill_gate_up_params(reax::TcParams& p, int sms, bool pair_ok, const int8_t* A, const int8_t* W, const void* AH,
+                        const void* WH, const float* sa, const float* sw, const float* bias, void* out, int M, int N2,
+                        int KL, int KH, int ldo, bool* split_ok) {
     init_params(p);
+    // many tokens and no BF16 columns: CTA-pair tiles of 256 token rows (whole tiles, dealt to pairs)
+    const bool pair = KH == 0 && M >= kPairMinRows && sms >= 2 && pair_ok;
     // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
-    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, sms, split_ok);
+    const bool swap = !pair && plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, sms, split_ok);
+    if (pair) {
+        p.cta_shift = 1;
+        p.tile_rows = 128;
+        p.tile_rows8 = 128;
+        p.a_rows = reax::kBM;
+        p.stages = kPairStages;
+        p.stage_bytes = 2 * reax::kBM * reax::kRowBytes;
+        p.out_vec16 = 0;
+        *split_ok = false;
+    }
     int rc;
     if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
         return rc;
@@ -472,13 +543,22 @@ int fill_gate_up_params(reax::TcParams& p, int sms, const int8_t* A, const int8_
     p.ldo = ldo;
     p.kb_int = KL / 128;
     p.kb_f16 = KH / 64;
-    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
+    const int unit_rows = reax::kBM << p.cta_shift;   // token rows per tile: 128, or 256 for a pair
+    p.m_tiles = (M + unit_rows - 1) / unit_rows;
     p.n_tiles = (N2 / 2 + p.tile_rows - 1) / p.tile_rows;
     p.tiles = p.m_tiles * p.n_tiles;
     p.mode = 0;
     p.acc_bufs = KH ? 1 : 2;
     p.evict_first_b = p.m_tiles == 1 ? 1 : 0;
     return REAX_OK;
+}
+
+// Whole tiles dealt to CTA pairs: grid = two CTAs per pair, at most one pair per two SMs of the share and
+// no more pairs than can be resident at once (`resident`).
+void plan_pairs(reax::TcParams& p, int sms, int resident, int* grid) {
+    p.dp_tiles = p.tiles;
+    p.sk_iters = 0;
+    *grid = 2 * std::max(1, std::min(p.tiles, std::min(sms / 2, resident)));
 }
 
 // reax_gate_up_i8 with the option of requesting the first weight tiles before the dependency wait.
@@ -495,15 +575,16 @@ int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const vo
     if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
     reax::TcParams p;
     bool split_ok = false;
-    if ((rc = fill_gate_up_params(p, info->sms, A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &split_ok)) !=
-        REAX_OK)
+    const int sms = stream_sms(stream, info->sms);
+    if ((rc = fill_gate_up_params(p, sms, info->pair_clusters > 0, A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &split_ok)) != REAX_OK)
         return rc;
     p.ws_partials = ws.partials;
     p.ws_counters = ws.counters;
     p.status = ws.status;
     p.early_b = early_b;
     int grid = 0;
-    plan_schedule(p, info->sms, split_ok, &grid);
+    if (p.cta_shift) plan_pairs(p, sms, info->pair_clusters, &grid);
+    else plan_schedule(p, sms, split_ok, &grid);
     return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
 }
 
@@ -542,6 +623,41 @@ int reax_quant_rows(const void* x, const int32_t* low_columns, const int32_t* hi
     if (rc != REAX_OK) return rc;
     const int aligned_x = (aligned(x, 16) && K % 8 == 0) ? 1 : 0;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // many rows: persistent CTAs streaming whole rows into a ring of shared-memory buffers by bulk copies,
+    // as many rows in flight per SM as the shared memory holds (at most kStreamMaxBufs)
+    if (M > kQuantStreamMinRows && aligned_x) {
+        // row buffers that fit, then warps x depth of them: two rows in flight per warp when that still
+        // leaves at least 8 warps, else one row for each of up to kStreamWarps warps
+        int nbuf = reax::kStreamMaxBufs;
+        while (nbuf > 0 && reax::quant_stream_smem(K, KL, KH, center, nbuf) > kQuantStreamSmemMax) --nbuf;
+        const int depth = nbuf >= 16 ? 2 : 1;
+        const int warps = std::min(reax::kStreamWarps, nbuf / depth);
+        if (warps >= 4) {
+            const size_t smem = reax::quant_stream_smem(K, KL, KH, center, warps * depth);
+            if (!info->stream_smem_set) {
+                cudaError_t e = cudaFuncSetAttribute(reax::quant_rows_stream_kernel<kQuantDivision>,
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     static_cast<int>(kQuantStreamSmemMax));
+                if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(quant_rows_stream_kernel smem)");
+                info->stream_smem_set = true;
+            }
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(static_cast<unsigned>(std::min(M, info->sms)), 1, 1);
+            cfg.blockDim = dim3(32 * warps, 1, 1);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = s;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            const cudaError_t e = cudaLaunchKernelEx(
+                &cfg, reax::quant_rows_stream_kernel<kQuantDivision>, static_cast<const __nv_bfloat16*>(x),
+                static_cast<const int*>(low_columns), static_cast<const int*>(high_columns), smoothing, centers, low,
+                static_cast<__nv_bfloat16*>(high), scales, M, K, KL, KH, center ? 1 : 0, depth, g_timeout_ns);
+            return e == cudaSuccess ? REAX_OK : cuda_fail(e, "quant_rows launch");
+        }
+    }
     // more rows than four per SM: narrower CTAs (wide enough to hold a row's values up to 8192 columns),
     // more rows in flight on each SM
     if (M > 4 * info->sms && KL <= 32 * reax::kQuantThreadsMany)
@@ -760,7 +876,8 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     reax::TcParams p;
     init_params(p);
     bool split_ok = false;   // BF16 tiles are never split
-    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, K / 64, true, false, info->sms, &split_ok);
+    const int sms = stream_sms(stream, info->sms);
+    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, K / 64, true, false, sms, &split_ok);
     if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : p.a_rows)) != REAX_OK)
         return rc;
     if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K, p.tile_rows)) !=
@@ -786,7 +903,7 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     int grid = 0;
     // float32 partial sums of one tile would round differently from one unsplit accumulation, which
     // would make a row's result depend on the batch it came in: BF16 tiles are never split.
-    plan_schedule(p, info->sms, false, &grid);
+    plan_schedule(p, sms, false, &grid);
     return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
 }
 
@@ -848,7 +965,7 @@ int reax_bf16_partials(const void* x, const void* w, const int32_t* split, void*
     p.ws_counters = ws.counters;
     p.status = ws.status;
     int grid = 0;
-    plan_schedule(p, info->sms, false, &grid);
+    plan_schedule(p, stream_sms(stream, info->sms), false, &grid);
     return launch_tc(reax::kEpiPlain, p, grid, s);
 }
 
@@ -917,7 +1034,7 @@ int sliced_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const voi
     p.status = ws.status;
     p.early_b = early_b;
     int grid = 0;
-    plan_schedule(p, info->sms, false, &grid);
+    plan_schedule(p, stream_sms(stream, info->sms), false, &grid);
     return launch_tc(reax::kEpiPlain, p, grid, static_cast<cudaStream_t>(stream));
 }
 
@@ -962,13 +1079,14 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     if ((rc = noalloc_scratch(dev, &scratch)) != REAX_OK) return rc;
     reax::TcParams p;
     bool split_ok = false;
-    if ((rc = fill_gate_up_params(p, info->sms, A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &split_ok)) !=
-        REAX_OK)
+    const int sms = stream_sms(stream, info->sms);
+    if ((rc = fill_gate_up_params(p, sms, info->pair_clusters > 0, A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &split_ok)) != REAX_OK)
         return rc;
     // Whole-tile plans need no partials; a plan that splits tiles is re-planned for at most
     // kNoAllocMaxCtas CTAs, whose partials the static scratch holds.
     int grid = 0;
-    plan_schedule(p, info->sms, split_ok, &grid);
+    if (p.cta_shift) plan_pairs(p, sms, info->pair_clusters, &grid);
+    else plan_schedule(p, sms, split_ok, &grid);
     if (p.sk_iters > 0 && grid > kNoAllocMaxCtas) plan_schedule(p, kNoAllocMaxCtas, true, &grid);
     const int slots = p.sk_iters > 0 ? grid : 0;
     const size_t counter_bytes = ((static_cast<size_t>(2 * (slots > 0 ? slots : 1)) * sizeof(int)) + 255) / 256 * 256;
@@ -985,6 +1103,22 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     const cudaError_t e = cudaMemsetAsync(scratch, 0, kStatusBytes + counter_bytes, s);
     if (e != cudaSuccess) return cuda_fail(e, "gate_up_i8_noalloc: clearing the scratch");
     return launch_tc(reax::kEpiSwiglu, p, grid, s);
+}
+
+int reax_set_stream_sms(void* stream, int sms) {
+    if (sms < 0) return fail(REAX_ERR_INVALID, "set_stream_sms: sms=%d", sms);
+    std::lock_guard<std::mutex> lock(g_share_mutex);
+    for (int i = 0; i < g_n_shares; ++i)
+        if (g_shares[i].stream == stream) {
+            if (sms == 0) g_shares[i] = g_shares[--g_n_shares];
+            else g_shares[i].sms = sms;
+            return REAX_OK;
+        }
+    if (sms == 0) return REAX_OK;
+    if (g_n_shares == kMaxStreamShares)
+        return fail(REAX_ERR_INVALID, "set_stream_sms: more than %d streams with an SM share", kMaxStreamShares);
+    g_shares[g_n_shares++] = StreamShare{stream, sms};
+    return REAX_OK;
 }
 
 int reax_noalloc_status(unsigned* status, int clear, void* stream) {

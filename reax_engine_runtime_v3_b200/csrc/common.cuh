@@ -86,6 +86,18 @@ REAX_DEVI void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
         : "memory");
 }
+// 1-D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global memory into
+// this CTA's shared memory, completing on `bar`.
+REAX_DEVI void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(smem_dst)),
+                 "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+// Order this thread's earlier generic-proxy accesses of shared memory before later async-proxy ones
+// (e.g. a bulk copy into a buffer the thread has just read).
+REAX_DEVI void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 REAX_DEVI uint64_t l2_policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -159,6 +171,78 @@ REAX_DEVI void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
 REAX_DEVI void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
 REAX_DEVI void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ------------------------------------------------------------------- CTA pairs (tcgen05 .cta_group::2)
+// Two CTAs of a cluster (ranks 0 and 1) share one MMA of M = 256: each holds 128 rows of A and half of the
+// N rows of B in its own shared memory at the same offsets, rank 0 issues the MMAs, and each CTA's TMEM
+// receives its 128 accumulator rows.  Every tcgen05 instruction of such a kernel uses .cta_group::2.
+REAX_DEVI uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address in the shared-memory window of CTA `rank` of this cluster of the object at `p` in this CTA.
+REAX_DEVI uint32_t cluster_map(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// Every thread of both CTAs: release this CTA's prior shared-memory writes (mbarrier inits) to the
+// cluster and wait for the other CTA to do the same.
+REAX_DEVI void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+REAX_DEVI void mbar_arrive_expect_tx_cluster(uint32_t bar_cluster_addr, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cluster_addr),
+                 "r"(bytes)
+                 : "memory");
+}
+REAX_DEVI void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+// Tiled load of one box into this CTA's shared memory whose completion is counted on an mbarrier of either
+// CTA of the pair (bar_cluster_addr: a shared::cluster address).  No multicast: each CTA loads its own boxes.
+REAX_DEVI void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int x, int y,
+                                uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+REAX_DEVI void umma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive once on the mbarrier at the offset of `bar` in both CTAs of the pair when every tcgen05
+// operation this thread issued before it has completed.
+REAX_DEVI void umma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+// Arrive on the mbarrier at `bar` of this CTA only (the drain barrier before TMEM is freed).
+REAX_DEVI void umma_commit_pair_local(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+REAX_DEVI void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+REAX_DEVI void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+REAX_DEVI void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
 // 32 lanes x 32 consecutive 32-bit columns: register i of lane t <- TMEM[lane base + t][column + i].

@@ -121,7 +121,13 @@ struct TcParams {
     int plan_parts0;
     int plan_chunk_kb0, plan_chunk_kb1;
     const int* split;
+    // CTA pairs (PAIR kernels): tiles are dealt to pairs of CTAs (clusters of two), cta_shift = 1; 0 otherwise
+    int cta_shift;
 };
+
+// The unit that tiles are dealt to (a CTA, or a CTA pair) and how many there are.
+REAX_DEVI int unit_id(const TcParams& p) { return static_cast<int>(blockIdx.x) >> p.cta_shift; }
+REAX_DEVI int unit_count(const TcParams& p) { return static_cast<int>(gridDim.x) >> p.cta_shift; }
 
 struct Segment {
     int tile;    // linear tile index (grouped order)
@@ -201,7 +207,7 @@ REAX_DEVI bool tile_active(const TcParams& p, int t, int split, int& k0, int& k1
 REAX_DEVI bool cursor_next(const TcParams& p, int split, Cursor& c, Segment& s) {
     const int KB = p.kb_int + p.kb_f16;
     while (true) {
-        const int t = blockIdx.x + c.dp_i * gridDim.x;
+        const int t = unit_id(p) + c.dp_i * unit_count(p);
         if (t >= p.dp_tiles) break;
         ++c.dp_i;
         if (tile_active(p, t, split, s.k0, s.k1)) {
@@ -406,9 +412,19 @@ REAX_DEVI void add_partials(const int4* const (&contrib)[kMaxContrib], int n, in
 // activation tile (n_tok token rows); TMEM lanes are weight rows, columns [0, n_tok) gate and
 // [n_tok, 2 n_tok) up, one column per token.  Every TMEM lane quarter then holds real rows even when
 // only a few tokens exist, so all four SM sub-partitions share the epilogue.
-template <int EPI_WARPS, int STAGES, int EPI, int MODE, bool ADD_F, bool SWAP>
+// PAIR: token-major INT8 SwiGLU tiles of 256 token rows computed by a CTA pair (a cluster of two) with
+// tcgen05.mma.cta_group::2 (M = 256): each CTA loads its own 128 token rows and half of the tile's B rows
+// (rank 0 the gate rows, rank 1 the matching up rows) into its own shared memory, rank 0 issues the MMAs
+// (N = 256: gate then up columns) on both CTAs' operands, and each CTA's TMEM receives its 128 token rows,
+// gate in columns [0, 128) and up in [128, 256) as for a single-CTA tile, so the epilogue is the same.
+// Per SM this moves two thirds of the operand bytes of a single-CTA 128 x 256 tile for the same MMA work.
+template <int EPI_WARPS, int STAGES, int EPI, int MODE, bool ADD_F, bool SWAP, bool PAIR = false>
 __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     static_assert(!SWAP || (EPI == kEpiSwiglu && !ADD_F), "weight-major tiles: SwiGLU without BF16 columns");
+    static_assert(!PAIR || (EPI == kEpiSwiglu && MODE == 0 && !ADD_F && !SWAP), "CTA pairs: INT8 SwiGLU tiles");
+    // the CTA's rank in its pair (0 issues the MMAs) and the pair's per-stage box bytes
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    constexpr int kPairBox = kBM * kRowBytes;   // 128 rows x 128 bytes: a CTA's A box and its half of B
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stage_a = smem;
@@ -431,11 +447,14 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     int* last_flag = abort_flag + 1;
     // pipeline stages and the boxes inside them
-    const int ns = SWAP ? p.stages : STAGES;
+    // pair stages: [this CTA's half of B | its A box], 32 KiB each
+    const int ns = (SWAP || PAIR) ? p.stages : STAGES;
     auto box_a = [&](int st) -> uint8_t* {   // activation box (weight-major) or A tile
+        if constexpr (PAIR) return smem + st * (2 * kPairBox) + kPairBox;
         return SWAP ? smem + st * p.stage_bytes + 2 * p.tile_rows8 * kRowBytes : stage_a + st * kAStage;
     };
     auto box_b = [&](int st) -> uint8_t* {   // gate rows (weight-major) or the first half of B
+        if constexpr (PAIR) return smem + st * (2 * kPairBox);
         return SWAP ? smem + st * p.stage_bytes : stage_b + st * kBStage;
     };
     auto box_bu = [&](int st) -> uint8_t* {  // up rows (weight-major) or the second half of B
@@ -447,12 +466,14 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ns; ++s) {
-            mbar_init(&full[s], 3);   // one arrival per producer (gate, up, activation boxes)
+            // one arrival per producer: gate, up and activation boxes; for a pair, rank 0's barrier counts
+            // both CTAs' B-half and A boxes
+            mbar_init(&full[s], PAIR ? 4 : 3);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], EPI_WARPS);
+            mbar_init(&acc_empty[b], PAIR ? 2 * EPI_WARPS : EPI_WARPS);   // a pair: both CTAs' epilogue warps
         }
         mbar_init(drain, 1);
         mbar_init(deq_ready, EPI_WARPS);
@@ -467,11 +488,18 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         tma_prefetch_desc(&p.tm_bh);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, kTmemCols);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    // a pair: the other CTA's barriers are initialised before anything arrives on them remotely
+    if constexpr (PAIR) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     volatile int* vabort = abort_flag;
@@ -495,7 +523,9 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         // One box per producer and K block: warp 0 the gate rows (first half of B), warp 2 the up rows
         // (second half of B), warp 3 the activation rows (A).  Each arms the stage's full barrier with
         // its own bytes (three arrivals per phase), so the three copies are issued in parallel.
-        if (lane == 0) {
+        // A pair has two boxes per CTA and K block: warp 0 loads this CTA's half of B (rank 0 the gate rows,
+        // rank 1 the up rows), warp 3 its 128 activation rows; warp 2 has nothing to load.
+        if (lane == 0 && !(PAIR && warp == 2)) {
             const int role = warp == 0 ? 0 : warp - 1;   // 0 gate, 1 up, 2 activation
             const uint64_t policy = role == 2 ? l2_policy_evict_last()
                                               : (p.evict_first_b ? l2_policy_evict_first() : l2_policy_evict_normal());
@@ -507,10 +537,18 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             uint32_t armed = 0;        // bit s: stage s has been armed at least once
             uint32_t armed_parity = 0; // bit s: parity of the last arming of stage s
             // this producer's box of K block kb of the tile (part, m0, b0, b1) into stage st
+            // arm the stage's full barrier with this box's bytes (a pair: rank 0's barrier counts both CTAs')
+            auto arm = [&](int st) {
+                if constexpr (PAIR) mbar_arrive_expect_tx_cluster(cluster_map(&full[st], 0), box_tx);
+                else mbar_arrive_expect_tx(&full[st], box_tx);
+            };
             auto load_box = [&](int st, int kb, int part, int m0, int b0, int b1) {
                 uint8_t* dst = role == 0 ? box_b(st) : (role == 1 ? box_bu(st) : box_a(st));
-                const int y = role == 0 ? b0 : (role == 1 ? b1 : m0);
-                if (kb < p.kb_int) {
+                const int y = role == 0 ? ((PAIR && rank == 1) ? b1 : b0) : (role == 1 ? b1 : m0);
+                if constexpr (PAIR) {
+                    const int x = kb * kRowBytes;
+                    tma_load_2d_pair(dst, role == 2 ? &p.tm_a : &p.tm_b, cluster_map(&full[st], 0), x, y, policy);
+                } else if (kb < p.kb_int) {
                     const int x = (part * p.kb_int_part + kb) * kRowBytes;
                     tma_load_2d(dst, role == 2 ? &p.tm_a : &p.tm_b, &full[st], x, y, policy);
                 } else {
@@ -521,7 +559,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             auto tile_rows = [&](const Segment& sg, int& part, int& m0, int& b0, int& b1) {
                 int mt, nt;
                 tile_coords(p, sg.tile, part, mt, nt);
-                m0 = mt * kBM;
+                m0 = PAIR ? mt * 2 * kBM + kBM * static_cast<int>(rank) : mt * kBM;
                 b0 = (EPI == kEpiSwiglu) ? nt * p.tile_rows : nt * kBN;
                 b1 = (EPI == kEpiSwiglu) ? p.H + nt * p.tile_rows : nt * kBN + kBN / 2;
             };
@@ -536,7 +574,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     tile_rows(s0, part, m0, b0, b1);
                     pre = min(min(ns, kEarlyStages), s0.k1 - s0.k0);
                     for (int i = 0; i < pre; ++i) {
-                        mbar_arrive_expect_tx(&full[i], box_tx);
+                        arm(i);
                         load_box(i, s0.k0 + i, part, m0, b0, b1);
                         armed |= 1u << i;
                     }
@@ -560,7 +598,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(&full[stage], box_tx);
+                        arm(stage);
                         load_box(stage, kb, part, m0, b0, b1);
                     }
                     armed |= 1u << stage;
@@ -572,8 +610,11 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 }
                 first = false;
             }
-            // Drain: every copy this thread started must have landed before the CTA can exit.
-            for (int s = 0; s < ns; ++s) {
+            // Drain: every copy this thread started must have landed before the CTA can exit.  A pair's copies
+            // complete on rank 0's barriers, which only rank 0 can wait on: there the MMA issuer consumes every
+            // K block that was loaded and drains its MMAs before the pair's final cluster barrier, which
+            // neither CTA passes before the other has arrived.
+            for (int s = 0; s < (PAIR ? 0 : ns); ++s) {
                 if (armed & (1u << s)) {
                     if (!mbar_wait_bounded(&full[s], (armed_parity >> s) & 1, p.timeout_ns, nullptr)) {
                         atomicOr(p.status, kStatusTimeoutDrain);
@@ -583,11 +624,12 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
+        // (a pair: rank 0 issues the MMAs of both CTAs; rank 1's warp 1 only holds its TMEM allocation)
+        if (lane == 0 && (!PAIR || rank == 0)) {
             const int split = dependency_wait();
             // token-major SwiGLU tiles: N = the gate rows and the up rows of the tile (2 x tile_rows8)
             const int n_mma = SWAP ? p.n_tok : (EPI == kEpiSwiglu ? 2 * p.tile_rows8 : kBN);
-            const uint32_t idesc_i8 = idesc_i8_s32(kBM, n_mma);
+            const uint32_t idesc_i8 = idesc_i8_s32(PAIR ? 2 * kBM : kBM, n_mma);
             const uint32_t idesc_f16 = idesc_bf16_f32(kBM, n_mma);
             int stage = 0;
             uint32_t phase = 0;
@@ -629,6 +671,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             if constexpr (SWAP) {
                                 umma_i8(d_int, bd + 2 * k, ad + 2 * k, idesc_i8, acc);
                                 umma_i8(d_int + p.n_tok, bd_up + 2 * k, ad + 2 * k, idesc_i8, acc);
+                            } else if constexpr (PAIR) {
+                                umma_i8_pair(d_int, ad + 2 * k, bd + 2 * k, idesc_i8, acc);
                             } else {
                                 umma_i8(d_int, ad + 2 * k, bd + 2 * k, idesc_i8, acc);
                             }
@@ -660,7 +704,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             }
                         }
                     }
-                    umma_commit(&empty[stage]);
+                    if constexpr (PAIR) umma_commit_pair(&empty[stage]);   // frees the stage in both CTAs
+                    else umma_commit(&empty[stage]);
                     // ADD_F: the INT8 accumulators of the tile are complete
                     if (ADD_F && kb == p.kb_int - 1) umma_commit(&acc_full[0]);
                     if (++stage == ns) {
@@ -669,7 +714,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     }
                 }
                 if (!ok) break;
-                umma_commit(&acc_full[ADD_F ? 1 : buf]);
+                if constexpr (PAIR) umma_commit_pair(&acc_full[buf]);   // both CTAs' accumulators are ready
+                else umma_commit(&acc_full[ADD_F ? 1 : buf]);
                 if (p.acc_bufs == 2) {
                     buf ^= 1;
                     if (buf == 0) acc_phase ^= 1;
@@ -678,18 +724,22 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 }
             }
             // Drain: all MMAs issued by this thread complete before TMEM is freed.
-            umma_commit(drain);
+            if constexpr (PAIR) umma_commit_pair_local(drain);
+            else umma_commit(drain);
             if (!mbar_wait_bounded(drain, 0, p.timeout_ns, nullptr)) atomicOr(p.status, kStatusTimeoutDrain);
         }
         __syncwarp();
     }
     // Teardown of the control warps; every role ends in its own copy, so no code runs under both
-    // register counts.
+    // register counts.  A pair meets at a cluster barrier first: neither CTA frees its TMEM or exits while
+    // rank 0's MMAs may still read the other's shared memory or its epilogue still arrives remotely.
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
+        if constexpr (PAIR) tmem_dealloc_pair(tmem_base, kTmemCols);
+        else tmem_dealloc(tmem_base, kTmemCols);
     }
     return;
     }
@@ -729,7 +779,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         while (cursor_next(p, split, cur, seg)) {
             int part, mt, nt;
             tile_coords(p, seg.tile, part, mt, nt);
-            const int m0 = mt * kBM;
+            const int m0 = PAIR ? mt * 2 * kBM + kBM * static_cast<int>(rank) : mt * kBM;
             int row_lo, row_hi, out_part;
             tile_plan(p, part, split, row_lo, row_hi, out_part);
             float* s_sw = stage_sw + buf * kBN;
@@ -1082,7 +1132,10 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            if (lane == 0) {
+                if constexpr (PAIR) mbar_arrive_cluster(cluster_map(&acc_empty[buf], 0));   // rank 0 issues the MMAs
+                else mbar_arrive(&acc_empty[buf]);
+            }
             if (p.acc_bufs == 2) {
                 buf ^= 1;
                 if (buf == 0) acc_phase ^= 1;
@@ -1094,6 +1147,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync_all();
 }
 
 }  // namespace reax

@@ -221,6 +221,179 @@ __global__ void __launch_bounds__(THREADS) quant_rows_kernel(const __nv_bfloat16
     for (int c = threadIdx.x; c < KH; c += blockDim.x) hr[c] = xr[__ldg(high_columns + c)];
 }
 
+// Many rows (prefill): persistent CTAs of `warps` warps (at most kStreamWarps), each with its own `depth`
+// row buffers in shared memory.  Warp w quantizes the CTA's rows w, w + warps, ... (row j of the warp is
+// blockIdx.x + (w + warps j) gridDim.x), each loaded whole by a bulk copy (TMA) into the warp's buffer
+// j % depth; after row j the warp requests row j + depth into the same buffer.  Only the warp that owns a
+// buffer waits on it and refills it, so its k-th wait on a buffer always follows its own consumption of
+// phase k - 1 (a parity wait never runs ahead of the buffer).  warps x depth rows are in flight per SM with
+// no per-element load instructions.  The CTA stages the bank's column maps, smoothing and centres in shared
+// memory once.  When the low columns are the identity map, the smoothing all ones and there is no
+// centring (every BASELINE bank), a row is read as 16-byte runs: the absmax is a bf16x2 max, and the codes
+// come two at a time from packed float32 pairs (below); otherwise each value is gathered and divided as in
+// quant_row.  The float32 operations that decide the scale and the codes are quant_row's, so both are the
+// same.  A row whose copy does not land within timeout_ns gets a NaN scale and ends its warp's work (a
+// failed copy; no other path leaves a row unwritten).
+constexpr int kStreamWarps = 16;
+constexpr int kStreamMaxBufs = 32;
+constexpr int kStreamBarBytes = kStreamMaxBufs * 8;
+
+// Four codes (the low bytes of a, b, c, d) as one little-endian word.
+REAX_DEVI uint32_t pack4_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// Codes of four bf16 pairs (the words of a 16-byte run) for scale / inv = rcp_rn(scale), as 8 bytes.
+// Per pair: q = x * inv, rounded by adding and removing 1.5 * 2^23.  quant_rint_div's bound says rint(q)
+// is rint(div_rn(x, scale)) unless q is within 2^-14 of a half-integer; the packed check
+// (q - rint(q))^2 - (1/4 - 2^-14) < 0 is that bound give or take far less than its margin, and q^2 < 16192
+// (|q| < 127.24) keeps the clamp at +-127 a no-op (the sum's low byte is then the code).  A run with any other value (a
+// NaN fails both checks) is coded by quant_rint_div and the clamp, value by value.
+REAX_DEVI uint2 quant_codes8_packed(const uint4 v, float scale, float inv) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const uint64_t inv2 = f2(inv, inv), magic2 = f2(12582912.0f, 12582912.0f);
+    const uint64_t lim2 = f2(-(0.25f - 6.103515625e-05f), -(0.25f - 6.103515625e-05f));
+    const uint64_t top2 = f2(-16192.0f, -16192.0f);
+    uint32_t r[8];
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint64_t q = mul2_rn(bf16x2_to_f2(w[i]), inv2);
+        const uint64_t s2 = add2_rn(q, magic2);
+        const uint64_t e = sub2_rn(q, sub2_rn(s2, magic2));
+        const uint64_t t = fma2_rn(e, e, lim2);
+        const uint64_t u = fma2_rn(q, q, top2);
+        ok = ok && f2_lo(t) < 0.f && f2_hi(t) < 0.f && f2_lo(u) < 0.f && f2_hi(u) < 0.f;
+        r[2 * i] = __float_as_uint(f2_lo(s2));
+        r[2 * i + 1] = __float_as_uint(f2_hi(s2));
+    }
+    if (!ok) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float x = __uint_as_float(i % 2 == 0 ? w[i / 2] << 16 : w[i / 2] & 0xFFFF0000u);
+            r[i] = static_cast<uint32_t>(static_cast<int>(fminf(fmaxf(quant_rint_div<true>(x, scale, inv), -127.f), 127.f)));
+        }
+    }
+    return make_uint2(pack4_low_bytes(r[0], r[1], r[2], r[3]), pack4_low_bytes(r[4], r[5], r[6], r[7]));
+}
+
+template <int DIV>
+__global__ void __launch_bounds__(32 * kStreamWarps, 1) quant_rows_stream_kernel(
+    const __nv_bfloat16* __restrict__ x, const int* __restrict__ low_columns, const int* __restrict__ high_columns,
+    const float* __restrict__ smoothing, const float* __restrict__ centers, int8_t* __restrict__ low,
+    __nv_bfloat16* __restrict__ high, float* __restrict__ scales, int M, int K, int KL, int KH, int center, int depth,
+    unsigned long long timeout_ns) {
+    extern __shared__ __align__(128) uint8_t qs[];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int warps = static_cast<int>(blockDim.x) / 32;
+    const int nbuf = warps * depth;                              // the host keeps it <= kStreamMaxBufs
+    const uint32_t row_bytes = static_cast<uint32_t>(K) * 2u;   // the host keeps K % 8 == 0
+    uint64_t* bars = reinterpret_cast<uint64_t*>(qs);           // [warp][depth]
+    uint8_t* rows = qs + kStreamBarBytes;                        // [warp][depth][K] bf16
+    int* lc_s = reinterpret_cast<int*>(rows + static_cast<size_t>(nbuf) * row_bytes);
+    float* sm_s = reinterpret_cast<float*>(lc_s + KL);
+    float* ce_s = sm_s + KL;                                     // KL floats when center
+    int* hc_s = reinterpret_cast<int*>(ce_s + (center ? KL : 0));
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < nbuf; ++i) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    grid_dependency_wait();
+    grid_dependents_launch();
+    // row j of this warp, its buffer and that buffer's barrier
+    auto row_of = [&](int j) { return static_cast<int>(blockIdx.x) + (warp + warps * j) * static_cast<int>(gridDim.x); };
+    auto slot_of = [&](int j) { return warp * depth + j % depth; };
+    auto buf_of = [&](int j) { return reinterpret_cast<__nv_bfloat16*>(rows + static_cast<size_t>(slot_of(j)) * row_bytes); };
+    auto fetch = [&](int j) {
+        const int r = row_of(j);
+        if (r >= M) return;
+        mbar_arrive_expect_tx(&bars[slot_of(j)], row_bytes);
+        bulk_load(buf_of(j), x + static_cast<size_t>(r) * K, row_bytes, &bars[slot_of(j)]);
+    };
+    if (lane == 0)
+        for (int j = 0; j < depth; ++j) fetch(j);
+    // the bank's maps, while the first rows are in flight
+    bool ident = true, unit = true;
+    for (int c = threadIdx.x; c < KL; c += blockDim.x) {
+        const int src = __ldg(low_columns + c);
+        const float sv = __ldg(smoothing + c);
+        lc_s[c] = src;
+        sm_s[c] = sv;
+        if (center) ce_s[c] = __ldg(centers + c);
+        ident = ident && src == c;
+        unit = unit && sv == 1.0f;
+    }
+    for (int c = threadIdx.x; c < KH; c += blockDim.x) hc_s[c] = __ldg(high_columns + c);
+    const bool fast = __syncthreads_and(ident && unit && !center && (KL & 7) == 0) != 0;
+    unit = __syncthreads_and(unit) != 0;
+
+    for (int j = 0;; ++j) {
+        const int r = row_of(j);
+        if (r >= M) break;
+        const __nv_bfloat16* xb = buf_of(j);
+        // every lane waits (its own view of the copy); the warp goes on only if all saw it land
+        const bool landed = mbar_wait_bounded(&bars[slot_of(j)], static_cast<uint32_t>(j / depth) & 1u, timeout_ns,
+                                              nullptr);
+        if (!__all_sync(0xffffffffu, landed)) {
+            if (lane == 0) scales[r] = __int_as_float(0x7fffffff);
+            break;
+        }
+        // x / 1 is x under both divisions (unit smoothing skips them)
+        auto value = [&](int c) {
+            float t = __bfloat162float(xb[lc_s[c]]);
+            if (center) t = __fsub_rn(t, ce_s[c]);
+            return unit ? t : quant_div<DIV>(t, sm_s[c]);
+        };
+        if (KL > 0) {
+            float amax;
+            if (fast) {
+                // |x| of bf16 pairs by masking the sign bits; a bf16x2 max keeps the larger (NaN dropped, as
+                // fmaxf does), which is exactly the float32 absmax of the same values
+                __nv_bfloat162 m2 = __floats2bfloat162_rn(0.f, 0.f);
+#pragma unroll 4
+                for (int c8 = lane; c8 < KL / 8; c8 += 32) {
+                    const uint4 v = reinterpret_cast<const uint4*>(xb)[c8];
+                    const uint32_t w[4] = {v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu, v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, *reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+                }
+                amax = fmaxf(__low2float(m2), __high2float(m2));
+            } else {
+                amax = 0.f;
+                for (int c = lane; c < KL; c += 32) amax = fmaxf(amax, fabsf(value(c)));
+            }
+            amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+            const float scale = quant_div<DIV>(fmaxf(amax, 1.0e-12f), 127.0f);
+            const float inv = __frcp_rn(scale);
+            if (lane == 0) scales[r] = scale;
+            int8_t* lr = low + static_cast<size_t>(r) * KL;
+            if (fast) {
+#pragma unroll 2
+                for (int c8 = lane; c8 < KL / 8; c8 += 32)
+                    *reinterpret_cast<uint2*>(lr + 8 * c8) = quant_codes8_packed(reinterpret_cast<const uint4*>(xb)[c8], scale, inv);
+            } else {
+                for (int c = lane; c < KL; c += 32)
+                    lr[c] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(quant_rint_div<true>(value(c), scale, inv), -127.f), 127.f)));
+            }
+        } else if (lane == 0) {
+            scales[r] = 1.0f;
+        }
+        __nv_bfloat16* hr = high + static_cast<size_t>(r) * KH;
+        for (int c = lane; c < KH; c += 32) hr[c] = xb[hc_s[c]];
+        // every lane has read the buffer before the copy of the warp's row j + depth lands in it
+        __syncwarp();
+        fence_proxy_async_smem();
+        if (lane == 0) fetch(j + depth);
+    }
+}
+
+// Shared memory of quant_rows_stream_kernel with nbuf (= warps x depth) row buffers of K columns.
+inline size_t quant_stream_smem(int K, int KL, int KH, int center, int nbuf) {
+    return static_cast<size_t>(kStreamBarBytes) + static_cast<size_t>(nbuf) * K * 2 +
+           static_cast<size_t>(KL) * 4 * (center ? 3 : 2) + static_cast<size_t>(KH) * 4;
+}
+
 // ---------------------------------------------------------------------------- a2: grouped quantization
 // grid (M, P): row `blockIdx.x`, group `blockIdx.y` (reaxv2/quantize.py:31-52).  Sources of -1 pad a
 // group and quantize as 0; the centre is always subtracted; the codes are not clamped.
@@ -391,11 +564,6 @@ REAX_DEVI float rot_absmax(const uint64_t (&p)[R][V / 2]) {
 #pragma unroll
         for (int i = 0; i < V / 2; ++i) m = fmaxf(m, fmaxf(fabsf(f2_lo(p[k][i])), fabsf(f2_hi(p[k][i]))));
     return m;
-}
-
-// Four codes (the low bytes of a, b, c, d) as one little-endian word.
-REAX_DEVI uint32_t pack4_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 // The codes float2int_rn(div_rn(v, scale)) of the thread's values, as bytes in the flat order k V + j.

@@ -190,6 +190,15 @@ def test_rank_shard_shapes(M, Hh):
     assert _native.read_status(ws) == 0, _native.describe_status(_native.read_status(ws))
 
 
+@pytest.mark.parametrize("M,K,Hh", [(512, 1024, 128), (513, 1024, 1024), (1000, 512, 2816), (2304, 2560, 1536),
+                                    (777, 4096, 384)])
+def test_cta_pair_tiles(M, K, Hh):
+    """Many tokens without BF16 columns take CTA-pair tiles (256 token rows over two SMs, tcgen05
+    cta_group::2): ragged last pair (one CTA of it wholly past M), fewer tiles than pairs, one n-tile."""
+    g = H.gen(M * 3 + K + Hh)
+    compare_int8(H.activations(g, M, K), H.int8_bank(g, K, Hh))
+
+
 def test_cfg3_prefill_rows_sample():
     """BASELINE config 3 (M=4096, K=4096, H=14336): full GPU run, oracle on a sample of rows."""
     g = H.gen(3)
