@@ -59,7 +59,7 @@ struct DeviceInfo {
 };
 // Shared memory the many-rows quantizer may use per CTA (one CTA per SM), and the rows from which it runs.
 constexpr size_t kQuantStreamSmemMax = 227 * 1024;
-constexpr int kQuantStreamMinRows = 1 << 30;   // off until it measures faster than the 128-thread rows kernel
+constexpr int kQuantStreamMinRowsPerSm = 4;
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mutex;
 
@@ -70,7 +70,7 @@ enum Variant : int {
 
 // Token rows from which an INT8 gate/up launch without BF16 columns takes CTA-pair tiles (256 token rows x
 // 128 gate + 128 up columns per pair, tcgen05 cta_group::2).
-constexpr int kPairMinRows = 1 << 30;   // CTA-pair tiles: off until they measure faster
+constexpr int kPairMinRows = 512;
 // Stages of a pair's ring: [half of B | A box] of 32 KiB each in the same pool as four 48 KiB stages.
 constexpr int kPairStages = 6;
 
@@ -625,15 +625,16 @@ int reax_quant_rows(const void* x, const int32_t* low_columns, const int32_t* hi
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // many rows: persistent CTAs streaming whole rows into a ring of shared-memory buffers by bulk copies,
     // as many rows in flight per SM as the shared memory holds (at most kStreamMaxBufs)
-    if (M > kQuantStreamMinRows && aligned_x) {
-        // row buffers that fit, then warps x depth of them: two rows in flight per warp when that still
-        // leaves at least 8 warps, else one row for each of up to kStreamWarps warps
+    if (M > kQuantStreamMinRowsPerSm * info->sms && aligned_x) {
+        // row buffers that fit, shared out as groups x depth: the most rows in flight, then the most groups
+        // (of kStreamGroupWarps warps, at most kStreamMaxGroups)
         int nbuf = reax::kStreamMaxBufs;
         while (nbuf > 0 && reax::quant_stream_smem(K, KL, KH, center, nbuf) > kQuantStreamSmemMax) --nbuf;
-        const int depth = nbuf >= 16 ? 2 : 1;
-        const int warps = std::min(reax::kStreamWarps, nbuf / depth);
-        if (warps >= 4) {
-            const size_t smem = reax::quant_stream_smem(K, KL, KH, center, warps * depth);
+        int groups = 0, depth = 0;
+        for (int g = 2; g <= reax::kStreamMaxGroups; ++g)
+            if (g * (nbuf / g) >= groups * depth) groups = g, depth = nbuf / g;
+        if (groups >= 2 && depth >= 1) {
+            const size_t smem = reax::quant_stream_smem(K, KL, KH, center, groups * depth);
             if (!info->stream_smem_set) {
                 cudaError_t e = cudaFuncSetAttribute(reax::quant_rows_stream_kernel<kQuantDivision>,
                                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -643,7 +644,7 @@ int reax_quant_rows(const void* x, const int32_t* low_columns, const int32_t* hi
             }
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(static_cast<unsigned>(std::min(M, info->sms)), 1, 1);
-            cfg.blockDim = dim3(32 * warps, 1, 1);
+            cfg.blockDim = dim3(32 * reax::kStreamGroupWarps * groups, 1, 1);
             cfg.dynamicSmemBytes = smem;
             cfg.stream = s;
             cudaLaunchAttribute attr[1];

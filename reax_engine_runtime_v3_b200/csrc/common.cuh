@@ -193,13 +193,17 @@ REAX_DEVI uint32_t cluster_map(const void* p, uint32_t rank) {
 REAX_DEVI void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// Arrivals on an mbarrier of either CTA of the pair, with the default (CTA-scope release) semantics: a
+// cluster-scope release puts a cluster-wide memory barrier in front of every arrival, which waits for the
+// thread's earlier copies and so serialises a producer's boxes.  The data these arrivals publish is TMA
+// bytes (counted by complete_tx) or TMEM reads (ordered by tcgen05.fence::before_thread_sync), neither
+// of which needs it.
 REAX_DEVI void mbar_arrive_expect_tx_cluster(uint32_t bar_cluster_addr, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cluster_addr),
-                 "r"(bytes)
+    asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cluster_addr), "r"(bytes)
                  : "memory");
 }
 REAX_DEVI void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
 }
 // Tiled load of one box into this CTA's shared memory whose completion is counted on an mbarrier of either
 // CTA of the pair (bar_cluster_addr: a shared::cluster address).  No multicast: each CTA loads its own boxes.

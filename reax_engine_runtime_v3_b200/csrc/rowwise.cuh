@@ -221,22 +221,26 @@ __global__ void __launch_bounds__(THREADS) quant_rows_kernel(const __nv_bfloat16
     for (int c = threadIdx.x; c < KH; c += blockDim.x) hr[c] = xr[__ldg(high_columns + c)];
 }
 
-// Many rows (prefill): persistent CTAs of `warps` warps (at most kStreamWarps), each with its own `depth`
-// row buffers in shared memory.  Warp w quantizes the CTA's rows w, w + warps, ... (row j of the warp is
-// blockIdx.x + (w + warps j) gridDim.x), each loaded whole by a bulk copy (TMA) into the warp's buffer
-// j % depth; after row j the warp requests row j + depth into the same buffer.  Only the warp that owns a
-// buffer waits on it and refills it, so its k-th wait on a buffer always follows its own consumption of
-// phase k - 1 (a parity wait never runs ahead of the buffer).  warps x depth rows are in flight per SM with
-// no per-element load instructions.  The CTA stages the bank's column maps, smoothing and centres in shared
-// memory once.  When the low columns are the identity map, the smoothing all ones and there is no
-// centring (every BASELINE bank), a row is read as 16-byte runs: the absmax is a bf16x2 max, and the codes
-// come two at a time from packed float32 pairs (below); otherwise each value is gathered and divided as in
-// quant_row.  The float32 operations that decide the scale and the codes are quant_row's, so both are the
-// same.  A row whose copy does not land within timeout_ns gets a NaN scale and ends its warp's work (a
-// failed copy; no other path leaves a row unwritten).
-constexpr int kStreamWarps = 16;
+// Many rows (prefill): persistent CTAs of `groups` groups of kStreamGroupWarps warps, each group with its
+// own `depth` row buffers in shared memory.  Group g quantizes the CTA's rows g, g + groups, ... (row j of
+// the group is blockIdx.x + (g + groups j) gridDim.x), each loaded whole by a bulk copy (TMA) into the
+// group's buffer j % depth; once every thread of the group has read row j, the group requests row
+// j + depth into the same buffer.  Only the group that owns a buffer waits on it and refills it, so its
+// k-th wait on a buffer always follows its own consumption of phase k - 1 (a parity wait never runs ahead
+// of the buffer).  groups x depth rows are in flight per SM with no per-element load instructions, and
+// the warps of a group split each row's columns (the absmax is combined through shared memory at a named
+// barrier of the group), so enough warps run per SM to hide the arithmetic's latency.  The CTA stages the
+// bank's column maps, smoothing and centres in shared memory once.  When the low columns are the identity
+// map, the smoothing all ones and there is no centring (every BASELINE bank), a row is read as 16-byte
+// runs: the absmax is a bf16x2 max, and the codes come two at a time from packed float32 pairs (below);
+// otherwise each value is gathered and divided as in quant_row.  The float32 operations that decide the
+// scale and the codes are quant_row's, so both are the same.  A row whose copy does not land within
+// timeout_ns gets a NaN scale and ends its group's work (a failed copy; no other path leaves a row
+// unwritten).
+constexpr int kStreamGroupWarps = 4;
+constexpr int kStreamMaxGroups = 6;
 constexpr int kStreamMaxBufs = 32;
-constexpr int kStreamBarBytes = kStreamMaxBufs * 8;
+constexpr int kStreamBarBytes = kStreamMaxBufs * 8 + kStreamMaxGroups * kStreamGroupWarps * 4;
 
 // Four codes (the low bytes of a, b, c, d) as one little-endian word.
 REAX_DEVI uint32_t pack4_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -278,18 +282,21 @@ REAX_DEVI uint2 quant_codes8_packed(const uint4 v, float scale, float inv) {
 }
 
 template <int DIV>
-__global__ void __launch_bounds__(32 * kStreamWarps, 1) quant_rows_stream_kernel(
+__global__ void __launch_bounds__(32 * kStreamGroupWarps * kStreamMaxGroups, 1) quant_rows_stream_kernel(
     const __nv_bfloat16* __restrict__ x, const int* __restrict__ low_columns, const int* __restrict__ high_columns,
     const float* __restrict__ smoothing, const float* __restrict__ centers, int8_t* __restrict__ low,
     __nv_bfloat16* __restrict__ high, float* __restrict__ scales, int M, int K, int KL, int KH, int center, int depth,
     unsigned long long timeout_ns) {
     extern __shared__ __align__(128) uint8_t qs[];
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int warps = static_cast<int>(blockDim.x) / 32;
-    const int nbuf = warps * depth;                              // the host keeps it <= kStreamMaxBufs
+    constexpr int GT = 32 * kStreamGroupWarps;                   // threads of a group
+    const int group = threadIdx.x / GT, gt = threadIdx.x % GT;   // group, thread within it
+    const int gw = gt / 32, lane = threadIdx.x % 32;
+    const int groups = static_cast<int>(blockDim.x) / GT;
+    const int nbuf = groups * depth;                             // the host keeps it <= kStreamMaxBufs
     const uint32_t row_bytes = static_cast<uint32_t>(K) * 2u;   // the host keeps K % 8 == 0
-    uint64_t* bars = reinterpret_cast<uint64_t*>(qs);           // [warp][depth]
-    uint8_t* rows = qs + kStreamBarBytes;                        // [warp][depth][K] bf16
+    uint64_t* bars = reinterpret_cast<uint64_t*>(qs);           // [group][depth]
+    float* red = reinterpret_cast<float*>(qs + kStreamMaxBufs * 8) + group * kStreamGroupWarps;   // [warp of group]
+    uint8_t* rows = qs + kStreamBarBytes;                        // [group][depth][K] bf16
     int* lc_s = reinterpret_cast<int*>(rows + static_cast<size_t>(nbuf) * row_bytes);
     float* sm_s = reinterpret_cast<float*>(lc_s + KL);
     float* ce_s = sm_s + KL;                                     // KL floats when center
@@ -301,9 +308,9 @@ __global__ void __launch_bounds__(32 * kStreamWarps, 1) quant_rows_stream_kernel
     __syncthreads();
     grid_dependency_wait();
     grid_dependents_launch();
-    // row j of this warp, its buffer and that buffer's barrier
-    auto row_of = [&](int j) { return static_cast<int>(blockIdx.x) + (warp + warps * j) * static_cast<int>(gridDim.x); };
-    auto slot_of = [&](int j) { return warp * depth + j % depth; };
+    // row j of this group, its buffer and that buffer's barrier
+    auto row_of = [&](int j) { return static_cast<int>(blockIdx.x) + (group + groups * j) * static_cast<int>(gridDim.x); };
+    auto slot_of = [&](int j) { return group * depth + j % depth; };
     auto buf_of = [&](int j) { return reinterpret_cast<__nv_bfloat16*>(rows + static_cast<size_t>(slot_of(j)) * row_bytes); };
     auto fetch = [&](int j) {
         const int r = row_of(j);
@@ -311,7 +318,8 @@ __global__ void __launch_bounds__(32 * kStreamWarps, 1) quant_rows_stream_kernel
         mbar_arrive_expect_tx(&bars[slot_of(j)], row_bytes);
         bulk_load(buf_of(j), x + static_cast<size_t>(r) * K, row_bytes, &bars[slot_of(j)]);
     };
-    if (lane == 0)
+    auto group_sync = [&] { named_bar_sync(1 + group, GT); };
+    if (gt == 0)
         for (int j = 0; j < depth; ++j) fetch(j);
     // the bank's maps, while the first rows are in flight
     bool ident = true, unit = true;
@@ -332,11 +340,18 @@ __global__ void __launch_bounds__(32 * kStreamWarps, 1) quant_rows_stream_kernel
         const int r = row_of(j);
         if (r >= M) break;
         const __nv_bfloat16* xb = buf_of(j);
-        // every lane waits (its own view of the copy); the warp goes on only if all saw it land
+        // every thread waits (its own view of the copy); the group goes on only if all saw it land
         const bool landed = mbar_wait_bounded(&bars[slot_of(j)], static_cast<uint32_t>(j / depth) & 1u, timeout_ns,
                                               nullptr);
-        if (!__all_sync(0xffffffffu, landed)) {
-            if (lane == 0) scales[r] = __int_as_float(0x7fffffff);
+        const bool warp_landed = __all_sync(0xffffffffu, landed);
+        if (lane == 0) red[gw] = warp_landed ? 0.f : 1.f;
+        group_sync();
+        bool failed = false;
+#pragma unroll
+        for (int w = 0; w < kStreamGroupWarps; ++w) failed = failed || red[w] != 0.f;
+        group_sync();   // every thread has read the flags before red is reused for the maximum
+        if (failed) {
+            if (gt == 0) scales[r] = __int_as_float(0x7fffffff);
             break;
         }
         // x / 1 is x under both divisions (unit smoothing skips them)
@@ -352,7 +367,7 @@ __global__ void __launch_bounds__(32 * kStreamWarps, 1) quant_rows_stream_kernel
                 // fmaxf does), which is exactly the float32 absmax of the same values
                 __nv_bfloat162 m2 = __floats2bfloat162_rn(0.f, 0.f);
 #pragma unroll 4
-                for (int c8 = lane; c8 < KL / 8; c8 += 32) {
+                for (int c8 = gt; c8 < KL / 8; c8 += GT) {
                     const uint4 v = reinterpret_cast<const uint4*>(xb)[c8];
                     const uint32_t w[4] = {v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu, v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu};
 #pragma unroll
@@ -361,30 +376,36 @@ __global__ void __launch_bounds__(32 * kStreamWarps, 1) quant_rows_stream_kernel
                 amax = fmaxf(__low2float(m2), __high2float(m2));
             } else {
                 amax = 0.f;
-                for (int c = lane; c < KL; c += 32) amax = fmaxf(amax, fabsf(value(c)));
+                for (int c = gt; c < KL; c += GT) amax = fmaxf(amax, fabsf(value(c)));
             }
+            // the group's maximum: one redux per warp, the warps' maxima through shared memory
             amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+            if (lane == 0) red[gw] = amax;
+            group_sync();
+#pragma unroll
+            for (int w = 0; w < kStreamGroupWarps; ++w) amax = fmaxf(amax, red[w]);
             const float scale = quant_div<DIV>(fmaxf(amax, 1.0e-12f), 127.0f);
             const float inv = __frcp_rn(scale);
-            if (lane == 0) scales[r] = scale;
+            if (gt == 0) scales[r] = scale;
             int8_t* lr = low + static_cast<size_t>(r) * KL;
             if (fast) {
 #pragma unroll 2
-                for (int c8 = lane; c8 < KL / 8; c8 += 32)
+                for (int c8 = gt; c8 < KL / 8; c8 += GT)
                     *reinterpret_cast<uint2*>(lr + 8 * c8) = quant_codes8_packed(reinterpret_cast<const uint4*>(xb)[c8], scale, inv);
             } else {
-                for (int c = lane; c < KL; c += 32)
+                for (int c = gt; c < KL; c += GT)
                     lr[c] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(quant_rint_div<true>(value(c), scale, inv), -127.f), 127.f)));
             }
-        } else if (lane == 0) {
+        } else if (gt == 0) {
             scales[r] = 1.0f;
         }
         __nv_bfloat16* hr = high + static_cast<size_t>(r) * KH;
-        for (int c = lane; c < KH; c += 32) hr[c] = xb[hc_s[c]];
-        // every lane has read the buffer before the copy of the warp's row j + depth lands in it
-        __syncwarp();
+        for (int c = gt; c < KH; c += GT) hr[c] = xb[hc_s[c]];
+        // every thread of the group has read the buffer (and the maxima) before the copy of the group's row
+        // j + depth lands in it
         fence_proxy_async_smem();
-        if (lane == 0) fetch(j + depth);
+        group_sync();
+        if (gt == 0) fetch(j + depth);
     }
 }
 
