@@ -1,7 +1,6 @@
 """Generate golden vectors by running the reference's own Triton kernels on the CPU.
 
-Run in a container where the reference project is mounted (its path as the first argument, or the
-default mount point).  The reference's ``reaxv2/quantize.py`` kernels (``_prepare``,
+Run in a container where the reference project is mounted (its root as the first argument).  The reference's ``reaxv2/quantize.py`` kernels (``_prepare``,
 ``prepare_kernel``, ``reduce_kernel``) and ``runtime/mixed_origin_bf16.py``'s ``fold`` are
 executed unmodified by Triton's CPU interpreter (``TRITON_INTERPRET=1``).  The interpreter cannot
 lower the two libdevice calls of ``quantize.py:20,44``; they are supplied with their documented
@@ -187,4 +186,6 @@ def main(reference_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) < 2:
+        sys.exit("usage: python tests/golden/gen_golden.py <reference root>")
+    main(sys.argv[1])
