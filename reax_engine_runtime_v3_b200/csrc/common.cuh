@@ -73,6 +73,29 @@ REAX_DEVI bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_
     }
 }
 
+// mbar_wait_bounded for waits that are expected to last (a copy in flight): each try asks the hardware to
+// suspend the thread for up to suspend_ns while the phase is incomplete, so a waiting warp does not take
+// issue slots from the warps that work.
+REAX_DEVI bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t suspend_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+        : "memory");
+    return ok != 0;
+}
+REAX_DEVI bool mbar_wait_bounded_suspend(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+    if (mbar_try_wait_suspend(bar, parity, 1000u)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait_suspend(bar, parity, 1000u)) return true;
+        if (global_timer_ns() - t0 > limit_ns) return false;
+    }
+}
+
 // ---------------------------------------------------------------------------------------------------------- TMA
 REAX_DEVI void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

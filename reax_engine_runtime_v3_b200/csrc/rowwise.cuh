@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(THREADS) quant_rows_kernel(const __nv_bfloat16
 constexpr int kStreamGroupWarps = 4;
 constexpr int kStreamMaxGroups = 6;
 constexpr int kStreamMaxBufs = 32;
-constexpr int kStreamBarBytes = kStreamMaxBufs * 8 + kStreamMaxGroups * kStreamGroupWarps * 4;
+constexpr int kStreamBarBytes = kStreamMaxBufs * 8 + kStreamMaxGroups * 2 * kStreamGroupWarps * 4;
 
 // Four codes (the low bytes of a, b, c, d) as one little-endian word.
 REAX_DEVI uint32_t pack4_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -295,7 +295,8 @@ __global__ void __launch_bounds__(32 * kStreamGroupWarps * kStreamMaxGroups, 1) 
     const int nbuf = groups * depth;                             // the host keeps it <= kStreamMaxBufs
     const uint32_t row_bytes = static_cast<uint32_t>(K) * 2u;   // the host keeps K % 8 == 0
     uint64_t* bars = reinterpret_cast<uint64_t*>(qs);           // [group][depth]
-    float* red = reinterpret_cast<float*>(qs + kStreamMaxBufs * 8) + group * kStreamGroupWarps;   // [warp of group]
+    // the warps' maxima of a row, two slots so that row j + 1 can write while row j's are still read
+    float* red = reinterpret_cast<float*>(qs + kStreamMaxBufs * 8) + group * 2 * kStreamGroupWarps;   // [2][warp]
     uint8_t* rows = qs + kStreamBarBytes;                        // [group][depth][K] bf16
     int* lc_s = reinterpret_cast<int*>(rows + static_cast<size_t>(nbuf) * row_bytes);
     float* sm_s = reinterpret_cast<float*>(lc_s + KL);
@@ -336,32 +337,25 @@ __global__ void __launch_bounds__(32 * kStreamGroupWarps * kStreamMaxGroups, 1) 
     const bool fast = __syncthreads_and(ident && unit && !center && (KL & 7) == 0) != 0;
     unit = __syncthreads_and(unit) != 0;
 
+    // One group barrier per row: after it every thread has finished row j - 1 (so its buffer is refilled
+    // with row j - 1 + depth) and every warp's maximum of row j (or its failed copy, as -1) is visible.
     for (int j = 0;; ++j) {
         const int r = row_of(j);
         if (r >= M) break;
         const __nv_bfloat16* xb = buf_of(j);
-        // every thread waits (its own view of the copy); the group goes on only if all saw it land
-        const bool landed = mbar_wait_bounded(&bars[slot_of(j)], static_cast<uint32_t>(j / depth) & 1u, timeout_ns,
-                                              nullptr);
+        float* red_j = red + (j & 1) * kStreamGroupWarps;
+        // every thread waits (its own view of the copy); a warp in which any thread gave up reports -1
+        const bool landed = mbar_wait_bounded_suspend(&bars[slot_of(j)], static_cast<uint32_t>(j / depth) & 1u,
+                                                      timeout_ns);
         const bool warp_landed = __all_sync(0xffffffffu, landed);
-        if (lane == 0) red[gw] = warp_landed ? 0.f : 1.f;
-        group_sync();
-        bool failed = false;
-#pragma unroll
-        for (int w = 0; w < kStreamGroupWarps; ++w) failed = failed || red[w] != 0.f;
-        group_sync();   // every thread has read the flags before red is reused for the maximum
-        if (failed) {
-            if (gt == 0) scales[r] = __int_as_float(0x7fffffff);
-            break;
-        }
         // x / 1 is x under both divisions (unit smoothing skips them)
         auto value = [&](int c) {
             float t = __bfloat162float(xb[lc_s[c]]);
             if (center) t = __fsub_rn(t, ce_s[c]);
             return unit ? t : quant_div<DIV>(t, sm_s[c]);
         };
-        if (KL > 0) {
-            float amax;
+        float amax = 0.f;
+        if (KL > 0 && warp_landed) {
             if (fast) {
                 // |x| of bf16 pairs by masking the sign bits; a bf16x2 max keeps the larger (NaN dropped, as
                 // fmaxf does), which is exactly the float32 absmax of the same values
@@ -375,15 +369,26 @@ __global__ void __launch_bounds__(32 * kStreamGroupWarps * kStreamMaxGroups, 1) 
                 }
                 amax = fmaxf(__low2float(m2), __high2float(m2));
             } else {
-                amax = 0.f;
                 for (int c = gt; c < KL; c += GT) amax = fmaxf(amax, fabsf(value(c)));
             }
-            // the group's maximum: one redux per warp, the warps' maxima through shared memory
+            // one redux per warp; the warps' maxima meet through shared memory at the group barrier
             amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
-            if (lane == 0) red[gw] = amax;
-            group_sync();
+        }
+        if (lane == 0) red_j[gw] = warp_landed ? amax : -1.0f;
+        fence_proxy_async_smem();   // this thread's reads of row j - 1's buffer come before its refill
+        group_sync();
+        if (gt == 0 && j > 0) fetch(j - 1 + depth);
+        bool failed = false;
 #pragma unroll
-            for (int w = 0; w < kStreamGroupWarps; ++w) amax = fmaxf(amax, red[w]);
+        for (int w = 0; w < kStreamGroupWarps; ++w) {
+            failed = failed || red_j[w] < 0.f;
+            amax = fmaxf(amax, red_j[w]);
+        }
+        if (failed) {
+            if (gt == 0) scales[r] = __int_as_float(0x7fffffff);
+            break;
+        }
+        if (KL > 0) {
             const float scale = quant_div<DIV>(fmaxf(amax, 1.0e-12f), 127.0f);
             const float inv = __frcp_rn(scale);
             if (gt == 0) scales[r] = scale;
@@ -401,11 +406,6 @@ __global__ void __launch_bounds__(32 * kStreamGroupWarps * kStreamMaxGroups, 1) 
         }
         __nv_bfloat16* hr = high + static_cast<size_t>(r) * KH;
         for (int c = gt; c < KH; c += GT) hr[c] = xb[hc_s[c]];
-        // every thread of the group has read the buffer (and the maxima) before the copy of the group's row
-        // j + depth lands in it
-        fence_proxy_async_smem();
-        group_sync();
-        if (gt == 0) fetch(j + depth);
     }
 }
 
