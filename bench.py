@@ -19,6 +19,9 @@ INT8-TOPS half of the metric, through the same public API, with the GEMM's TOP/s
 ``ref_kernel`` (the reference's own GPU implementation, its Triton quantizer and its native_hybrid8
 kernel built from source, timed per call on the same buckets and weights, next to ours).
 
+The default workload's line also carries ``cfg4`` at every N: BASELINE config 4 (X [8192, 8192], H = 28672)
+sharded the same way, per-rank GEMM TOP/s and the job's tokens/s.
+
 ``--impl reference`` times the reference arithmetic of the path on the host cores (the reference
 ships no CPU implementation of it; the timed code is the oracle's restatement, ``oracle/``), on
 rank 0 only: every bucket, every output column, one pass per step.
@@ -674,6 +677,35 @@ def prefill_record(banks, dev, cap, steps):
                    "reax_gate_up_i8_static on pre-quantized codes; torch._int_mm 8192^3 best of 5 measured in this run"}
 
 
+def cfg4_record(rank, world, dev, cap, steps):
+    """BASELINE config 4, the large MLP N-sharded over the ranks: X bf16 [8192, 8192] replicated, this
+    rank's H / world gate rows and the matching up rows of Wg/Wu int8 [28672, 8192], per-channel scales
+    U(5e-4, 5e-3).  Per rank: one gate_up.Native.project call (the replicated quantizer + this rank's
+    GEMM) and the GEMM alone, CUDA graphs over two weight copies, max over ranks.  tokens_per_s is the
+    job's (every rank produces its columns of all 8192 rows at once)."""
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native, gate_up_i8, quantize_rows
+    xs_cpu, banks, h = make_inputs("cfg4", rank, world, 2)
+    _, K, H, _, _, desc = WORKLOADS["cfg4"]
+    x = xs_cpu[0].to(dev)
+    M = x.shape[0]
+    nat = Native(None)
+    n_rep = max(2, steps // 4)
+    with torch.cuda.stream(cap):
+        call = graph_time(lambda r: nat.project(x, banks[r % 2], "hybrid8_b128n256_s64n256"), 2, n_rep, cap)
+        low, high, sc = quantize_rows(x, banks[0])
+        gemm = graph_time(lambda r: gate_up_i8(low, banks[r % 2].low_weight, high, banks[r % 2].high_weight, sc,
+                                               banks[r % 2].scales, banks[r % 2].bias, static_weights=True), 2, n_rep,
+                          cap)
+        quant = graph_time(lambda r: quantize_rows(x, banks[r % 2]), 2, n_rep, cap)
+    call, gemm, quant = (max_over_ranks(v, world) for v in (call, gemm, quant))
+    del banks, x, low, high, sc
+    torch.cuda.empty_cache()
+    return {"workload": desc, "H_per_rank": h, "tokens_per_s": M / call, "call_us": call * 1e6,
+            "gemm_us": gemm * 1e6, "quant_us": quant * 1e6, "gemm_tops_per_rank": gemm_ops(M, K, h) / gemm / 1e12,
+            "how": "per rank: CUDA graphs of back-to-back calls over 2 weight copies, max over ranks; the quantizer "
+                   "runs on every rank over the replicated activations; no collective"}
+
+
 def ref_kernel_record(banks, xs, dev, cap, steps):
     """The reference's own implementation of the path on this GPU, as reaxv2.gate_up.Native.project runs
     it (reaxv2/gate_up.py:29-37): its Triton _prepare, compiled ahead of time from the unmodified source,
@@ -888,7 +920,9 @@ def main():
 
     # Side records of the one-GPU default line (outside `value`): the prefill half of the metric (cfg3)
     # and the reference's own GPU implementation on the same buckets.
-    prefill = ref_kernel = None
+    prefill = ref_kernel = cfg4 = None
+    if shard_world == world and args.workload == DEFAULT_WORKLOAD and int8 and not args.no_side_records:
+        cfg4 = cfg4_record(rank, world, dev, cap, args.steps)
     if world == 1 and shard_world == 1 and args.workload == DEFAULT_WORKLOAD and int8 and not args.no_side_records:
         prefill = prefill_record(banks, dev, cap, args.steps)
         gx = torch.Generator().manual_seed(20261201)
@@ -1032,7 +1066,7 @@ def main():
                            "l2": f"{copies} rotating weight copies ({copies * 2 * h * K * (1 if int8 else 2) / 1e6:.0f} MB > 126 MB L2), "
                                  "a different copy on consecutive calls"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
-                "allgather": allgather, "prefill": prefill, "ref_kernel": ref_kernel,
+                "allgather": allgather, "prefill": prefill, "ref_kernel": ref_kernel, "cfg4": cfg4,
                 "device_status": status, "timing": "CUDA-graph replay of the captured step",
                 "eager_ms_per_step": eager_ms}
         print(json.dumps(line), flush=True)
