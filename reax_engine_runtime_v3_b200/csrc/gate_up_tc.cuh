@@ -824,12 +824,13 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         tmem_ld_pairs_sync<CH>(t_acc + t0, t_acc + n_tok + t0, g, u);
                     };
                     // one contributor's int32 partial of chunk c: gate and up columns, four tokens per int4
+                    // (lanes of no output column neither publish nor gather: their sums are never stored)
                     auto fetch = [&](const int4* src, int c, int4 (&pg)[CH / 2], int4 (&pu)[CH / 2]) {
 #pragma unroll
                         for (int i = 0; i < CH / 2; ++i) {
                             const int t = tok_lo + 2 * CH * c + 4 * i;
-                            pg[i] = __ldcg(src + (t / 4) * kBM + r_tile);
-                            pu[i] = __ldcg(src + ((n_tok + t) / 4) * kBM + r_tile);
+                            pg[i] = col_ok ? __ldcg(src + (t / 4) * kBM + r_tile) : make_int4(0, 0, 0, 0);
+                            pu[i] = col_ok ? __ldcg(src + ((n_tok + t) / 4) * kBM + r_tile) : make_int4(0, 0, 0, 0);
                         }
                     };
                     auto add = [&](uint32_t (&g)[2 * CH], uint32_t (&u)[2 * CH], const int4 (&pg)[CH / 2],
@@ -868,7 +869,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 #pragma unroll
                             for (int i = 0; i < CH / 2; ++i) {
                                 const int tw = 2 * CH * c + 4 * i;   // token offset within the warp's columns
-                                if (tw < per_warp) {
+                                if (col_ok && tw < per_warp) {
                                     __stcg(slot + ((tok_lo + tw) / 4) * kBM + r_tile,
                                            make_int4(g[4 * i], g[4 * i + 1], g[4 * i + 2], g[4 * i + 3]));
                                     __stcg(slot + ((n_tok + tok_lo + tw) / 4) * kBM + r_tile,
