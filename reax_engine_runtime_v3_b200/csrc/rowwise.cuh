@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(THREADS) quant_rows_kernel(const __nv_bfloat16
 // timeout_ns gets a NaN scale and ends its group's work (a failed copy; no other path leaves a row
 // unwritten).
 constexpr int kStreamGroupWarps = 4;
-constexpr int kStreamMaxGroups = 6;
+constexpr int kStreamMaxGroups = 8;
 constexpr int kStreamMaxBufs = 32;
 constexpr int kStreamBarBytes = kStreamMaxBufs * 8 + kStreamMaxGroups * 2 * kStreamGroupWarps * 4;
 
