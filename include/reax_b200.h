@@ -54,8 +54,9 @@ REAX_API const char* reax_last_error(void);
  * workspace may not be used by two launches that can run at the same time (use one per stream). */
 REAX_API size_t reax_workspace_bytes(int device);
 
-/* SM share of the GEMM launches on `stream`: their tile plans and grids use at most `sms` SMs (0 removes
- * the share: the whole GPU).  For callers that run several lanes at once (streams whose launches
+/* SM share of the decode GEMM launches on `stream` (at most 64 token rows: weight-streaming launches):
+ * their tile plans and grids use at most `sms` SMs (0 removes the share: the whole GPU).  Larger launches
+ * are compute-bound and always plan for the whole GPU.  For callers that run several lanes at once (streams whose launches
  * overlap, as the reference's two serving lanes do: runtime/bootstrap.py:29, vendor/s1eng/s1eng/kprio.py):
  * each lane's persistent grid then fits beside the other's instead of queueing for the whole GPU.
  * At most 64 streams hold a share.  No counterpart in the reference, whose kernels take fixed grids. */

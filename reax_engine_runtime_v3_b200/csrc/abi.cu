@@ -65,12 +65,16 @@ std::mutex g_dev_mutex;
 
 // The kernel variants: (epilogue, mode, BF16 columns added to INT8 accumulators).
 enum Variant : int {
-    kSwigluI8 = 0, kSwigluI8F, kSwigluBf16, kPlainI8, kPlainI8F, kPlainBf16, kSwapI8, kSwapBf16, kPairI8, kVariants
+    kSwigluI8 = 0, kSwigluI8F, kSwigluBf16, kPlainI8, kPlainI8F, kPlainBf16, kSwapI8, kSwapBf16, kPairI8, kPairBf16,
+    kVariants
 };
 
 // Token rows from which an INT8 gate/up launch without BF16 columns takes CTA-pair tiles (256 token rows x
 // 128 gate + 128 up columns per pair, tcgen05 cta_group::2).
 constexpr int kPairMinRows = 512;
+// Grouped INT8 projections with fewer tiles than SMs may split their tiles by K (parity-green, but the
+// down projection's 40-tile decode launches measured 16-17.6 us split against 10.3-11 us whole, so off).
+constexpr bool kSplitPlainTiles = false;   // measured slower at every decode shape
 // Stages of a pair's ring: [half of B | A box] of 32 KiB each in the same pool as four 48 KiB stages.
 constexpr int kPairStages = 6;
 
@@ -89,12 +93,14 @@ void* tc_kernel_ptr(int v) {
         case kSwapI8: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 0, false, true>);
         case kPairI8:
             return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 0, false, false, true>);
+        case kPairBf16:
+            return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 1, false, false, true>);
         default: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 1, false, true>);
     }
 }
 
 int variant_of(int epi, const reax::TcParams& p) {
-    if (p.cta_shift == 1) return kPairI8;
+    if (p.cta_shift == 1) return p.mode == 1 ? kPairBf16 : kPairI8;
     if (p.n_tok > 0) return p.mode == 1 ? kSwapBf16 : kSwapI8;
     if (epi == reax::kEpiSwiglu) return p.mode == 1 ? kSwigluBf16 : (p.kb_f16 > 0 ? kSwigluI8F : kSwigluI8);
     return p.mode == 1 ? kPlainBf16 : (p.kb_f16 > 0 ? kPlainI8F : kPlainI8);
@@ -182,8 +188,12 @@ StreamShare g_shares[kMaxStreamShares];
 int g_n_shares = 0;
 std::mutex g_share_mutex;
 
-// SMs the GEMM plans of `stream` may use on a device of `sms` SMs.
-int stream_sms(void* stream, int sms) {
+// SMs the GEMM plans of `stream` may use on a device of `sms` SMs, for a launch of M token rows.  The share
+// applies to weight-streaming (decode) launches of at most kSwapMaxRows rows, which are HBM- and latency-
+// bound and gain from running beside the other lane; larger launches are compute-bound and plan for the
+// whole GPU.
+int stream_sms(void* stream, int sms, int M) {
+    if (M > reax::kSwapMaxTok) return sms;
     std::lock_guard<std::mutex> lock(g_share_mutex);
     for (int i = 0; i < g_n_shares; ++i)
         if (g_shares[i].stream == stream) return std::min(sms, g_shares[i].sms);
@@ -363,10 +373,10 @@ bool plan_gate_up_tiles(reax::TcParams& p, int M, int H, int K_blocks, bool weig
 }
 
 int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
-    // Grouped / mixed-origin (plain epilogue) plans always deal whole tiles: their K-split path is not
-    // used (forced on, it measured slower and did not match the oracle), so refuse such a plan.
-    if (epi == reax::kEpiPlain && p.sk_iters > 0)
-        return fail(REAX_ERR_INVALID, "internal: a plain-epilogue plan must not split tiles by K");
+    // Plain-epilogue plans split tiles by K only for INT8 grouped tiles without BF16 columns (the float32
+    // mixed-origin partials and the BF16-column association are never split).
+    if (epi == reax::kEpiPlain && p.sk_iters > 0 && (p.mode != 0 || p.kb_f16 > 0))
+        return fail(REAX_ERR_INVALID, "internal: this plain-epilogue plan must not split tiles by K");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(reax::kCtlThreads + 32 * kEpiWarps, 1, 1);
@@ -501,6 +511,18 @@ int check_gate_up_args(const char* who, const int8_t* A, const int8_t* W, const 
     return REAX_OK;
 }
 
+// CTA-pair tiles: 256 token rows per pair (128 per CTA), 128 gate + 128 up rows, a six-stage ring of
+// [half of B | A box] stages of 32 KiB.
+void set_pair_tiles(reax::TcParams& p) {
+    p.cta_shift = 1;
+    p.tile_rows = 128;
+    p.tile_rows8 = 128;
+    p.a_rows = reax::kBM;
+    p.stages = kPairStages;
+    p.stage_bytes = 2 * reax::kBM * reax::kRowBytes;
+    p.out_vec16 = 0;
+}
+
 // Tile plan, tensor maps and operands of an INT8 gate/up launch (everything but the scratch pointers,
 // early_b and the schedule), shared by the workspace and the allocation-free entry points so that both
 // run the same kernel on the same plan.  *split_ok: whether the plan may split tiles by K.
@@ -513,13 +535,7 @@ int fill_gate_up_params(reax::TcParams& p, int sms, bool pair_ok, const int8_t* 
     // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
     const bool swap = !pair && plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, sms, split_ok);
     if (pair) {
-        p.cta_shift = 1;
-        p.tile_rows = 128;
-        p.tile_rows8 = 128;
-        p.a_rows = reax::kBM;
-        p.stages = kPairStages;
-        p.stage_bytes = 2 * reax::kBM * reax::kRowBytes;
-        p.out_vec16 = 0;
+        set_pair_tiles(p);
         *split_ok = false;
     }
     int rc;
@@ -575,7 +591,7 @@ int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const vo
     if ((rc = carve_workspace(workspace, workspace_bytes, info->sms, &ws)) != REAX_OK) return rc;
     reax::TcParams p;
     bool split_ok = false;
-    const int sms = stream_sms(stream, info->sms);
+    const int sms = stream_sms(stream, info->sms, M);
     if ((rc = fill_gate_up_params(p, sms, info->pair_clusters > 0, A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &split_ok)) != REAX_OK)
         return rc;
     p.ws_partials = ws.partials;
@@ -877,8 +893,11 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     reax::TcParams p;
     init_params(p);
     bool split_ok = false;   // BF16 tiles are never split
-    const int sms = stream_sms(stream, info->sms);
-    const bool swap = plan_gate_up_tiles(p, M, N2 / 2, K / 64, true, false, sms, &split_ok);
+    const int sms = stream_sms(stream, info->sms, M);
+    // many tokens: CTA-pair tiles of 256 token rows (as the INT8 gate/up), else the single-CTA plans
+    const bool pair = M >= kPairMinRows && sms >= 2 && info->pair_clusters > 0;
+    const bool swap = !pair && plan_gate_up_tiles(p, M, N2 / 2, K / 64, true, false, sms, &split_ok);
+    if (pair) set_pair_tiles(p);
     if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : p.a_rows)) != REAX_OK)
         return rc;
     if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, K, N2, K, p.tile_rows)) !=
@@ -892,7 +911,7 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     p.ldo = ldo;
     p.kb_int = 0;
     p.kb_f16 = K / 64;
-    p.m_tiles = (M + reax::kBM - 1) / reax::kBM;
+    p.m_tiles = (M + (reax::kBM << p.cta_shift) - 1) / (reax::kBM << p.cta_shift);
     p.n_tiles = (N2 / 2 + p.tile_rows - 1) / p.tile_rows;
     p.tiles = p.m_tiles * p.n_tiles;
     p.mode = 1;
@@ -904,7 +923,8 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     int grid = 0;
     // float32 partial sums of one tile would round differently from one unsplit accumulation, which
     // would make a row's result depend on the batch it came in: BF16 tiles are never split.
-    plan_schedule(p, sms, false, &grid);
+    if (p.cta_shift) plan_pairs(p, sms, info->pair_clusters, &grid);
+    else plan_schedule(p, sms, false, &grid);
     return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
 }
 
@@ -966,7 +986,7 @@ int reax_bf16_partials(const void* x, const void* w, const int32_t* split, void*
     p.ws_counters = ws.counters;
     p.status = ws.status;
     int grid = 0;
-    plan_schedule(p, stream_sms(stream, info->sms), false, &grid);
+    plan_schedule(p, stream_sms(stream, info->sms, M), false, &grid);
     return launch_tc(reax::kEpiPlain, p, grid, s);
 }
 
@@ -1035,7 +1055,9 @@ int sliced_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const voi
     p.status = ws.status;
     p.early_b = early_b;
     int grid = 0;
-    plan_schedule(p, stream_sms(stream, info->sms), false, &grid);
+    // Fewer tiles than SMs (decode): split them by K over the SMs (int32 partials, exact).  Tiles with
+    // BF16 columns are never split: their float32 association must stay the reference's.
+    plan_schedule(p, stream_sms(stream, info->sms, M), HP == 0 && kSplitPlainTiles, &grid);
     return launch_tc(reax::kEpiPlain, p, grid, static_cast<cudaStream_t>(stream));
 }
 
@@ -1080,7 +1102,7 @@ int reax_gate_up_i8_noalloc(const int8_t* A, const int8_t* W, const void* AH, co
     if ((rc = noalloc_scratch(dev, &scratch)) != REAX_OK) return rc;
     reax::TcParams p;
     bool split_ok = false;
-    const int sms = stream_sms(stream, info->sms);
+    const int sms = stream_sms(stream, info->sms, M);
     if ((rc = fill_gate_up_params(p, sms, info->pair_clusters > 0, A, W, AH, WH, sa, sw, bias, out, M, N2, KL, KH, ldo, &split_ok)) != REAX_OK)
         return rc;
     // Whole-tile plans need no partials; a plan that splits tiles is re-planned for at most

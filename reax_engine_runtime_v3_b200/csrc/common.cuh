@@ -246,6 +246,14 @@ REAX_DEVI void umma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, u
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+REAX_DEVI void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 // Arrive once on the mbarrier at the offset of `bar` in both CTAs of the pair when every tcgen05
 // operation this thread issued before it has completed.
 REAX_DEVI void umma_commit_pair(uint64_t* bar) {

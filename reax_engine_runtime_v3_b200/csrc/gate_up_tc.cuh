@@ -421,7 +421,7 @@ REAX_DEVI void add_partials(const int4* const (&contrib)[kMaxContrib], int n, in
 template <int EPI_WARPS, int STAGES, int EPI, int MODE, bool ADD_F, bool SWAP, bool PAIR = false>
 __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     static_assert(!SWAP || (EPI == kEpiSwiglu && !ADD_F), "weight-major tiles: SwiGLU without BF16 columns");
-    static_assert(!PAIR || (EPI == kEpiSwiglu && MODE == 0 && !ADD_F && !SWAP), "CTA pairs: INT8 SwiGLU tiles");
+    static_assert(!PAIR || (EPI == kEpiSwiglu && !ADD_F && !SWAP), "CTA pairs: INT8 or BF16 SwiGLU tiles");
     // the CTA's rank in its pair (0 issues the MMAs) and the pair's per-stage box bytes
     const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
     constexpr int kPairBox = kBM * kRowBytes;   // 128 rows x 128 bytes: a CTA's A box and its half of B
@@ -545,9 +545,11 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             auto load_box = [&](int st, int kb, int part, int m0, int b0, int b1) {
                 uint8_t* dst = role == 0 ? box_b(st) : (role == 1 ? box_bu(st) : box_a(st));
                 const int y = role == 0 ? ((PAIR && rank == 1) ? b1 : b0) : (role == 1 ? b1 : m0);
-                if constexpr (PAIR) {
-                    const int x = kb * kRowBytes;
-                    tma_load_2d_pair(dst, role == 2 ? &p.tm_a : &p.tm_b, cluster_map(&full[st], 0), x, y, policy);
+                if constexpr (PAIR) {   // INT8 (128 codes) or BF16 (64 values) per K block
+                    const bool i8 = kb < p.kb_int;
+                    const int x = i8 ? kb * kRowBytes : (kb - p.kb_int) * (kRowBytes / 2);
+                    const CUtensorMap* map = role == 2 ? (i8 ? &p.tm_a : &p.tm_ah) : (i8 ? &p.tm_b : &p.tm_bh);
+                    tma_load_2d_pair(dst, map, cluster_map(&full[st], 0), x, y, policy);
                 } else if (kb < p.kb_int) {
                     const int x = (part * p.kb_int_part + kb) * kRowBytes;
                     tma_load_2d(dst, role == 2 ? &p.tm_a : &p.tm_b, &full[st], x, y, policy);
@@ -630,7 +632,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             // token-major SwiGLU tiles: N = the gate rows and the up rows of the tile (2 x tile_rows8)
             const int n_mma = SWAP ? p.n_tok : (EPI == kEpiSwiglu ? 2 * p.tile_rows8 : kBN);
             const uint32_t idesc_i8 = idesc_i8_s32(PAIR ? 2 * kBM : kBM, n_mma);
-            const uint32_t idesc_f16 = idesc_bf16_f32(kBM, n_mma);
+            const uint32_t idesc_f16 = idesc_bf16_f32(PAIR ? 2 * kBM : kBM, n_mma);
             int stage = 0;
             uint32_t phase = 0;
             int buf = 0;
@@ -700,7 +702,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                                 umma_f16(d_f32, bd + 2 * k, ad + 2 * k, idesc_f16, acc);
                                 umma_f16(d_f32 + p.n_tok, bd_up + 2 * k, ad + 2 * k, idesc_f16, acc);
                             } else {
-                                umma_f16(d_f32, ad + 2 * k, bd + 2 * k, idesc_f16, acc);
+                                if constexpr (PAIR) umma_f16_pair(d_f32, ad + 2 * k, bd + 2 * k, idesc_f16, acc);
+                                else umma_f16(d_f32, ad + 2 * k, bd + 2 * k, idesc_f16, acc);
                             }
                         }
                     }

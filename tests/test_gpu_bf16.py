@@ -46,8 +46,10 @@ def gpu_table():
 
 
 @pytest.mark.parametrize("M,K,H2", [(1, 1024, 512), (64, 4096, 2048), (8, 512, 10240), (128, 4096, 14336),
-                                    (333, 1024, 4096)])
+                                    (333, 1024, 4096), (600, 1024, 1024), (1024, 2048, 384)])
 def test_gate_up_bf16_unsplit(M, K, H2):
+    """The fused BF16 gate/up (CTA-pair tiles from 512 rows) against the unfused partials of the same
+    GPU: the SwiGLU of those partials bit for bit, and each partial within the float32 dot-product bound."""
     from reax_engine_runtime_v3_b200.runtime.mixed_origin_bf16 import Native
     g = H.gen(M + K)
     x = H.activations(g, M, K, "student")
