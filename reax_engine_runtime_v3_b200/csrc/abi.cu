@@ -241,6 +241,25 @@ int make_map(CUtensorMap* map, CUtensorMapDataType dt, size_t elem, const void* 
     return REAX_OK;
 }
 
+// Map of a bf16 output [rows, cols] with row stride ld (elements) for TMA stores of 32 x 32 boxes with the
+// 64-byte swizzle (the epilogue's shared-memory layout).
+int make_out_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int rc = get_encoder(&enc);
+    if (rc != REAX_OK) return rc;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(REAX_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for the [%llu, %llu] output", static_cast<int>(r),
+                    static_cast<unsigned long long>(rows), static_cast<unsigned long long>(cols));
+    return REAX_OK;
+}
+
 // ------------------------------------------------------------------------------------------------- workspace
 struct Workspace {
     unsigned* status;
@@ -549,6 +568,13 @@ int fill_gate_up_params(reax::TcParams& p, int sms, bool pair_ok, const int8_t* 
     } else {
         p.tm_ah = p.tm_a;
         p.tm_bh = p.tm_b;
+    }
+    // token-major tiles of 128 gate rows store their output through shared memory with TMA, one box of 32
+    // rows x 32 columns per warp and chunk (16-byte aligned; a box never reaches the next tile's columns).
+    // Balanced tiles of few tokens with BF16 columns keep the per-thread stores.
+    if (!swap && p.tile_rows == 128) {
+        if ((rc = make_out_map(&p.tm_out, out, N2 / 2, M, ldo)) != REAX_OK) return rc;
+        p.out_tma = 1;
     }
     p.sa = sa;
     p.sw = sw;
@@ -905,6 +931,10 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
         return rc;
     p.tm_a = p.tm_ah;
     p.tm_b = p.tm_bh;
+    if (!swap && p.tile_rows == 128) {   // token-major tiles of 128 gate rows: output through TMA stores
+        if ((rc = make_out_map(&p.tm_out, out, N2 / 2, M, ldo)) != REAX_OK) return rc;
+        p.out_tma = 1;
+    }
     p.out = static_cast<__nv_bfloat16*>(out);
     p.M = M;
     p.H = N2 / 2;

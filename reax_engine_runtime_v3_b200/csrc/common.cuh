@@ -109,6 +109,20 @@ REAX_DEVI void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
         : "memory");
 }
+// 2-D tiled store of one box from this CTA's shared memory to global memory (coordinates x, y >= 0; the
+// tensor map clips the box at the tensor's bounds), in the thread's bulk async-group.
+REAX_DEVI void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+                 : "memory");
+}
+REAX_DEVI void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the thread's committed bulk stores have read their shared-memory source (the buffer is free).
+REAX_DEVI void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until the thread's committed bulk stores have completed.
+REAX_DEVI void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // 1-D bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global memory into
 // this CTA's shared memory, completing on `bar`.
 REAX_DEVI void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {

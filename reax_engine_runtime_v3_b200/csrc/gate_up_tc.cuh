@@ -52,6 +52,8 @@ constexpr int kSwapMaxTok = 64;                 // weight-major tiles: at most 6
 // their 16-byte phase in the output row, so rows of 136 halfwords.
 constexpr int kOutStagePitch = kBN / 2 + 8;
 constexpr int kOutStageBytes = kSwapMaxTok * kOutStagePitch * 2;
+// Token-major tiles with TMA stores use the same region: one 32 x 32 bf16 box per epilogue warp.
+constexpr int kOutTmaWarpBytes = 32 * 32 * 2;
 // How long the contributor holding a split tile's last K blocks waits for the others to publish
 // before it publishes itself (a performance choice; both paths give the same result).
 constexpr unsigned long long kFinisherWaitNs = 10000;
@@ -123,6 +125,10 @@ struct TcParams {
     const int* split;
     // CTA pairs (PAIR kernels): tiles are dealt to pairs of CTAs (clusters of two), cta_shift = 1; 0 otherwise
     int cta_shift;
+    // Token-major SwiGLU tiles: store the output through shared memory with TMA (tm_out: the output [M, H]
+    // bf16, boxes of 32 rows x 32 columns, 64-byte swizzle) instead of per-thread global stores.
+    int out_tma;
+    CUtensorMap tm_out;
 };
 
 // The unit that tiles are dealt to (a CTA, or a CTA pair) and how many there are.
@@ -422,6 +428,7 @@ template <int EPI_WARPS, int STAGES, int EPI, int MODE, bool ADD_F, bool SWAP, b
 __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     static_assert(!SWAP || (EPI == kEpiSwiglu && !ADD_F), "weight-major tiles: SwiGLU without BF16 columns");
     static_assert(!PAIR || (EPI == kEpiSwiglu && !ADD_F && !SWAP), "CTA pairs: INT8 or BF16 SwiGLU tiles");
+    static_assert(EPI_WARPS * kOutTmaWarpBytes <= kOutStageBytes, "TMA store boxes fit the staging region");
     // the CTA's rank in its pair (0 issues the MMAs) and the pair's per-stage box bytes
     const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
     constexpr int kPairBox = kBM * kRowBytes;   // 128 rows x 128 bytes: a CTA's A box and its half of B
@@ -486,6 +493,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         tma_prefetch_desc(&p.tm_b);
         tma_prefetch_desc(&p.tm_ah);
         tma_prefetch_desc(&p.tm_bh);
+        if (p.out_tma) tma_prefetch_desc(&p.tm_out);
     }
     if (warp == 1) {
         if constexpr (PAIR) {
@@ -1113,7 +1121,26 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             }
                             dst = p.out + out_part * p.out_part_stride + static_cast<size_t>(grow) * p.ldo + nt * kBN + cc;
                         }
-                        if (row_ok) {
+                        if (EPI == kEpiSwiglu && p.out_tma) {
+                            // The warp's 32 rows x 32 columns through shared memory (64-byte rows, 16-byte chunk
+                            // c of row r at c ^ ((r >> 1) & 3), the tensor map's 64-byte swizzle, so the four
+                            // 16-byte writes of the 32 lanes are free of bank conflicts), then one TMA store;
+                            // rows past M and columns past H are clipped by the tensor map.  The buffer is
+                            // reused once the previous store has read it.
+                            uint8_t* wbuf = out_stage + e * kOutTmaWarpBytes;
+                            if (lane == 0) bulk_wait_read_all();
+                            __syncwarp();
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                *reinterpret_cast<uint4*>(wbuf + lane * 64 + ((i ^ ((lane >> 1) & 3)) * 16)) =
+                                    make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                tma_store_2d(&p.tm_out, wbuf, nt * rows + cc, m0 + q * 32);
+                                bulk_commit_group();
+                            }
+                        } else if (row_ok) {
                             if (EPI != kEpiSwiglu || (rows & 7) == 0) {
                                 // 16-byte pieces: c_end is a multiple of 8, so a piece is wholly in or out
 #pragma unroll
@@ -1149,6 +1176,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         }
     }
 
+    // the epilogue's TMA stores have completed before the grid does
+    if (warp >= kCtlWarps && lane == 0 && p.out_tma) bulk_wait_all();
     tc_fence_before();
     __syncthreads();
     if constexpr (PAIR) cluster_sync_all();
