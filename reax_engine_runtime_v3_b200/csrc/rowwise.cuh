@@ -221,6 +221,71 @@ __global__ void __launch_bounds__(THREADS) quant_rows_kernel(const __nv_bfloat16
     for (int c = threadIdx.x; c < KH; c += blockDim.x) hr[c] = xr[__ldg(high_columns + c)];
 }
 
+// Stages the bank's maps in shared memory (lc_s, sm_s, ce_s when center, hc_s) and says whether this
+// thread's share of the low columns is the identity map (*ident) and of the smoothing all ones (*unit).
+// The low-column map, smoothing and centres (16-byte aligned, checked by the host) are read as 16-byte
+// runs, B runs per thread in flight at once, so a CTA pays about one L2 round trip per B runs a thread
+// stages instead of one per column it stages.
+// issued() runs once, right after the first batch of loads has gone out (the streaming kernel then
+// requests its first rows, so that the maps' loads are not queued behind them).
+template <int B, class Issued>
+REAX_DEVI void stage_maps(const int* __restrict__ low_columns, const float* __restrict__ smoothing,
+                          const float* __restrict__ centers, const int* __restrict__ high_columns, int KL, int KH,
+                          int center, int* lc_s, float* sm_s, float* ce_s, int* hc_s, bool* ident, bool* unit,
+                          Issued issued) {
+    bool id = true, un = true;
+    const int T = static_cast<int>(blockDim.x), t = static_cast<int>(threadIdx.x);
+    const int KL4 = KL / 4;
+    bool first = true;
+    for (int base = 0; base < KL4; base += B * T) {   // whole batches, so that every thread calls issued()
+        int4 a[B];
+        float4 sv[B], cv[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const int i = base + t + b * T;
+            if (i < KL4) {
+                a[b] = __ldg(reinterpret_cast<const int4*>(low_columns) + i);
+                sv[b] = __ldg(reinterpret_cast<const float4*>(smoothing) + i);
+                if (center) cv[b] = __ldg(reinterpret_cast<const float4*>(centers) + i);
+            }
+        }
+        if (first) issued();
+        first = false;
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const int i = base + t + b * T;
+            if (i >= KL4) break;
+            const int c = 4 * i;
+            lc_s[c] = a[b].x; lc_s[c + 1] = a[b].y; lc_s[c + 2] = a[b].z; lc_s[c + 3] = a[b].w;
+            sm_s[c] = sv[b].x; sm_s[c + 1] = sv[b].y; sm_s[c + 2] = sv[b].z; sm_s[c + 3] = sv[b].w;
+            if (center) { ce_s[c] = cv[b].x; ce_s[c + 1] = cv[b].y; ce_s[c + 2] = cv[b].z; ce_s[c + 3] = cv[b].w; }
+            id = id && a[b].x == c && a[b].y == c + 1 && a[b].z == c + 2 && a[b].w == c + 3;
+            un = un && sv[b].x == 1.0f && sv[b].y == 1.0f && sv[b].z == 1.0f && sv[b].w == 1.0f;
+        }
+    }
+    if (first) issued();
+    for (int c = 4 * KL4 + t; c < KL; c += T) {   // the last KL % 4 columns
+        const int src = __ldg(low_columns + c);
+        const float s = __ldg(smoothing + c);
+        lc_s[c] = src;
+        sm_s[c] = s;
+        if (center) ce_s[c] = __ldg(centers + c);
+        id = id && src == c;
+        un = un && s == 1.0f;
+    }
+    for (int base = t; base < KH; base += B * T) {
+        int h[B];
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+            if (base + b * T < KH) h[b] = __ldg(high_columns + base + b * T);
+#pragma unroll
+        for (int b = 0; b < B; ++b)
+            if (base + b * T < KH) hc_s[base + b * T] = h[b];
+    }
+    *ident = id;
+    *unit = un;
+}
+
 // Many rows (prefill): persistent CTAs of `groups` groups of kStreamGroupWarps warps, each group with its
 // own `depth` row buffers in shared memory.  Group g quantizes the CTA's rows g, g + groups, ... (row j of
 // the group is blockIdx.x + (g + groups j) gridDim.x), each loaded whole by a bulk copy (TMA) into the
@@ -247,31 +312,59 @@ REAX_DEVI uint32_t pack4_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t 
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// Codes of four bf16 pairs (the words of a 16-byte run) for scale / inv = rcp_rn(scale), as 8 bytes.
-// Per pair: q = x * inv, rounded by adding and removing 1.5 * 2^23.  quant_rint_div's bound says rint(q)
-// is rint(div_rn(x, scale)) unless q is within 2^-14 of a half-integer; the packed check
-// (q - rint(q))^2 - (1/4 - 2^-14) < 0 is that bound give or take far less than its margin, and q^2 < 16192
-// (|q| < 127.24) keeps the clamp at +-127 a no-op (the sum's low byte is then the code).  A run with any other value (a
-// NaN fails both checks) is coded by quant_rint_div and the clamp, value by value.
+// NaN-propagating maximum of three float32 values (sm_100 three-input max.NaN).
+REAX_DEVI float max3_nan(float a, float b, float c) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// A bf16x2 word whose two magnitudes are max(|a|, |b|) lane-wise (the signs are the XOR of the inputs');
+// a NaN input yields the other input, as fmaxf drops a NaN.
+REAX_DEVI uint32_t bf16x2_max_abs(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.xorsign.abs.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+// Float32 absmax of the bf16 values of a row's 16-byte runs, folded into the bf16x2 word m (its
+// magnitudes): exact, NaN dropped as fmaxf does.  amax_of(m) reads it out.
+REAX_DEVI uint32_t absmax_run(uint32_t m, const uint4 v) {
+    return bf16x2_max_abs(m, bf16x2_max_abs(bf16x2_max_abs(v.x, v.y), bf16x2_max_abs(v.z, v.w)));
+}
+REAX_DEVI float amax_of(uint32_t m) {
+    return fmaxf(__uint_as_float((m & 0x7FFFu) << 16), __uint_as_float(m & 0x7FFF0000u));
+}
+
+// Codes of four bf16 pairs (the words of a 16-byte run) for scale / inv = rcp_rn(scale), as 8 bytes, when
+// every value x of the run has |x| <= the row's absmax (the scale's source).
+// Per pair: s = fma(x, inv, 1.5 * 2^23) holds n = rint(x * inv) (exact product) in its low bits, and
+// e = fma(x, inv, 1.5 * 2^23 - s) = x * inv - n with one rounding.  inv = (1 / scale)(1 + d), |d| <= 2^-24,
+// and |x / scale| <= 127.0001, so x * inv lies within 2^-16 of x / scale, and div_rn(x, scale) within 2^-18
+// of x / scale: unless x * inv is within 2^-15 of a half-integer, rint(div_rn(x, scale)) = n, the
+// reference's code.  The packed check e^2 - (1/4 - 2^-14) < 0 (|e| < 1/2 - 2^-14, give or take far less
+// than the margin) certifies that, and |n| <= 127 (so the clamp at +-127 is a no-op and s's low byte is
+// the code) follows from |x| <= absmax: scale = div_full(max(absmax, 1e-12), 127) within 2 ulp, so
+// |x * inv| <= 127 (1 + 2^-21).  The eight checks meet in one NaN-propagating max: a run with a value at
+// a half-integer, a NaN or an infinite x * inv (a NaN margin) is coded by quant_rint_div and the clamp,
+// value by value.
 REAX_DEVI uint2 quant_codes8_packed(const uint4 v, float scale, float inv) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     const uint64_t inv2 = f2(inv, inv), magic2 = f2(12582912.0f, 12582912.0f);
     const uint64_t lim2 = f2(-(0.25f - 6.103515625e-05f), -(0.25f - 6.103515625e-05f));
-    const uint64_t top2 = f2(-16192.0f, -16192.0f);
     uint32_t r[8];
-    bool ok = true;
+    float t[8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const uint64_t q = mul2_rn(bf16x2_to_f2(w[i]), inv2);
-        const uint64_t s2 = add2_rn(q, magic2);
-        const uint64_t e = sub2_rn(q, sub2_rn(s2, magic2));
-        const uint64_t t = fma2_rn(e, e, lim2);
-        const uint64_t u = fma2_rn(q, q, top2);
-        ok = ok && f2_lo(t) < 0.f && f2_hi(t) < 0.f && f2_lo(u) < 0.f && f2_hi(u) < 0.f;
+        const uint64_t x = bf16x2_to_f2(w[i]);
+        const uint64_t s2 = fma2_rn(x, inv2, magic2);
+        const uint64_t e = fma2_rn(x, inv2, sub2_rn(magic2, s2));
+        const uint64_t m = fma2_rn(e, e, lim2);
+        t[2 * i] = f2_lo(m);
+        t[2 * i + 1] = f2_hi(m);
         r[2 * i] = __float_as_uint(f2_lo(s2));
         r[2 * i + 1] = __float_as_uint(f2_hi(s2));
     }
-    if (!ok) {
+    const float worst = max3_nan(max3_nan(t[0], t[1], t[2]), max3_nan(t[3], t[4], t[5]), max3_nan(t[6], t[7], t[7]));
+    if (!(worst < 0.f)) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float x = __uint_as_float(i % 2 == 0 ? w[i / 2] << 16 : w[i / 2] & 0xFFFF0000u);
@@ -320,21 +413,16 @@ __global__ void __launch_bounds__(32 * kStreamGroupWarps * kStreamMaxGroups, 1) 
         bulk_load(buf_of(j), x + static_cast<size_t>(r) * K, row_bytes, &bars[slot_of(j)]);
     };
     auto group_sync = [&] { named_bar_sync(1 + group, GT); };
-    if (gt == 0)
-        for (int j = 0; j < depth; ++j) fetch(j);
-    // the bank's maps, while the first rows are in flight
-    bool ident = true, unit = true;
-    for (int c = threadIdx.x; c < KL; c += blockDim.x) {
-        const int src = __ldg(low_columns + c);
-        const float sv = __ldg(smoothing + c);
-        lc_s[c] = src;
-        sm_s[c] = sv;
-        if (center) ce_s[c] = __ldg(centers + c);
-        ident = ident && src == c;
-        unit = unit && sv == 1.0f;
-    }
-    for (int c = threadIdx.x; c < KH; c += blockDim.x) hc_s[c] = __ldg(high_columns + c);
-    const bool fast = __syncthreads_and(ident && unit && !center && (KL & 7) == 0) != 0;
+    // the bank's maps: their loads go out first and the first rows are requested right after them (queued
+    // behind the rows' copies, the maps' loads took microseconds to return)
+    bool ident, unit;
+    stage_maps<2>(low_columns, smoothing, centers, high_columns, KL, KH, center, lc_s, sm_s, ce_s, hc_s, &ident, &unit,
+                  [&] {
+                      if (gt == 0)
+                          for (int j = 0; j < depth; ++j) fetch(j);
+                  });
+    const bool aligned_low = (reinterpret_cast<uintptr_t>(low) & 7u) == 0;   // 8-byte code stores
+    const bool fast = __syncthreads_and(ident && unit && !center && (KL & 7) == 0 && aligned_low) != 0;
     unit = __syncthreads_and(unit) != 0;
 
     // One group barrier per row: after it every thread has finished row j - 1 (so its buffer is refilled
@@ -359,15 +447,10 @@ __global__ void __launch_bounds__(32 * kStreamGroupWarps * kStreamMaxGroups, 1) 
             if (fast) {
                 // |x| of bf16 pairs by masking the sign bits; a bf16x2 max keeps the larger (NaN dropped, as
                 // fmaxf does), which is exactly the float32 absmax of the same values
-                __nv_bfloat162 m2 = __floats2bfloat162_rn(0.f, 0.f);
+                uint32_t m = 0u;
 #pragma unroll 4
-                for (int c8 = gt; c8 < KL / 8; c8 += GT) {
-                    const uint4 v = reinterpret_cast<const uint4*>(xb)[c8];
-                    const uint32_t w[4] = {v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu, v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, *reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-                }
-                amax = fmaxf(__low2float(m2), __high2float(m2));
+                for (int c8 = gt; c8 < KL / 8; c8 += GT) m = absmax_run(m, reinterpret_cast<const uint4*>(xb)[c8]);
+                amax = amax_of(m);
             } else {
                 for (int c = gt; c < KL; c += GT) amax = fmaxf(amax, fabsf(value(c)));
             }
