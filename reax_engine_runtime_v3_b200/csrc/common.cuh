@@ -134,6 +134,12 @@ REAX_DEVI void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint6
 // Order this thread's earlier generic-proxy accesses of shared memory before later async-proxy ones
 // (e.g. a bulk copy into a buffer the thread has just read).
 REAX_DEVI void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 16 bytes from global memory (through L2) into this thread's shared memory, asynchronously; the
+// thread's own copies are complete, and visible to it, after cp_async_wait_all().
+REAX_DEVI void cp_async16_cg(void* smem_dst, const void* gsrc) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+REAX_DEVI void cp_async_wait_all() { asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory"); }
 
 REAX_DEVI uint64_t l2_policy_evict_first() {
     uint64_t p;

@@ -856,10 +856,19 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     // The contributor holding the tile's last K blocks waits (bounded) for the others
                     // instead of publishing, and fetches the first one's partial while its own last MMAs
                     // still run.
+                    // A finisher whose split segment is the CTA's last gathers the other partials through the
+                    // pipeline ring, idle once this segment's accumulators are complete: every thread copies
+                    // its share of every contributor's chunks at once (cp.async, no registers held), instead
+                    // of one contributor's chunk per L2 round trip.
+                    Cursor peek = cur;
+                    Segment after;
+                    const bool ring_free = !cursor_next(p, split, peek, after);
+                    const bool ring_gather = ring_free && n_contrib > 0 &&
+                                             NCH * n_contrib * (CH / 2) * 2 * (EPI_WARPS * 32) * 16 <= STAGES * (kAStage + kBStage);
                     bool early = false;
                     if (!whole && seg.k1 == p.kb_int + p.kb_f16) {
                         early = wait_others_counted<EPI_WARPS>(p, seg, st, last_flag, kFinisherWaitNs);
-                        if (early && n_contrib > 0) fetch(contrib[0], 0, qg, qu);
+                        if (early && n_contrib > 0 && !ring_gather) fetch(contrib[0], 0, qg, qu);
                     }
                     if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
                         raise_error(p, abort_flag, kStatusTimeoutAccFull);
@@ -889,9 +898,32 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             }
                         }
                         finish = count_published<EPI_WARPS>(p, seg, st, last_flag);
-                        if (finish && n_contrib > 0) fetch(contrib[0], 0, qg, qu);
+                        if (finish && n_contrib > 0 && !ring_gather) fetch(contrib[0], 0, qg, qu);
                     }
                     if (!finish) return true;
+                    // ring slot of this thread's int4 i (gate h = 0, up h = 1) of contributor ci, chunk c
+                    const int etid = static_cast<int>(threadIdx.x) - kCtlThreads;
+                    auto ring_slot = [&](int c, int ci, int i, int h) -> int4* {
+                        return reinterpret_cast<int4*>(smem) +
+                               ((((c * n_contrib + ci) * (CH / 2) + i) * 2 + h) * (EPI_WARPS * 32) + etid);
+                    };
+                    if (ring_gather) {
+                        fence_proxy_async_smem();   // the ring's last writes were TMA copies
+                        if (col_ok) {
+#pragma unroll
+                            for (int c = 0; c < NCH; ++c) {
+                                if (2 * CH * c >= n_w) break;   // warp-uniform, as in the chunk loop below
+                                for (int ci = 0; ci < n_contrib; ++ci)
+#pragma unroll
+                                    for (int i = 0; i < CH / 2; ++i) {
+                                        const int t = tok_lo + 2 * CH * c + 4 * i;
+                                        cp_async16_cg(ring_slot(c, ci, i, 0), contrib[ci] + (t / 4) * kBM + r_tile);
+                                        cp_async16_cg(ring_slot(c, ci, i, 1), contrib[ci] + ((n_tok + t) / 4) * kBM + r_tile);
+                                    }
+                            }
+                        }
+                        cp_async_wait_all();
+                    }
                     const uint64_t swg2 = f2(swg, swg), swu2 = f2(swu, swu), bg2 = f2(bg, bg), bu2 = f2(bu, bu);
                     uint16_t* ot = reinterpret_cast<uint16_t*>(out_stage);
                     const int ph = n0 & 7;
@@ -901,7 +933,19 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         if (tc >= n_w) break;        // no real token left for this warp (warp-uniform)
                         uint32_t g[2 * CH], u[2 * CH];
                         load_acc(c, g, u);
-                        if (n_contrib > 0) {
+                        if (ring_gather) {
+                            if (col_ok) {
+                                for (int ci = 0; ci < n_contrib; ++ci) {
+                                    int4 pg[CH / 2], pu[CH / 2];
+#pragma unroll
+                                    for (int i = 0; i < CH / 2; ++i) {
+                                        pg[i] = *ring_slot(c, ci, i, 0);
+                                        pu[i] = *ring_slot(c, ci, i, 1);
+                                    }
+                                    add(g, u, pg, pu);
+                                }
+                            }
+                        } else if (n_contrib > 0) {
                             if (c > 0) fetch(contrib[0], c, qg, qu);
                             add(g, u, qg, qu);
                             for (int ci = 1; ci < n_contrib; ++ci) {
