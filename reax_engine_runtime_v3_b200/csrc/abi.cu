@@ -241,6 +241,41 @@ int make_map(CUtensorMap* map, CUtensorMapDataType dt, size_t elem, const void* 
     return REAX_OK;
 }
 
+// Maps of weight-major INT8 tiles with stages of kk K blocks (TcParams::kk): the weights [2H, KL] as
+// [KL / 128 K blocks][2 halves][H rows][128 bytes], box kk x 2 x box_rows x 128 bytes, so that one copy
+// lands, per K block, the tile's box_rows gate rows and then the matching up rows; the activation codes
+// [M, KL] as [K blocks][M rows][128 bytes], box kk x n_tok x 128 bytes.  Rows past H or M read as zeros.
+int make_multi_maps(CUtensorMap* a_map, CUtensorMap* w_map, const void* A, const void* W, uint64_t KL, uint64_t M,
+                    uint64_t H, uint32_t n_tok, uint32_t box_rows, uint32_t kk) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int rc = get_encoder(&enc);
+    if (rc != REAX_OK) return rc;
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    {
+        cuuint64_t dims[4] = {static_cast<cuuint64_t>(reax::kRowBytes), H, 2, KL / reax::kRowBytes};
+        cuuint64_t strides[3] = {KL, H * KL, static_cast<cuuint64_t>(reax::kRowBytes)};
+        cuuint32_t box[4] = {static_cast<cuuint32_t>(reax::kRowBytes), box_rows, 2, kk};
+        CUresult r = enc(w_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(W), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(REAX_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for the [%llu, %llu] weight stages",
+                        static_cast<int>(r), static_cast<unsigned long long>(2 * H), static_cast<unsigned long long>(KL));
+    }
+    {
+        cuuint64_t dims[3] = {static_cast<cuuint64_t>(reax::kRowBytes), M, KL / reax::kRowBytes};
+        cuuint64_t strides[2] = {KL, static_cast<cuuint64_t>(reax::kRowBytes)};
+        cuuint32_t box[3] = {static_cast<cuuint32_t>(reax::kRowBytes), n_tok, kk};
+        CUresult r = enc(a_map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(A), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(REAX_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for the [%llu, %llu] activation stages",
+                        static_cast<int>(r), static_cast<unsigned long long>(M), static_cast<unsigned long long>(KL));
+    }
+    return REAX_OK;
+}
+
 // Map of a bf16 output [rows, cols] with row stride ld (elements) for TMA stores of 32 x 32 boxes with the
 // 64-byte swizzle (the epilogue's shared-memory layout).
 int make_out_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld) {
@@ -318,8 +353,35 @@ void plan_schedule(reax::TcParams& p, int sms, bool allow_split, int* grid) {
 // boxes rounded up to whole 8-row swizzle atoms), as many as fit the kStages x kStageBytes pool (at most
 // kMaxStages).  The M = 128 MMAs read 128 rows from each weight box, so the last stage's up box keeps
 // 16 KiB of the pool behind it.
-void set_swap_pipeline(reax::TcParams& p) {
+// Whole INT8 weight-major tiles of at most kMultiMaxRows gate rows stream kk > 1 K blocks per stage
+// (TcParams::kk) and multiply each K block's [gate | up] rows with one M = 128 MMA: the largest kk in {4, 2}
+// whose stage of kk x [gate | up | activation] rows leaves at least two stages in the pool; 1 otherwise.
+constexpr int kMultiMaxRows = 64;
+constexpr int kFusedMinRows = 24;
+int multi_kk(int r8, int n_tok, int* stage_bytes, int* stages) {
+    const int pool = kStages * reax::kStageBytes;
+    if (r8 > kMultiMaxRows) return 1;
+    for (int kk = 4; kk >= 2; kk /= 2) {
+        const int bytes = ((kk * (2 * r8 + n_tok) * reax::kRowBytes) + 1023) & ~1023;
+        // the M = 128 MMAs read 128 rows from each slab: past the last stage's last slab they read at most
+        // 16 KiB beyond the pool, inside the output staging region that follows it
+        const int n = std::min(reax::kMaxStages, pool / bytes);
+        if (n >= 2) {
+            if (stage_bytes) *stage_bytes = bytes;
+            if (stages) *stages = n;
+            return kk;
+        }
+    }
+    return 1;
+}
+
+void set_swap_pipeline(reax::TcParams& p, bool multi_ok) {
     const int r8 = (p.tile_rows + 7) & ~7;
+    p.kk = multi_ok ? multi_kk(r8, p.n_tok, &p.stage_bytes, &p.stages) : 1;
+    if (p.kk > 1) {
+        p.tile_rows8 = r8;
+        return;
+    }
     const int bytes = (((2 * r8 + p.n_tok) * reax::kRowBytes) + 1023) & ~1023;
     const int pool = kStages * reax::kStageBytes;
     int stages = (pool - r8 * reax::kRowBytes - reax::kBM * reax::kRowBytes) / bytes + 1;
@@ -339,7 +401,7 @@ void set_swap_pipeline(reax::TcParams& p) {
 //   kHbmBytesPerNs, and a split adds the exchange of int32 partials, kSplitNs[s] + kSplitTokNs[s] per
 //   token column of the tile (the finisher gathers s - 1 partials of 2 x 128 x n_tok words).  The
 //   constants are fitted to launches timed on B200 at K = 4096, H = 1792 and 3584, n_tok = 16 .. 64.
-int tile_rows_for(int H, int K_blocks, int n_tok, int sms, bool can_split, bool* split) {
+int tile_rows_for(int H, int K_blocks, int n_tok, int sms, bool can_split, bool multi, bool* split) {
     *split = false;
     const int t128 = (H + 127) / 128;
     if (t128 % sms == 0) return 128;
@@ -347,7 +409,14 @@ int tile_rows_for(int H, int K_blocks, int n_tok, int sms, bool can_split, bool*
         const int waves = (t128 + sms - 1) / sms;
         return (H + waves * sms - 1) / (waves * sms);
     }
+    // A CTA's time per K block, measured on B200: about 470 ns with one-K-block stages, whose eight M = 128
+    // MMAs take about 340 ns and whose three copies as long; whole tiles of up to 64 gate rows with stages of
+    // kk K blocks (multi_kk: two copies per stage, four MMAs per K block) about 230 ns.
     constexpr double kKBlockNs = 470.0, kHbmBytesPerNs = 6400.0;
+    auto kblock_ns = [&](int r, int s) {
+        const bool fused = multi && s == 1 && multi_kk((r + 7) & ~7, n_tok, nullptr, nullptr) > 1;
+        return fused ? 230.0 : kKBlockNs;
+    };
     constexpr double kSplitNs[4] = {0.0, 2860.0, 2930.0, 5920.0};
     constexpr double kSplitTokNs[4] = {0.0, 40.0, 57.0, 136.0};
     const double hbm_ns = 2.0 * H * K_blocks * 128.0 / kHbmBytesPerNs;
@@ -355,11 +424,16 @@ int tile_rows_for(int H, int K_blocks, int n_tok, int sms, bool can_split, bool*
     double best = 1e30;
     for (int i = 0, s = 1; s <= 8; ++i, s *= 2) {
         if (s > 1 && !can_split) break;
-        const int r = (H * s + sms - 1) / sms;
+        int r = (H * s + sms - 1) / sms;
         if (r > 128) break;
+        // whole tiles with kk-block stages cost about the same per CTA from 1 to 64 gate rows, and
+        // launches of tiles below kFusedMinRows rows measured slower on B200 (more, smaller copies): at
+        // least that many rows per tile, on fewer CTAs
+        if (s == 1 && multi && r < kFusedMinRows && multi_kk(kFusedMinRows, n_tok, nullptr, nullptr) > 1)
+            r = std::min(H, kFusedMinRows);
         const int tiles = (H + r - 1) / r;
         const double per_cta = static_cast<double>(tiles) * K_blocks / std::min(sms, tiles * s);
-        const double t = std::max(per_cta * kKBlockNs, hbm_ns) + kSplitNs[i] + kSplitTokNs[i] * n_tok;
+        const double t = std::max(per_cta * kblock_ns(r, s), hbm_ns) + kSplitNs[i] + kSplitTokNs[i] * n_tok;
         if (t < best) {
             best = t;
             best_r = r;
@@ -375,16 +449,16 @@ int tile_rows_for(int H, int K_blocks, int n_tok, int sms, bool can_split, bool*
 // with balanced gate rows and an activation box of round16(M) rows.  Returns whether the tiles are
 // weight-major; *split says whether the plan may split tiles by K.
 bool plan_gate_up_tiles(reax::TcParams& p, int M, int H, int K_blocks, bool weight_major_ok, bool can_split, int sms,
-                        bool* split) {
+                        bool multi_ok, bool* split) {
     const bool few = M <= kSwapMaxRows;
     const bool swap = weight_major_ok && few;
     p.n_tok = swap ? ((M + 15) / 16) * 16 : 0;
     *split = can_split;
     p.tile_rows = 128;
-    if (few) p.tile_rows = tile_rows_for(H, K_blocks, ((M + 15) / 16) * 16, sms, can_split, split);
+    if (few) p.tile_rows = tile_rows_for(H, K_blocks, ((M + 15) / 16) * 16, sms, can_split, swap && multi_ok, split);
     p.tile_rows8 = (p.tile_rows + 7) & ~7;
     p.a_rows = M < reax::kBM ? ((M + 15) / 16) * 16 : reax::kBM;
-    if (swap) set_swap_pipeline(p);
+    if (swap) set_swap_pipeline(p, multi_ok && !*split);   // kk-block stages only for whole tiles
     // out 16-byte aligned and ldo % 8 == 0 (checked by the callers): 128-row weight-major tiles store
     // through shared memory in 16-byte pieces; balanced weight-major tiles store their columns directly
     p.out_vec16 = p.tile_rows == 128 ? 1 : 0;
@@ -396,6 +470,9 @@ int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
     // mixed-origin partials and the BF16-column association are never split).
     if (epi == reax::kEpiPlain && p.sk_iters > 0 && (p.mode != 0 || p.kb_f16 > 0))
         return fail(REAX_ERR_INVALID, "internal: this plain-epilogue plan must not split tiles by K");
+    if (p.kk > 1 && (p.sk_iters > 0 || p.tile_rows8 > kMultiMaxRows || p.n_tok == 0))
+        return fail(REAX_ERR_INVALID, "internal: K-block stages need whole weight-major tiles of at most %d rows",
+                    kMultiMaxRows);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(reax::kCtlThreads + 32 * kEpiWarps, 1, 1);
@@ -428,6 +505,7 @@ void init_params(reax::TcParams& p) {
     p.tile_rows = 128;
     p.tile_rows8 = 128;
     p.a_rows = 128;
+    p.kk = 1;
 }
 
 // Plain launch (no attributes) whose error comes from the launch call itself, so no sticky error
@@ -552,15 +630,19 @@ int fill_gate_up_params(reax::TcParams& p, int sms, bool pair_ok, const int8_t* 
     // many tokens and no BF16 columns: CTA-pair tiles of 256 token rows (whole tiles, dealt to pairs)
     const bool pair = KH == 0 && M >= kPairMinRows && sms >= 2 && pair_ok;
     // few tokens and no BF16 columns: weight-major tiles, the activation box covers n_tok token rows
-    const bool swap = !pair && plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, sms, split_ok);
+    const bool swap = !pair && plan_gate_up_tiles(p, M, N2 / 2, KL / 128 + KH / 64, KH == 0, KH == 0, sms, true, split_ok);
     if (pair) {
         set_pair_tiles(p);
         *split_ok = false;
     }
     int rc;
-    if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
-        return rc;
-    if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, p.tile_rows)) != REAX_OK) return rc;
+    if (swap && p.kk > 1) {
+        if ((rc = make_multi_maps(&p.tm_a, &p.tm_b, A, W, KL, M, N2 / 2, p.n_tok, p.tile_rows8, p.kk)) != REAX_OK) return rc;
+    } else {
+        if ((rc = make_map(&p.tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, KL, M, KL, swap ? p.n_tok : p.a_rows)) != REAX_OK)
+            return rc;
+        if ((rc = make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, KL, N2, KL, p.tile_rows)) != REAX_OK) return rc;
+    }
     if (KH) {
         if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, AH, KH, M, KH, p.a_rows)) != REAX_OK) return rc;
         if ((rc = make_map(&p.tm_bh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, WH, KH, N2, KH, p.tile_rows)) != REAX_OK)
@@ -922,7 +1004,7 @@ int reax_gate_up_bf16(const void* x, const void* w, void* out, int M, int N2, in
     const int sms = stream_sms(stream, info->sms, M);
     // many tokens: CTA-pair tiles of 256 token rows (as the INT8 gate/up), else the single-CTA plans
     const bool pair = M >= kPairMinRows && sms >= 2 && info->pair_clusters > 0;
-    const bool swap = !pair && plan_gate_up_tiles(p, M, N2 / 2, K / 64, true, false, sms, &split_ok);
+    const bool swap = !pair && plan_gate_up_tiles(p, M, N2 / 2, K / 64, true, false, sms, false, &split_ok);
     if (pair) set_pair_tiles(p);
     if ((rc = make_map(&p.tm_ah, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, K, M, K, swap ? p.n_tok : p.a_rows)) != REAX_OK)
         return rc;

@@ -109,6 +109,22 @@ REAX_DEVI void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
         : "memory");
 }
+// 3-D and 4-D tiled loads (x innermost, x = 0 here: the box covers the whole 128-byte innermost extent).
+REAX_DEVI void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
+        : "memory");
+}
+REAX_DEVI void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z, int w,
+                           uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
+        : "memory");
+}
 // 2-D tiled store of one box from this CTA's shared memory to global memory (coordinates x, y >= 0; the
 // tensor map clips the box at the tensor's bounds), in the thread's bulk async-group.
 REAX_DEVI void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {

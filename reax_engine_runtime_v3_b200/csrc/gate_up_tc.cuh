@@ -129,6 +129,13 @@ struct TcParams {
     // bf16, boxes of 32 rows x 32 columns, 64-byte swizzle) instead of per-thread global stores.
     int out_tma;
     CUtensorMap tm_out;
+    // INT8 weight-major tiles: K blocks per pipeline stage.  1: one 2-D box per producer and K block (gate
+    // rows, up rows, activation rows).  kk > 1 (tiles of at most 64 rows): tm_b is a 4-D map of W viewed as
+    // [K blocks][2 halves][H rows][128 bytes] and tm_a a 3-D map of A as [K blocks][M rows][128 bytes], so
+    // one copy brings the gate and up rows of kk K blocks and another their activation rows.  Small decode
+    // tiles are bound by the number of copies a CTA's TMA unit completes (a few hundred ns each, whatever
+    // their size), so fewer, larger copies stream the same rows several times faster.
+    int kk;
 };
 
 // The unit that tiles are dealt to (a CTA, or a CTA pair) and how many there are.
@@ -471,11 +478,13 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
+    // INT8 weight-major tiles with stages of kk > 1 K blocks (p.kk): two producers, one copy each per stage
+    const bool multi = SWAP && MODE == 0 && p.kk > 1;
     if (threadIdx.x == 0) {
         for (int s = 0; s < ns; ++s) {
-            // one arrival per producer: gate, up and activation boxes; for a pair, rank 0's barrier counts
-            // both CTAs' B-half and A boxes
-            mbar_init(&full[s], PAIR ? 4 : 3);
+            // one arrival per producer: gate, up and activation boxes (multi: weight slabs and activation
+            // boxes); for a pair, rank 0's barrier counts both CTAs' B-half and A boxes
+            mbar_init(&full[s], PAIR ? 4 : (multi ? 2 : 3));
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -526,7 +535,71 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 
     if (warp < kCtlWarps) {
     regs_shrink<kCtlRegs>();
-    if (warp == 0 || warp >= 2) {
+    if ((warp == 0 || warp >= 2) && multi) {
+        // ------------------------------------------------------- TMA producers, stages of kk K blocks
+        // Stage layout: kk slabs of [tile_rows8 gate rows | tile_rows8 up rows] (one 4-D copy by warp 0),
+        // then kk activation boxes of n_tok rows (one 3-D copy by warp 3); warp 2 has nothing to load.  A
+        // segment is loaded in stages of kk K blocks from its first; the K blocks of its last stage past the
+        // segment's end are loaded (zeros past K) but never multiplied.
+        if (lane == 0 && warp != 2) {
+            const bool act = warp == 3;
+            const int kk = p.kk;
+            const uint64_t policy = act ? l2_policy_evict_last()
+                                        : (p.evict_first_b ? l2_policy_evict_first() : l2_policy_evict_normal());
+            const uint32_t tx = static_cast<uint32_t>(kk * (act ? p.n_tok : 2 * p.tile_rows8) * kRowBytes);
+            int stage = 0;
+            uint32_t phase = 0, armed = 0, armed_parity = 0;
+            auto load = [&](int st, int kb, int nt) {
+                mbar_arrive_expect_tx(&full[st], tx);
+                uint8_t* base = smem + st * p.stage_bytes;
+                if (act) tma_load_3d(base + kk * 2 * p.tile_rows8 * kRowBytes, &p.tm_a, &full[st], 0, 0, kb, policy);
+                else tma_load_4d(base, &p.tm_b, &full[st], 0, nt * p.tile_rows, 0, kb, policy);
+            };
+            // early_b: the first segment's first weight stages before the dependency wait (as below)
+            int pre = 0;
+            if (!act && p.early_b && !p.slice_mode) {
+                Cursor c0 = cursor_init(p);
+                Segment s0;
+                if (cursor_next(p, 0, c0, s0)) {
+                    int part, mt, nt;
+                    tile_coords(p, s0.tile, part, mt, nt);
+                    pre = min(min(ns, (kEarlyStages + kk - 1) / kk), (s0.k1 - s0.k0 + kk - 1) / kk);
+                    for (int i = 0; i < pre; ++i) load(i, s0.k0 + i * kk, nt);
+                }
+            }
+            const int split = dependency_wait();
+            bool ok = true, first = true;
+            Cursor cur = cursor_init(p);
+            Segment seg;
+            while (ok && cursor_next(p, split, cur, seg)) {
+                int part, mt, nt;
+                tile_coords(p, seg.tile, part, mt, nt);
+                for (int kb = seg.k0, i = 0; kb < seg.k1; kb += kk, ++i) {
+                    if (!(first && i < pre)) {   // a stage requested early owns its fresh slot (see below)
+                        if (!mbar_wait_bounded(&empty[stage], phase ^ 1, p.timeout_ns, vabort)) {
+                            if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutEmpty);
+                            ok = false;
+                            break;
+                        }
+                        load(stage, kb, nt);
+                    }
+                    armed |= 1u << stage;
+                    armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == ns) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                first = false;
+            }
+            for (int s = 0; s < ns; ++s) {   // drain: every copy started has landed before the CTA exits
+                if (armed & (1u << s)) {
+                    if (!mbar_wait_bounded(&full[s], (armed_parity >> s) & 1, p.timeout_ns, nullptr))
+                        atomicOr(p.status, kStatusTimeoutDrain);
+                }
+            }
+        }
+    } else if (warp == 0 || warp >= 2) {
         // ----------------------------------------------------------------------------- TMA producers
         // One box per producer and K block: warp 0 the gate rows (first half of B), warp 2 the up rows
         // (second half of B), warp 3 the activation rows (A).  Each arms the stage's full barrier with
@@ -664,7 +737,38 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 const uint32_t d_int = tmem_base + buf * kBN;
                 const uint32_t d_f32 = (MODE == 1) ? tmem_base + buf * kBN : tmem_base + kBN;
                 const int first_f = max(seg.k0, p.kb_int);
-                for (int kb = seg.k0; kb < seg.k1; ++kb) {
+                if (multi) {
+                    // stages of kk K blocks: per K block j of a stage, its [gate | up] slab against its
+                    // activation box (TMEM lanes [0, tile_rows8) gate rows, [tile_rows8, 2 tile_rows8) up
+                    // rows, columns the tokens); K blocks past the segment's end are skipped
+                    const uint32_t slab = 2u * p.tile_rows8 * kRowBytes;
+                    for (int kb = seg.k0; kb < seg.k1; kb += p.kk) {
+                        if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns, vabort)) {
+                            if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutFull);
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t base = smem_u32(smem + stage * p.stage_bytes);
+                        const int nb = min(p.kk, seg.k1 - kb);
+                        for (int j = 0; j < nb; ++j) {
+                            // one M = 128 MMA covers the slab's gate rows and up rows (2 x tile_rows8 <= 128)
+                            const uint64_t wd = sw128_kmajor_desc(base + j * slab);
+                            const uint64_t ad = sw128_kmajor_desc(base + p.kk * slab + j * p.n_tok * kRowBytes);
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const uint32_t acc = (kb + j > seg.k0 || k > 0) ? 1u : 0u;
+                                umma_i8(d_int, wd + 2 * k, ad + 2 * k, idesc_i8, acc);
+                            }
+                        }
+                        umma_commit(&empty[stage]);
+                        if (++stage == ns) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                }
+                for (int kb = seg.k0; kb < (multi ? seg.k0 : seg.k1); ++kb) {
                     if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns, vabort)) {
                         if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutFull);
                         ok = false;
@@ -801,7 +905,54 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             const uint32_t t_f32 = ((MODE == 1) ? tmem_base + buf * kBN : tmem_base + kBN) + lane_off;
             const uint32_t t_acc = (MODE == 0) ? t_int : t_f32;
 
-            if constexpr (SWAP) {
+            if (SWAP && multi) {
+                // ------------------------ weight-major tile of kk-block stages: one accumulator per lane row
+                // TMEM lane L < tile_rows8 holds gate row n0 + L, lane tile_rows8 + L its up row, columns the
+                // tokens.  Every lane dequantizes its rows' values into a [token][lane] bf16 block in shared
+                // memory; then the threads pair each gate value with its up value, consecutive threads on
+                // consecutive output columns.  The plan never splits these tiles.
+                const int r8 = p.tile_rows8;
+                const int n0 = nt * p.tile_rows;
+                const bool is_up = r_tile >= r8;
+                const int r = is_up ? r_tile - r8 : r_tile;
+                const bool row_ok = r_tile < 2 * r8 && r < p.tile_rows && n0 + r < p.H;
+                const int wrow = (is_up ? p.H : 0) + min(n0 + r, p.H - 1);
+                const uint64_t sw2 = row_ok ? f2(__ldg(p.sw + wrow), __ldg(p.sw + wrow)) : 0ull;
+                const uint64_t b2 = row_ok ? f2(__ldg(p.bias + wrow), __ldg(p.bias + wrow)) : 0ull;
+                const int per_warp = p.n_tok / kSplit;                  // the warps of a lane quarter split the tokens
+                const int tok_lo = (e / 4) * per_warp;
+                uint16_t* xs = reinterpret_cast<uint16_t*>(out_stage);  // [n_tok][kOutStagePitch] bf16 values
+                if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
+                    raise_error(p, abort_flag, kStatusTimeoutAccFull);
+                    break;
+                }
+                tc_fence_after();
+                if (q * 32 < 2 * r8) {   // warp-uniform: this lane quarter holds gate or up rows
+                    for (int t0 = tok_lo; t0 < tok_lo + per_warp && t0 < p.M; t0 += 8) {
+                        uint32_t a[8];
+                        tmem_ld_x8_sync(t_acc + t0, a);
+                        if (row_ok) {
+#pragma unroll
+                            for (int i = 0; i < 8; i += 2) {
+                                const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(stage_sw + t0 + i);
+                                const uint32_t w = bf16x2_rn(dequant2(a[i], a[i + 1], sa2, sw2, b2));
+                                xs[(t0 + i) * kOutStagePitch + r_tile] = static_cast<uint16_t>(w & 0xFFFFu);
+                                xs[(t0 + i + 1) * kOutStagePitch + r_tile] = static_cast<uint16_t>(w >> 16);
+                            }
+                        }
+                    }
+                }
+                named_bar_sync(1, EPI_WARPS * 32);
+                const int nv = min(p.tile_rows, p.H - n0);   // output columns of the tile
+                const int total = p.M * nv;
+                for (int idx = static_cast<int>(threadIdx.x) - kCtlThreads; idx < total; idx += EPI_WARPS * 32) {
+                    const int t = idx / nv, c = idx - t * nv;
+                    const float gv = __uint_as_float(static_cast<uint32_t>(xs[t * kOutStagePitch + c]) << 16);
+                    const float uv = __uint_as_float(static_cast<uint32_t>(xs[t * kOutStagePitch + r8 + c]) << 16);
+                    p.out[static_cast<size_t>(t) * p.ldo + n0 + c] = swiglu_bf16(gv, uv, silu_tab_s);
+                }
+                named_bar_sync(1, EPI_WARPS * 32);   // the staging block is free again
+            } else if constexpr (SWAP) {
                 // ---------------------------------------------- weight-major tile: lanes are weight rows
                 const int n_tok = p.n_tok;
                 const int n0 = nt * p.tile_rows;               // gate row (= output column) of lane 0

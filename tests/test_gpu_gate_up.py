@@ -108,6 +108,26 @@ def test_weight_major_plans(M, K, Hh):
     compare_int8(H.activations(g, M, K), H.int8_bank(g, K, Hh))
 
 
+@pytest.mark.parametrize("M,K,Hh,sms", [(1, 4096, 1792, 74), (64, 4096, 1792, 74), (33, 2432, 1792, 0),
+                                         (8, 640, 3584, 74), (64, 4096, 3584, 0), (16, 16384, 896, 0),
+                                         (40, 2432, 896, 37)])
+def test_multi_kblock_stages(M, K, Hh, sms):
+    """Weight-major tiles of at most 64 gate rows stream several K blocks per pipeline stage (one 4-D copy
+    of the tile's gate and up rows, one 3-D copy of its activation rows): the H shards of an 8- and a
+    4-GPU job on one lane's share of 74 SMs (reax_set_stream_sms) and on the whole GPU, K = 2432 and
+    640 (19 and 5 K blocks, so the last stage reaches past K and reads zeros), a long K over a small H,
+    whose tiles are split by K at boundaries that are not multiples of the stage, and a share of 37 SMs."""
+    from reax_engine_runtime_v3_b200 import _native
+    g = H.gen(5 * M + K + Hh + sms)
+    stream = torch.cuda.current_stream()
+    if sms:
+        _native.set_stream_sms(stream, sms)
+    try:
+        compare_int8(H.activations(g, M, K), H.int8_bank(g, K, Hh))
+    finally:
+        _native.set_stream_sms(stream, 0)
+
+
 @pytest.mark.parametrize("M", [8, 200])
 def test_silu_range_edges(M):
     """Gate values on both sides of every edge of the epilogue's SiLU table: column scales log-uniform
