@@ -466,7 +466,8 @@ def run_down(args, world, rank, local):
     native = Rotation(Sliced(None), None, 128)
 
     lanes, slot_of = deal_lanes(buckets)
-    run_lanes = lane_runner(lanes, dev)
+    side = torch.cuda.Stream(dev)
+    run_lanes = lane_runner(lanes, dev, side)
 
     def bank_of(i, j):
         return banks[(4 * i + slot_of[j]) % copies]
@@ -476,6 +477,8 @@ def run_down(args, world, rank, local):
 
     cap = torch.cuda.Stream(dev)
     cap.wait_stream(torch.cuda.current_stream(dev))
+    # each lane's grouped GEMMs planned for half of the SMs, as in the gate/up step
+    shares = LaneShares([cap, side], dev, args.lane_sms == "half" and len(lanes) > 1)
 
     def graphs_of(fn):
         gs = []
@@ -499,10 +502,11 @@ def run_down(args, world, rank, local):
         return e0.elapsed_time(e1) / n
 
     with torch.cuda.stream(cap):
-        for i in range(args.warmup):
-            step(i)
-        torch.cuda.synchronize()
-        graphs = graphs_of(step)
+        with shares:
+            for i in range(args.warmup):
+                step(i)
+            torch.cuda.synchronize()
+            graphs = graphs_of(step)
         sampler = ClockSampler(local)
         sampler.start()
         ms = timed(graphs, args.steps)
@@ -577,6 +581,9 @@ def run_down(args, world, rank, local):
                 "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs",
                 "traffic": ncu_traffic("down"),
                 "kernel": "grouped INT8 GEMM (tc_gemm_kernel, plain epilogue, one partial per group)",
+                "how": "back-to-back launches on the whole GPU (weight-major tiles of one wave); the two-lane step "
+                       "plans each lane for half of the SMs, where the groups' columns need two waves of those "
+                       "tiles and the token-major tiles run instead",
                 "per_launch_us": {str(M): round(d * 1e6, 2) for M, d in per_gemm},
                 "per_launch_us_plain": {str(M): round(d * 1e6, 2) for M, d in per_gemm_plain},
                 "quantizer_per_launch_us": {str(M): round(d * 1e6, 2) for M, d in per_quant}}
@@ -589,6 +596,8 @@ def run_down(args, world, rank, local):
             "scaling": "strong", "vs_baseline": None, "dtype": "s8",
             "data": "synthetic (seeded N(0,1) activations, uniform int8 rotated weights)",
             "config": {"workload": down_desc(), "tokens_per_step": tokens, "parallelism": "1 GPU",
+                       "lanes": [[buckets[j] for j in ln] for ln in lanes],
+                       "lane_sms": [shares.sms // 2, shares.sms - shares.sms // 2] if shares.streams else "whole GPU",
                        "l2": f"{copies} rotating weight copies, a different copy on consecutive calls"},
             "roofline": roofline, "cpu_baseline": cpu,
             "e2e": {"value": tokens / (ems * 1e-3), "unit": "tokens/s",

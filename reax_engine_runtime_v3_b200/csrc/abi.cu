@@ -66,7 +66,7 @@ std::mutex g_dev_mutex;
 // The kernel variants: (epilogue, mode, BF16 columns added to INT8 accumulators).
 enum Variant : int {
     kSwigluI8 = 0, kSwigluI8F, kSwigluBf16, kPlainI8, kPlainI8F, kPlainBf16, kSwapI8, kSwapBf16, kPairI8, kPairBf16,
-    kVariants
+    kPlainSwapI8, kVariants
 };
 
 // Token rows from which an INT8 gate/up launch without BF16 columns takes CTA-pair tiles (256 token rows x
@@ -95,13 +95,14 @@ void* tc_kernel_ptr(int v) {
             return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 0, false, false, true>);
         case kPairBf16:
             return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 1, false, false, true>);
+        case kPlainSwapI8: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiPlain, 0, false, true>);
         default: return reinterpret_cast<void*>(&tc_gemm_kernel<kEpiWarps, kStages, kEpiSwiglu, 1, false, true>);
     }
 }
 
 int variant_of(int epi, const reax::TcParams& p) {
     if (p.cta_shift == 1) return p.mode == 1 ? kPairBf16 : kPairI8;
-    if (p.n_tok > 0) return p.mode == 1 ? kSwapBf16 : kSwapI8;
+    if (p.n_tok > 0) return p.mode == 1 ? kSwapBf16 : (epi == reax::kEpiPlain ? kPlainSwapI8 : kSwapI8);
     if (epi == reax::kEpiSwiglu) return p.mode == 1 ? kSwigluBf16 : (p.kb_f16 > 0 ? kSwigluI8F : kSwigluI8);
     return p.mode == 1 ? kPlainBf16 : (p.kb_f16 > 0 ? kPlainI8F : kPlainI8);
 }
@@ -276,6 +277,33 @@ int make_multi_maps(CUtensorMap* a_map, CUtensorMap* w_map, const void* A, const
     return REAX_OK;
 }
 
+// Maps of weight-major grouped-projection tiles with stages of kk K blocks: the weights [N, KT] (KT = P * G
+// codes per row) as [KT / 128 K blocks][N rows][128 bytes], box kk x box_rows x 128 bytes, and the activation
+// codes [M, KT] as [K blocks][M rows][128 bytes], box kk x n_tok x 128 bytes.
+int make_plain_multi_maps(CUtensorMap* a_map, CUtensorMap* w_map, const void* A, const void* W, uint64_t KT, uint64_t M,
+                          uint64_t N, uint32_t n_tok, uint32_t box_rows, uint32_t kk) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int rc = get_encoder(&enc);
+    if (rc != REAX_OK) return rc;
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const void* bases[2] = {W, A};
+    const uint64_t rows[2] = {N, M};
+    const uint32_t boxes[2] = {box_rows, n_tok};
+    CUtensorMap* maps[2] = {w_map, a_map};
+    for (int i = 0; i < 2; ++i) {
+        cuuint64_t dims[3] = {static_cast<cuuint64_t>(reax::kRowBytes), rows[i], KT / reax::kRowBytes};
+        cuuint64_t strides[2] = {KT, static_cast<cuuint64_t>(reax::kRowBytes)};
+        cuuint32_t box[3] = {static_cast<cuuint32_t>(reax::kRowBytes), boxes[i], kk};
+        CUresult r = enc(maps[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(bases[i]), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(REAX_ERR_INVALID, "cuTensorMapEncodeTiled failed (%d) for the [%llu, %llu] grouped stages",
+                        static_cast<int>(r), static_cast<unsigned long long>(rows[i]), static_cast<unsigned long long>(KT));
+    }
+    return REAX_OK;
+}
+
 // Map of a bf16 output [rows, cols] with row stride ld (elements) for TMA stores of 32 x 32 boxes with the
 // 64-byte swizzle (the epilogue's shared-memory layout).
 int make_out_map(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld) {
@@ -353,16 +381,16 @@ void plan_schedule(reax::TcParams& p, int sms, bool allow_split, int* grid) {
 // boxes rounded up to whole 8-row swizzle atoms), as many as fit the kStages x kStageBytes pool (at most
 // kMaxStages).  The M = 128 MMAs read 128 rows from each weight box, so the last stage's up box keeps
 // 16 KiB of the pool behind it.
-// Whole INT8 weight-major tiles of at most kMultiMaxRows gate rows stream kk > 1 K blocks per stage
-// (TcParams::kk) and multiply each K block's [gate | up] rows with one M = 128 MMA: the largest kk in {4, 2}
-// whose stage of kk x [gate | up | activation] rows leaves at least two stages in the pool; 1 otherwise.
-constexpr int kMultiMaxRows = 64;
+// Whole INT8 weight-major tiles whose K-block slab (the gate then the up rows of a SwiGLU tile, or a grouped
+// projection tile's rows) has at most 128 rows stream kk > 1 K blocks per stage (TcParams::kk) and multiply
+// each slab with one M = 128 MMA: the largest kk in {4, 2} whose stage of kk x [slab | activation] rows
+// leaves at least two stages in the pool; 1 otherwise.
 constexpr int kFusedMinRows = 24;
-int multi_kk(int r8, int n_tok, int* stage_bytes, int* stages) {
+int multi_kk(int slab_rows, int n_tok, int* stage_bytes, int* stages) {
     const int pool = kStages * reax::kStageBytes;
-    if (r8 > kMultiMaxRows) return 1;
+    if (slab_rows > reax::kBM) return 1;
     for (int kk = 4; kk >= 2; kk /= 2) {
-        const int bytes = ((kk * (2 * r8 + n_tok) * reax::kRowBytes) + 1023) & ~1023;
+        const int bytes = ((kk * (slab_rows + n_tok) * reax::kRowBytes) + 1023) & ~1023;
         // the M = 128 MMAs read 128 rows from each slab: past the last stage's last slab they read at most
         // 16 KiB beyond the pool, inside the output staging region that follows it
         const int n = std::min(reax::kMaxStages, pool / bytes);
@@ -377,7 +405,7 @@ int multi_kk(int r8, int n_tok, int* stage_bytes, int* stages) {
 
 void set_swap_pipeline(reax::TcParams& p, bool multi_ok) {
     const int r8 = (p.tile_rows + 7) & ~7;
-    p.kk = multi_ok ? multi_kk(r8, p.n_tok, &p.stage_bytes, &p.stages) : 1;
+    p.kk = multi_ok ? multi_kk(2 * r8, p.n_tok, &p.stage_bytes, &p.stages) : 1;
     if (p.kk > 1) {
         p.tile_rows8 = r8;
         return;
@@ -414,7 +442,7 @@ int tile_rows_for(int H, int K_blocks, int n_tok, int sms, bool can_split, bool 
     // kk K blocks (multi_kk: two copies per stage, four MMAs per K block) about 230 ns.
     constexpr double kKBlockNs = 470.0, kHbmBytesPerNs = 6400.0;
     auto kblock_ns = [&](int r, int s) {
-        const bool fused = multi && s == 1 && multi_kk((r + 7) & ~7, n_tok, nullptr, nullptr) > 1;
+        const bool fused = multi && s == 1 && multi_kk(2 * ((r + 7) & ~7), n_tok, nullptr, nullptr) > 1;
         return fused ? 230.0 : kKBlockNs;
     };
     constexpr double kSplitNs[4] = {0.0, 2860.0, 2930.0, 5920.0};
@@ -429,7 +457,7 @@ int tile_rows_for(int H, int K_blocks, int n_tok, int sms, bool can_split, bool 
         // whole tiles with kk-block stages cost about the same per CTA from 1 to 64 gate rows, and
         // launches of tiles below kFusedMinRows rows measured slower on B200 (more, smaller copies): at
         // least that many rows per tile, on fewer CTAs
-        if (s == 1 && multi && r < kFusedMinRows && multi_kk(kFusedMinRows, n_tok, nullptr, nullptr) > 1)
+        if (s == 1 && multi && r < kFusedMinRows && multi_kk(2 * kFusedMinRows, n_tok, nullptr, nullptr) > 1)
             r = std::min(H, kFusedMinRows);
         const int tiles = (H + r - 1) / r;
         const double per_cta = static_cast<double>(tiles) * K_blocks / std::min(sms, tiles * s);
@@ -470,9 +498,11 @@ int launch_tc(int epi, const reax::TcParams& p, int grid, cudaStream_t stream) {
     // mixed-origin partials and the BF16-column association are never split).
     if (epi == reax::kEpiPlain && p.sk_iters > 0 && (p.mode != 0 || p.kb_f16 > 0))
         return fail(REAX_ERR_INVALID, "internal: this plain-epilogue plan must not split tiles by K");
-    if (p.kk > 1 && (p.sk_iters > 0 || p.tile_rows8 > kMultiMaxRows || p.n_tok == 0))
-        return fail(REAX_ERR_INVALID, "internal: K-block stages need whole weight-major tiles of at most %d rows",
-                    kMultiMaxRows);
+    if (p.kk > 1 && (p.sk_iters > 0 || (epi == reax::kEpiSwiglu ? 2 : 1) * p.tile_rows8 > reax::kBM || p.n_tok == 0))
+        return fail(REAX_ERR_INVALID, "internal: K-block stages need whole weight-major tiles of at most %d weight rows",
+                    reax::kBM);
+    if (p.n_tok > 0 && epi == reax::kEpiPlain && p.kk < 2)
+        return fail(REAX_ERR_INVALID, "internal: weight-major grouped tiles need K-block stages");
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(reax::kCtlThreads + 32 * kEpiWarps, 1, 1);
@@ -1167,9 +1197,31 @@ int sliced_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const voi
     p.status = ws.status;
     p.early_b = early_b;
     int grid = 0;
-    // Fewer tiles than SMs (decode): split them by K over the SMs (int32 partials, exact).  Tiles with
-    // BF16 columns are never split: their float32 association must stay the reference's.
-    plan_schedule(p, stream_sms(stream, info->sms, M), HP == 0 && kSplitPlainTiles, &grid);
+    const int sms = stream_sms(stream, info->sms, M);
+    if (HP == 0 && M <= kSwapMaxRows && P * N <= reax::kBM * sms) {
+        // Few tokens, and every group's columns fit one wave of tiles of at most 128 columns: weight-major
+        // tiles of R = P * N / SMs (rounded up) output columns of one group, K-block stages, whole tiles.
+        // (With a smaller SM share, two waves of these tiles measured no faster than the token-major tiles,
+        // which leave the other SMs to a concurrent lane.)
+        reax::TcParams q = p;
+        q.n_tok = ((M + 15) / 16) * 16;
+        q.tile_rows = std::min(reax::kBM, std::max(16, (P * N + sms - 1) / sms));
+        q.tile_rows8 = (q.tile_rows + 7) & ~7;
+        q.kk = multi_kk(q.tile_rows8, q.n_tok, &q.stage_bytes, &q.stages);
+        if (q.kk > 1) {
+            if ((rc = make_plain_multi_maps(&q.tm_a, &q.tm_b, A, W, static_cast<uint64_t>(P) * G, M, N, q.n_tok,
+                                            q.tile_rows8, q.kk)) != REAX_OK)
+                return rc;
+            q.H = N;   // output columns per group
+            q.n_tiles = (N + q.tile_rows - 1) / q.tile_rows;
+            q.tiles = P * q.m_tiles * q.n_tiles;
+            plan_schedule(q, sms, false, &grid);
+            return launch_tc(reax::kEpiPlain, q, grid, static_cast<cudaStream_t>(stream));
+        }
+    }
+    // Token-major tiles.  Fewer tiles than SMs (decode) may split them by K over the SMs (int32 partials,
+    // exact); tiles with BF16 columns are never split: their float32 association must stay the reference's.
+    plan_schedule(p, sms, HP == 0 && kSplitPlainTiles, &grid);
     return launch_tc(reax::kEpiPlain, p, grid, static_cast<cudaStream_t>(stream));
 }
 

@@ -433,7 +433,7 @@ REAX_DEVI void add_partials(const int4* const (&contrib)[kMaxContrib], int n, in
 // Per SM this moves two thirds of the operand bytes of a single-CTA 128 x 256 tile for the same MMA work.
 template <int EPI_WARPS, int STAGES, int EPI, int MODE, bool ADD_F, bool SWAP, bool PAIR = false>
 __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
-    static_assert(!SWAP || (EPI == kEpiSwiglu && !ADD_F), "weight-major tiles: SwiGLU without BF16 columns");
+    static_assert(!SWAP || !ADD_F, "weight-major tiles: no BF16 column region");
     static_assert(!PAIR || (EPI == kEpiSwiglu && !ADD_F && !SWAP), "CTA pairs: INT8 or BF16 SwiGLU tiles");
     static_assert(EPI_WARPS * kOutTmaWarpBytes <= kOutStageBytes, "TMA store boxes fit the staging region");
     // the CTA's rank in its pair (0 issues the MMAs) and the pair's per-stage box bytes
@@ -478,8 +478,11 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
-    // INT8 weight-major tiles with stages of kk > 1 K blocks (p.kk): two producers, one copy each per stage
+    // INT8 weight-major tiles with stages of kk > 1 K blocks (p.kk): two producers, one copy each per stage.
+    // A slab is one K block of the tile's weight rows: the gate rows then the up rows (SwiGLU), or the rows
+    // of one output-column range (plain, grouped projections).
     const bool multi = SWAP && MODE == 0 && p.kk > 1;
+    const int slab_rows = (EPI == kEpiSwiglu ? 2 : 1) * p.tile_rows8;
     if (threadIdx.x == 0) {
         for (int s = 0; s < ns; ++s) {
             // one arrival per producer: gate, up and activation boxes (multi: weight slabs and activation
@@ -537,23 +540,27 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
     regs_shrink<kCtlRegs>();
     if ((warp == 0 || warp >= 2) && multi) {
         // ------------------------------------------------------- TMA producers, stages of kk K blocks
-        // Stage layout: kk slabs of [tile_rows8 gate rows | tile_rows8 up rows] (one 4-D copy by warp 0),
-        // then kk activation boxes of n_tok rows (one 3-D copy by warp 3); warp 2 has nothing to load.  A
-        // segment is loaded in stages of kk K blocks from its first; the K blocks of its last stage past the
-        // segment's end are loaded (zeros past K) but never multiplied.
+        // Stage layout: kk slabs of slab_rows weight rows (one copy by warp 0: a 4-D box of the gate and up
+        // rows, or a 3-D box of a grouped projection's rows), then kk activation boxes of n_tok rows (one 3-D
+        // copy by warp 3); warp 2 has nothing to load.  A segment is loaded in stages of kk K blocks from its
+        // first; the K blocks of its last stage past the segment's end are loaded (the next group's, or zeros
+        // past K) but never multiplied.
         if (lane == 0 && warp != 2) {
             const bool act = warp == 3;
             const int kk = p.kk;
             const uint64_t policy = act ? l2_policy_evict_last()
                                         : (p.evict_first_b ? l2_policy_evict_first() : l2_policy_evict_normal());
-            const uint32_t tx = static_cast<uint32_t>(kk * (act ? p.n_tok : 2 * p.tile_rows8) * kRowBytes);
+            const uint32_t tx = static_cast<uint32_t>(kk * (act ? p.n_tok : slab_rows) * kRowBytes);
             int stage = 0;
             uint32_t phase = 0, armed = 0, armed_parity = 0;
-            auto load = [&](int st, int kb, int nt) {
+            // K block kb of group `part` (grouped projections) sits at K block part * kb_int_part + kb
+            auto load = [&](int st, int kb, int part, int nt) {
                 mbar_arrive_expect_tx(&full[st], tx);
                 uint8_t* base = smem + st * p.stage_bytes;
-                if (act) tma_load_3d(base + kk * 2 * p.tile_rows8 * kRowBytes, &p.tm_a, &full[st], 0, 0, kb, policy);
-                else tma_load_4d(base, &p.tm_b, &full[st], 0, nt * p.tile_rows, 0, kb, policy);
+                const int z = part * p.kb_int_part + kb;
+                if (act) tma_load_3d(base + kk * slab_rows * kRowBytes, &p.tm_a, &full[st], 0, 0, z, policy);
+                else if constexpr (EPI == kEpiSwiglu) tma_load_4d(base, &p.tm_b, &full[st], 0, nt * p.tile_rows, 0, z, policy);
+                else tma_load_3d(base, &p.tm_b, &full[st], 0, nt * p.tile_rows, z, policy);
             };
             // early_b: the first segment's first weight stages before the dependency wait (as below)
             int pre = 0;
@@ -564,7 +571,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     int part, mt, nt;
                     tile_coords(p, s0.tile, part, mt, nt);
                     pre = min(min(ns, (kEarlyStages + kk - 1) / kk), (s0.k1 - s0.k0 + kk - 1) / kk);
-                    for (int i = 0; i < pre; ++i) load(i, s0.k0 + i * kk, nt);
+                    for (int i = 0; i < pre; ++i) load(i, s0.k0 + i * kk, part, nt);
                 }
             }
             const int split = dependency_wait();
@@ -581,7 +588,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             ok = false;
                             break;
                         }
-                        load(stage, kb, nt);
+                        load(stage, kb, part, nt);
                     }
                     armed |= 1u << stage;
                     armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
@@ -741,7 +748,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     // stages of kk K blocks: per K block j of a stage, its [gate | up] slab against its
                     // activation box (TMEM lanes [0, tile_rows8) gate rows, [tile_rows8, 2 tile_rows8) up
                     // rows, columns the tokens); K blocks past the segment's end are skipped
-                    const uint32_t slab = 2u * p.tile_rows8 * kRowBytes;
+                    const uint32_t slab = static_cast<uint32_t>(slab_rows) * kRowBytes;
                     for (int kb = seg.k0; kb < seg.k1; kb += p.kk) {
                         if (!mbar_wait_bounded(&full[stage], phase, p.timeout_ns, vabort)) {
                             if (!*vabort) raise_error(p, abort_flag, kStatusTimeoutFull);
@@ -752,7 +759,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                         const uint32_t base = smem_u32(smem + stage * p.stage_bytes);
                         const int nb = min(p.kk, seg.k1 - kb);
                         for (int j = 0; j < nb; ++j) {
-                            // one M = 128 MMA covers the slab's gate rows and up rows (2 x tile_rows8 <= 128)
+                            // one M = 128 MMA covers the slab's rows (slab_rows <= 128)
                             const uint64_t wd = sw128_kmajor_desc(base + j * slab);
                             const uint64_t ad = sw128_kmajor_desc(base + p.kk * slab + j * p.n_tok * kRowBytes);
 #pragma unroll
@@ -885,7 +892,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
         Cursor ahead = cur;
         Segment aseg;
         float4 next_cs = make_float4(0.f, 0.f, 0.f, 0.f);   // (sw gate, sw up, bias gate, bias up)
-        if constexpr (SWAP && MODE == 0) {
+        if constexpr (SWAP && MODE == 0 && EPI == kEpiSwiglu) {
             for (int t = threadIdx.x - kCtlThreads; t < p.n_tok; t += EPI_WARPS * 32)
                 stage_sw[t] = t < p.M ? __ldg(p.sa + t) : 0.f;
             named_bar_sync(1, EPI_WARPS * 32);
@@ -905,7 +912,45 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
             const uint32_t t_f32 = ((MODE == 1) ? tmem_base + buf * kBN : tmem_base + kBN) + lane_off;
             const uint32_t t_acc = (MODE == 0) ? t_int : t_f32;
 
-            if (SWAP && multi) {
+            if (SWAP && multi && EPI == kEpiPlain) {
+                // ------------- weight-major grouped-projection tile of kk-block stages: lanes are output columns
+                // TMEM lane L < tile_rows holds output column n0 + L of group `part`, columns the tokens; each
+                // thread dequantizes its column's values, ((acc * sa) * sw) + bias as for token-major tiles,
+                // and stores them (a warp writes 32 consecutive columns of a token row).
+                const int n0 = nt * p.tile_rows;
+                const int j = n0 + r_tile;
+                const bool col_ok = r_tile < p.tile_rows && j < p.H;   // plain weight-major plans: H = N
+                const int jc = part * p.n_part_stride + min(j, p.H - 1);
+                const uint64_t sw2 = col_ok ? f2(__ldg(p.sw + jc), __ldg(p.sw + jc)) : 0ull;
+                const uint64_t b2 = col_ok ? f2(__ldg(p.bias + jc), __ldg(p.bias + jc)) : 0ull;
+                const float* sa_p = p.sa + part * p.sa_part_stride;
+                __nv_bfloat16* out_p = p.out + out_part * p.out_part_stride;
+                const int per_warp = p.n_tok / kSplit;
+                const int tok_lo = (e / 4) * per_warp;
+                if (!mbar_wait_bounded(&acc_full[buf], acc_phase, p.timeout_ns, nullptr)) {
+                    raise_error(p, abort_flag, kStatusTimeoutAccFull);
+                    break;
+                }
+                tc_fence_after();
+                if (q * 32 < p.tile_rows) {   // warp-uniform: this lane quarter holds output columns
+                    for (int t0 = tok_lo; t0 < tok_lo + per_warp && t0 < p.M; t0 += 8) {
+                        uint32_t a[8];
+                        tmem_ld_x8_sync(t_acc + t0, a);
+                        if (col_ok) {
+#pragma unroll
+                            for (int i = 0; i < 8; i += 2) {
+                                const int t = t0 + i;
+                                const float s0 = t < p.M ? __ldg(sa_p + t) : 0.f;
+                                const float s1 = t + 1 < p.M ? __ldg(sa_p + t + 1) : 0.f;
+                                const uint32_t w = bf16x2_rn(dequant2(a[i], a[i + 1], f2(s0, s1), sw2, b2));
+                                if (t < p.M) out_p[static_cast<size_t>(t) * p.ldo + j] = __ushort_as_bfloat16(w & 0xFFFFu);
+                                if (t + 1 < p.M)
+                                    out_p[static_cast<size_t>(t + 1) * p.ldo + j] = __ushort_as_bfloat16(w >> 16);
+                            }
+                        }
+                    }
+                }
+            } else if (SWAP && multi) {
                 // ------------------------ weight-major tile of kk-block stages: one accumulator per lane row
                 // TMEM lane L < tile_rows8 holds gate row n0 + L, lane tile_rows8 + L its up row, columns the
                 // tokens.  Every lane dequantizes its rows' values into a [token][lane] bf16 block in shared
@@ -952,7 +997,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     p.out[static_cast<size_t>(t) * p.ldo + n0 + c] = swiglu_bf16(gv, uv, silu_tab_s);
                 }
                 named_bar_sync(1, EPI_WARPS * 32);   // the staging block is free again
-            } else if constexpr (SWAP) {
+            } else if constexpr (SWAP && EPI == kEpiSwiglu) {
                 // ---------------------------------------------- weight-major tile: lanes are weight rows
                 const int n_tok = p.n_tok;
                 const int n0 = nt * p.tile_rows;               // gate row (= output column) of lane 0

@@ -113,6 +113,37 @@ def test_sliced_projection(P, G, HP, M, N):
         assert ok.all(), rep
 
 
+@pytest.mark.parametrize("P,G,M,N,sms", [(4, 2304, 64, 2560, 74), (4, 2304, 1, 2560, 37), (3, 640, 33, 1536, 74),
+                                         (1, 4096, 16, 256, 0), (2, 384, 64, 512, 148)])
+def test_sliced_weight_major_tiles(P, G, M, N, sms):
+    """Few tokens: the grouped projection runs weight-major tiles of ceil(P * N / SMs) output columns with
+    stages of several K blocks (the last stage of a group reaches into the next group's K blocks, or
+    past K, which are loaded but not multiplied), on a lane's share of the SMs and on the whole GPU;
+    the partials are the oracle's bit for bit."""
+    from reax_engine_runtime_v3_b200 import _native
+    from reax_engine_runtime_v3_b200.reaxv2.sliced import sliced_i8
+    g = H.gen(11 * M + P * G + N + sms)
+    dev = torch.device("cuda")
+    low = torch.randint(-127, 128, (M, P * G), generator=g, dtype=torch.int32).to(torch.int8)
+    w = torch.randint(-127, 128, (N, P * G), generator=g, dtype=torch.int32).to(torch.int8)
+    sa = 1e-3 + 9e-3 * torch.rand(P, M, generator=g)
+    sw = 1e-3 + 9e-3 * torch.rand(P, N, generator=g)
+    bias = torch.randn(P, N, generator=g) * 0.05
+    stream = torch.cuda.current_stream()
+    if sms:
+        _native.set_stream_sms(stream, sms)
+    try:
+        out = torch.empty(P, M, N, dtype=torch.bfloat16, device=dev)
+        sliced_i8(low.to(dev), w.to(dev), torch.zeros(M, 0, dtype=torch.bfloat16, device=dev),
+                  torch.zeros(N, 0, dtype=torch.bfloat16, device=dev), sa.to(dev), sw.to(dev), bias.to(dev), out, G, 0, P)
+        torch.cuda.synchronize()
+    finally:
+        _native.set_stream_sms(stream, 0)
+    want = ro.sliced_partials(low.numpy(), w.numpy(), np.zeros((M, 0), np.uint16), np.zeros((N, 0), np.uint16),
+                              sa.numpy(), sw.numpy(), bias.numpy(), G, 0, P)
+    assert np.array_equal(H.bits(out), want)
+
+
 @pytest.mark.parametrize("P,G,HP,M,N", [(4, 2304, 0, 1, 2560), (4, 2304, 0, 64, 2560), (2, 512, 64, 130, 768)])
 def test_sliced_static_entry_back_to_back(P, G, HP, M, N):
     """reax_sliced_i8_static launched back to back (each launch streams its weights under the previous
