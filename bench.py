@@ -922,7 +922,8 @@ def main():
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                     "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peak_kind} hbm_gbs"}
     # the committed capture is of the one-GPU launch; a rank of a sharded job moves 1/N of its bytes
-    roofline["traffic"] = ncu_traffic(args.workload) if world == 1 else None
+    # ncu DRAM bytes per launch of this rank's GEMM: the unsharded workload's, or the 8-way shard's
+    roofline["traffic"] = ncu_traffic(args.workload if shard_world == 1 else f"{args.workload}_shard{shard_world}")
     roofline["per_launch_us"] = {str(M): round(d * 1e6, 2) for M, d in per_bucket}
     if per_bucket_plain:
         roofline["per_launch_us_plain"] = {str(M): round(d * 1e6, 2) for M, d in per_bucket_plain}
