@@ -408,6 +408,7 @@ void set_swap_pipeline(reax::TcParams& p, bool multi_ok) {
     p.kk = multi_ok ? multi_kk(2 * r8, p.n_tok, &p.stage_bytes, &p.stages) : 1;
     if (p.kk > 1) {
         p.tile_rows8 = r8;
+        p.m64 = 2 * r8 <= 64 ? 1 : 0;
         return;
     }
     const int bytes = (((2 * r8 + p.n_tok) * reax::kRowBytes) + 1023) & ~1023;

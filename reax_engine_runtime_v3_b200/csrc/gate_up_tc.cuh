@@ -136,6 +136,9 @@ struct TcParams {
     // tiles are bound by the number of copies a CTA's TMA unit completes (a few hundred ns each, whatever
     // their size), so fewer, larger copies stream the same rows several times faster.
     int kk;
+    // SwiGLU tiles with K-block stages whose [gate | up] slab has at most 64 rows: M = 64 MMAs.  Their
+    // accumulator rows 16 q .. 16 q + 15 sit in TMEM lanes 32 q .. 32 q + 15 (lane quarter q).
+    int m64;
 };
 
 // The unit that tiles are dealt to (a CTA, or a CTA pair) and how many there are.
@@ -745,6 +748,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 const uint32_t d_f32 = (MODE == 1) ? tmem_base + buf * kBN : tmem_base + kBN;
                 const int first_f = max(seg.k0, p.kb_int);
                 if (multi) {
+                    const uint32_t idesc_s = p.m64 ? idesc_i8_s32(64, n_mma) : idesc_i8;
                     // stages of kk K blocks: per K block j of a stage, its [gate | up] slab against its
                     // activation box (TMEM lanes [0, tile_rows8) gate rows, [tile_rows8, 2 tile_rows8) up
                     // rows, columns the tokens); K blocks past the segment's end are skipped
@@ -765,7 +769,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
                                 const uint32_t acc = (kb + j > seg.k0 || k > 0) ? 1u : 0u;
-                                umma_i8(d_int, wd + 2 * k, ad + 2 * k, idesc_i8, acc);
+                                umma_i8(d_int, wd + 2 * k, ad + 2 * k, idesc_s, acc);
                             }
                         }
                         umma_commit(&empty[stage]);
@@ -958,9 +962,11 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                 // consecutive output columns.  The plan never splits these tiles.
                 const int r8 = p.tile_rows8;
                 const int n0 = nt * p.tile_rows;
-                const bool is_up = r_tile >= r8;
-                const int r = is_up ? r_tile - r8 : r_tile;
-                const bool row_ok = r_tile < 2 * r8 && r < p.tile_rows && n0 + r < p.H;
+                // this lane's slab row (M = 64 MMAs: 16 rows per lane quarter, in its first 16 lanes)
+                const int sr = p.m64 ? (lane < 16 ? q * 16 + lane : 2 * r8) : r_tile;
+                const bool is_up = sr >= r8;
+                const int r = is_up ? sr - r8 : sr;
+                const bool row_ok = sr < 2 * r8 && r < p.tile_rows && n0 + r < p.H;
                 const int wrow = (is_up ? p.H : 0) + min(n0 + r, p.H - 1);
                 const uint64_t sw2 = row_ok ? f2(__ldg(p.sw + wrow), __ldg(p.sw + wrow)) : 0ull;
                 const uint64_t b2 = row_ok ? f2(__ldg(p.bias + wrow), __ldg(p.bias + wrow)) : 0ull;
@@ -972,7 +978,7 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                     break;
                 }
                 tc_fence_after();
-                if (q * 32 < 2 * r8) {   // warp-uniform: this lane quarter holds gate or up rows
+                if (q * (p.m64 ? 16 : 32) < 2 * r8) {   // warp-uniform: this lane quarter holds gate or up rows
                     for (int t0 = tok_lo; t0 < tok_lo + per_warp && t0 < p.M; t0 += 8) {
                         uint32_t a[8];
                         tmem_ld_x8_sync(t_acc + t0, a);
@@ -981,8 +987,8 @@ __global__ void __launch_bounds__(kCtlThreads + 32 * EPI_WARPS, 1) tc_gemm_kerne
                             for (int i = 0; i < 8; i += 2) {
                                 const uint64_t sa2 = *reinterpret_cast<const uint64_t*>(stage_sw + t0 + i);
                                 const uint32_t w = bf16x2_rn(dequant2(a[i], a[i + 1], sa2, sw2, b2));
-                                xs[(t0 + i) * kOutStagePitch + r_tile] = static_cast<uint16_t>(w & 0xFFFFu);
-                                xs[(t0 + i + 1) * kOutStagePitch + r_tile] = static_cast<uint16_t>(w >> 16);
+                                xs[(t0 + i) * kOutStagePitch + sr] = static_cast<uint16_t>(w & 0xFFFFu);
+                                xs[(t0 + i + 1) * kOutStagePitch + sr] = static_cast<uint16_t>(w >> 16);
                             }
                         }
                     }
