@@ -657,7 +657,7 @@ def prefill_record(banks, dev, cap, steps):
     copies (same K, H and weight distribution): X bf16 [4096, 4096] ~ N(0,1).  Per call of
     gate_up.Native.project (quantize + gate/up), per GEMM launch and per quantizer launch, with the GEMM's
     TOP/s against three denominators."""
-    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native, gate_up_i8, quantize_rows
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native, gate_up_i8, project_quantizer
     _, K, H, _, _, desc = WORKLOADS["cfg3"]
     M = 4096
     gx = torch.Generator().manual_seed(20261201)
@@ -667,11 +667,11 @@ def prefill_record(banks, dev, cap, steps):
     n_rep = max(3, steps // copies)
     with torch.cuda.stream(cap):
         call = graph_time(lambda r: nat.project(x, banks[r % copies], "hybrid8_b128n256_s64n256"), copies, n_rep, cap)
-        low, high, sc = quantize_rows(x, banks[0])
+        low, high, sc = project_quantizer(x, banks[0])
         gemm = graph_time(lambda r: gate_up_i8(low, banks[r % copies].low_weight, high, banks[r % copies].high_weight,
                                                sc, banks[r % copies].scales, banks[r % copies].bias,
                                                static_weights=True), copies, n_rep, cap)
-        quant = graph_time(lambda r: quantize_rows(x, banks[r % copies]), copies, n_rep, cap)
+        quant = graph_time(lambda r: project_quantizer(x, banks[r % copies]), copies, n_rep, cap)
     ops = gemm_ops(M, K, H)
     tops = ops / gemm / 1e12
     live = int_mm_tops()
@@ -692,7 +692,7 @@ def cfg4_record(rank, world, dev, cap, steps):
     U(5e-4, 5e-3).  Per rank: one gate_up.Native.project call (the replicated quantizer + this rank's
     GEMM) and the GEMM alone, CUDA graphs over two weight copies, max over ranks.  tokens_per_s is the
     job's (every rank produces its columns of all 8192 rows at once)."""
-    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native, gate_up_i8, quantize_rows
+    from reax_engine_runtime_v3_b200.reaxv2.gate_up import Native, gate_up_i8, project_quantizer
     xs_cpu, banks, h = make_inputs("cfg4", rank, world, 2)
     _, K, H, _, _, desc = WORKLOADS["cfg4"]
     x = xs_cpu[0].to(dev)
@@ -701,11 +701,11 @@ def cfg4_record(rank, world, dev, cap, steps):
     n_rep = max(2, steps // 4)
     with torch.cuda.stream(cap):
         call = graph_time(lambda r: nat.project(x, banks[r % 2], "hybrid8_b128n256_s64n256"), 2, n_rep, cap)
-        low, high, sc = quantize_rows(x, banks[0])
+        low, high, sc = project_quantizer(x, banks[0])
         gemm = graph_time(lambda r: gate_up_i8(low, banks[r % 2].low_weight, high, banks[r % 2].high_weight, sc,
                                                banks[r % 2].scales, banks[r % 2].bias, static_weights=True), 2, n_rep,
                           cap)
-        quant = graph_time(lambda r: quantize_rows(x, banks[r % 2]), 2, n_rep, cap)
+        quant = graph_time(lambda r: project_quantizer(x, banks[r % 2]), 2, n_rep, cap)
     call, gemm, quant = (max_over_ranks(v, world) for v in (call, gemm, quant))
     del banks, x, low, high, sc
     torch.cuda.empty_cache()

@@ -69,7 +69,11 @@ REAX_API void reax_set_wait_timeout_ns(unsigned long long ns);
 /* ---- a1: per-token dynamic INT8 quantization --------------------------------------------------
  * Replaces reaxv2.quantize._prepare[(M,)] (reaxv2/quantize.py:5-29, launched at reaxv2/gate_up.py:34-36).
  * x bf16 [M, K]; low_columns int32 [KL]; high_columns int32 [KH]; smoothing, centers float32 [KL];
- * center = CENTER flag.  Writes low int8 [M, KL], high bf16 [M, KH], scales float32 [M]. */
+ * center = CENTER flag.  Writes low int8 [M, KL], high bf16 [M, KH], scales float32 [M].
+ * low_columns and smoothing both NULL describe a dense bank: low column c is column c of x and the
+ * smoothing is all ones (KL == K, KH == 0, center == 0, K a multiple of 1024 up to 8192, x 16-byte and
+ * low 8-byte aligned); the same codes and scales come from plain row loads, which suits many rows.  A
+ * caller that knows its bank is dense passes NULL maps; anything else is REAX_ERR_INVALID. */
 REAX_API int reax_quant_rows(const void* x, const int32_t* low_columns, const int32_t* high_columns,
                     const float* smoothing, const float* centers, int8_t* low, void* high, float* scales,
                     int M, int K, int KL, int KH, int center, void* stream);
@@ -145,7 +149,7 @@ REAX_API int reax_gate_up_i8_static(const int8_t* A, const int8_t* W, const void
  * into low int8 [M, KL], high bf16 [M, KH] and scales float32 [M], then reax_gate_up_i8 on them with W,
  * WH, sw and bias (the bank) into out.  Because the GEMM follows this library's quantizer on the
  * stream, it requests its first weight tiles while the quantizer still runs.  Same requirements as the
- * two calls it makes. */
+ * two calls it makes (NULL low_columns and smoothing: a dense bank, as for reax_quant_rows). */
 REAX_API int reax_project_i8(const void* x, const int32_t* low_columns, const int32_t* high_columns,
                              const float* smoothing, const float* centers, int center, const int8_t* W,
                              const void* WH, const float* sw, const float* bias, int8_t* low, void* high,

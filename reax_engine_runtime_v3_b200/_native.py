@@ -96,6 +96,18 @@ def stream_handle(device: torch.device | None = None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_sm_counts: dict[int, int] = {}
+
+
+def sm_count(device: torch.device) -> int:
+    """Multiprocessors of a CUDA device (cached)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    n = _sm_counts.get(index)
+    if n is None:
+        n = _sm_counts[index] = torch.cuda.get_device_properties(index).multi_processor_count
+    return n
+
+
 def require_cuda(*tensors: torch.Tensor) -> None:
     for t in tensors:
         if t is not None and not t.is_cuda:

@@ -743,6 +743,50 @@ int gate_up_i8_launch(const int8_t* A, const int8_t* W, const void* AH, const vo
     return launch_tc(reax::kEpiSwiglu, p, grid, static_cast<cudaStream_t>(stream));
 }
 
+template <int V>
+int launch_dense(const void* x, int8_t* low, float* scales, int M, int K, int sms, cudaStream_t s) {
+    static int per_sm[kMaxDevices] = {};   // resident CTAs per SM, from the occupancy calculator, per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (per_sm[dev] == 0) {
+        int n = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, reax::quant_rows_dense_kernel<kQuantDivision, V>,
+                                                                       reax::kDenseThreads, 0);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor (dense quantizer)");
+        per_sm[dev] = std::max(1, n);
+    }
+    const int grid = std::min(M, sms * per_sm[dev]);
+    return launch_dependent("quant_rows (dense) launch", reax::quant_rows_dense_kernel<kQuantDivision, V>, dim3(grid),
+                            dim3(reax::kDenseThreads), s, static_cast<const __nv_bfloat16*>(x), low, scales, M, K);
+}
+
+// reax_quant_rows for a dense bank (NULL low_columns and smoothing): every column in order, unit smoothing,
+// no centring, no high columns, K a multiple of 1024 up to 8192.
+int quant_rows_dense(const void* x, int8_t* low, float* scales, int M, int K, int KL, int KH, int center,
+                     void* stream) {
+    if (KL != K || KH != 0 || center != 0 || K % 1024 != 0 || K > 8192)
+        return fail(REAX_ERR_INVALID,
+                    "quant_rows: NULL low_columns and smoothing (a dense bank) need KL == K, KH == 0, no centring and "
+                    "K a multiple of 1024 up to 8192 (K=%d KL=%d KH=%d center=%d)", K, KL, KH, center);
+    if (!x || !low || !scales) return fail(REAX_ERR_INVALID, "quant_rows: NULL pointer argument");
+    if (!aligned(x, 16) || !aligned(low, 8))
+        return fail(REAX_ERR_ALIGN, "quant_rows: a dense bank needs x 16-byte and low 8-byte aligned");
+    int dev;
+    DeviceInfo* info;
+    int rc = current_device(&dev, &info);
+    if (rc != REAX_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (K / 1024) {
+        case 1: return launch_dense<1>(x, low, scales, M, K, info->sms, s);
+        case 2: return launch_dense<2>(x, low, scales, M, K, info->sms, s);
+        case 3: return launch_dense<3>(x, low, scales, M, K, info->sms, s);
+        case 4: return launch_dense<4>(x, low, scales, M, K, info->sms, s);
+        case 5: return launch_dense<5>(x, low, scales, M, K, info->sms, s);
+        case 6: return launch_dense<6>(x, low, scales, M, K, info->sms, s);
+        case 7: return launch_dense<7>(x, low, scales, M, K, info->sms, s);
+        default: return launch_dense<8>(x, low, scales, M, K, info->sms, s);
+    }
+}
 }  // namespace
 
 extern "C" {
@@ -767,6 +811,10 @@ int reax_quant_rows(const void* x, const int32_t* low_columns, const int32_t* hi
     if (M < 0 || K < 0 || KL < 0 || KH < 0 || KL + KH > K)
         return fail(REAX_ERR_INVALID, "quant_rows: bad sizes M=%d K=%d KL=%d KH=%d", M, K, KL, KH);
     if (M == 0) return REAX_OK;
+    // NULL low_columns and smoothing with low columns to quantize: a dense bank (low column c is column c,
+    // unit smoothing); with KL == 0 the maps are never read and may be NULL
+    const bool dense = KL > 0 && low_columns == nullptr && smoothing == nullptr;
+    if (dense) return quant_rows_dense(x, low, scales, M, K, KL, KH, center, stream);
     if (!x || !scales || (KL && (!low_columns || !smoothing || !low || (center && !centers))) ||
         (KH && (!high_columns || !high)))
         return fail(REAX_ERR_INVALID, "quant_rows: NULL pointer argument");

@@ -498,6 +498,49 @@ inline size_t quant_stream_smem(int K, int KL, int KH, int center, int nbuf) {
            static_cast<size_t>(KL) * 4 * (center ? 3 : 2) + static_cast<size_t>(KH) * 4;
 }
 
+// Dense banks (the low columns are every column in order, unit smoothing, no centring, no high columns:
+// every BASELINE bank), many rows: persistent CTAs of kDenseThreads threads, one row at a time each, several
+// CTAs per SM.  Each thread holds V 16-byte runs of the row in registers (K = 1024 V columns): the absmax of
+// the bf16 values (bf16x2 magnitudes, NaN dropped as fmaxf does), one redux per warp and the warps' maxima
+// through shared memory, then the codes from the held runs by quant_codes8_packed -- the float32 operations
+// of quant_row, so the same scales and codes.  No shared-memory staging and no bulk copies: the rows' loads
+// are plain 16-byte loads, V per thread in flight at once, and the many resident CTAs keep enough rows in
+// flight to stream HBM.  The host passes NULL maps for such a bank (reax_quant_rows).
+constexpr int kDenseThreads = 128;
+
+template <int DIV, int V>
+__global__ void __launch_bounds__(kDenseThreads) quant_rows_dense_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                        int8_t* __restrict__ low,
+                                                                        float* __restrict__ scales, int M, int K) {
+    __shared__ float red[2][kDenseThreads / 32];
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const int t = static_cast<int>(threadIdx.x), w = t / 32;
+    int j = 0;
+    for (int r = blockIdx.x; r < M; r += gridDim.x, ++j) {
+        const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(r) * K);
+        uint4 v[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[i] = __ldcs(xr + t + i * kDenseThreads);   // read once: streaming
+        uint32_t m = 0u;
+#pragma unroll
+        for (int i = 0; i < V; ++i) m = absmax_run(m, v[i]);
+        const float wmax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax_of(m))));
+        // two slots: row j + 1 writes the other slot while slow threads may still read row j's
+        if ((t & 31) == 0) red[j & 1][w] = wmax;
+        __syncthreads();
+        float amax = red[j & 1][0];
+#pragma unroll
+        for (int i = 1; i < kDenseThreads / 32; ++i) amax = fmaxf(amax, red[j & 1][i]);
+        const float scale = quant_div<DIV>(fmaxf(amax, 1.0e-12f), 127.0f);
+        const float inv = __frcp_rn(scale);
+        if (t == 0) scales[r] = scale;
+        uint2* lr = reinterpret_cast<uint2*>(low + static_cast<size_t>(r) * K);
+#pragma unroll
+        for (int i = 0; i < V; ++i) lr[t + i * kDenseThreads] = quant_codes8_packed(v[i], scale, inv);
+    }
+}
+
 // ---------------------------------------------------------------------------- a2: grouped quantization
 // grid (M, P): row `blockIdx.x`, group `blockIdx.y` (reaxv2/quantize.py:31-52).  Sources of -1 pad a
 // group and quantize as 0; the centre is always subtracted; the codes are not clamped.

@@ -33,6 +33,31 @@ CONFIGS = {
 }
 
 
+# Banks known to be dense: their low columns are every column in order and their smoothing is all ones (every
+# BASELINE bank).  Keyed by the maps' device addresses; checked once per bank, outside stream capture.
+_DENSE: dict = {}
+# rows per SM from which project() takes the dense quantizer (fewer rows keep the decode quantizer, one wide
+# CTA per row, whose latency is shorter)
+_DENSE_MIN_ROWS_PER_SM = 4
+
+
+def _dense_bank(p) -> bool:
+    """Whether the quantizer may treat the bank as dense (reax_quant_rows with NULL maps): no high columns, no
+    centring, low columns 0..K-1 in order and unit smoothing.  The first call per bank compares the maps on
+    the device (one synchronization); under stream capture an unchecked bank counts as not dense."""
+    if len(p.high_columns) or p.centered or len(p.low_columns) != p.width:
+        return False
+    key = (p.low_columns.data_ptr(), p.smoothing.data_ptr(), p.width)
+    hit = _DENSE.get(key)
+    if hit is None:
+        if torch.cuda.is_current_stream_capturing():
+            return False
+        cols = torch.arange(p.width, device=p.low_columns.device, dtype=p.low_columns.dtype)
+        hit = bool(torch.equal(p.low_columns, cols)) and bool((p.smoothing == 1.0).all())
+        _DENSE[key] = hit
+    return hit
+
+
 def _next_pow2(n: int) -> int:
     return 1 << max(0, int(n) - 1).bit_length()
 
@@ -78,6 +103,28 @@ def quantize_rows(x, p):
     return low, high, scales
 
 
+def project_quantizer(x, p):
+    """The quantizer as ``Native.project`` runs it: the dense kernel (NULL maps) for many rows of a dense bank,
+    else ``quantize_rows``.  Returns (low int8, high bf16, scales f32); the same bits either way."""
+    m = len(x)
+    if not _uses_dense(x, p, m):
+        return quantize_rows(x, p)
+    k = p.width
+    low = torch.empty((m, k), device=x.device, dtype=torch.int8)
+    high = torch.empty((m, 0), device=x.device, dtype=torch.bfloat16)
+    scales = torch.empty(m, device=x.device)
+    with torch.cuda.device(x.device):
+        _native.check(_native.load().reax_quant_rows(x.data_ptr(), None, None, None, None, low.data_ptr(), None,
+                                                     scales.data_ptr(), m, k, k, 0, 0, _native.stream_handle(x.device)))
+    return low, high, scales
+
+
+def _uses_dense(x, p, m) -> bool:
+    """Whether project() quantizes these rows with the dense kernel."""
+    return (m > _DENSE_MIN_ROWS_PER_SM * _native.sm_count(x.device) and p.width % 1024 == 0 and p.width <= 8192
+            and _dense_bank(p))
+
+
 class Native(NativeInt8):
     def tile_n(self, name):
         return CONFIGS[name][2]
@@ -108,11 +155,15 @@ class Native(NativeInt8):
         high = torch.empty((m, kh), device=x.device, dtype=torch.bfloat16)
         scales = torch.empty(m, device=x.device)
         out = torch.empty((m, n2 // 2), device=x.device, dtype=torch.bfloat16)
+        # many rows of a dense bank: the maps are passed as NULL, which selects the library's dense quantizer
+        # (same codes and scales; plain 16-byte row loads instead of staged maps and gathers)
+        dense = _uses_dense(x, p, m)
         with torch.cuda.device(x.device):
             ws = _native.workspace(x.device)
             _native.check(_native.load().reax_project_i8(
-                x.data_ptr(), p.low_columns.data_ptr(), _native.ptr(p.high_columns) if kh else None,
-                p.smoothing.data_ptr(), _native.ptr(p.centers), 1 if p.centered else 0, p.low_weight.data_ptr(),
+                x.data_ptr(), None if dense else p.low_columns.data_ptr(), _native.ptr(p.high_columns) if kh else None,
+                None if dense else p.smoothing.data_ptr(), _native.ptr(p.centers), 1 if p.centered else 0,
+                p.low_weight.data_ptr(),
                 _native.ptr(p.high_weight) if kh else None, p.scales.data_ptr(), p.bias.data_ptr(), low.data_ptr(),
                 _native.ptr(high) if kh else None, scales.data_ptr(), out.data_ptr(), m, p.width, kl, kh, n2,
                 out.stride(0), ws.data_ptr(), ws.numel(), _native.stream_handle(x.device)))

@@ -39,6 +39,11 @@ def test_library_rejects_bad_shapes_without_touching_a_device():
     assert rc == 1
     # empty batch: nothing to do
     assert lib.reax_quant_rows(None, None, None, None, None, None, None, None, 0, 16, 16, 0, 0, None) == 0
+    # NULL maps (a dense bank) with centring, or with K not a multiple of 1024: rejected on the host
+    rc = lib.reax_quant_rows(None, None, None, None, None, None, None, None, 4, 1024, 1024, 0, 1, None)
+    assert rc == 1 and b"dense" in lib.reax_last_error()
+    rc = lib.reax_quant_rows(None, None, None, None, None, None, None, None, 4, 1000, 1000, 0, 0, None)
+    assert rc == 1 and b"dense" in lib.reax_last_error()
     with pytest.raises(RuntimeError, match="status 1"):
         _native.check(1)
 

@@ -212,3 +212,56 @@ def test_scale_division_is_tritons_fp32_division_exhaustive():
     assert np.array_equal(scales.view(np.uint32), tri.view(np.uint32))
     ieee = ro.quant_scale(amax.float().numpy())
     print(f"scales differing from IEEE division: {int((ieee != tri).sum())} of {M}")
+
+
+@pytest.mark.parametrize("M,K", [(4096, 4096), (1000, 8192), (700, 3072), (5, 1024), (1500, 2048)])
+def test_dense_quantizer_matches_the_mapped_one(M, K):
+    """A dense bank (low column c is column c, unit smoothing, no centring) may be quantized with NULL
+    maps, which selects the library's dense kernel; its codes and scales are the mapped quantizer's bit
+    for bit, on rows of N(0,1) values, all-zero rows, rows with +-inf or NaN, huge and tiny values and
+    exact half-integer quotients."""
+    from reax_engine_runtime_v3_b200 import _native
+    g = H.gen(41 * M + K)
+    x = torch.randn(M, K, generator=g)
+    x[1] = 0.0
+    if M > 8:
+        x[2, 7] = float("inf")
+        x[3, 11] = float("-inf")
+        x[4, 5] = float("nan")
+        x[5] *= 1e30
+        x[6] *= 1e-30
+        x[7] = torch.arange(K, dtype=torch.float32) % 255 - 127.0 + 0.5
+        x[7, 0] = 127.0
+    xb = x.to(torch.bfloat16).cuda()
+    dev = xb.device
+    lib = _native.load()
+    cols = torch.arange(K, dtype=torch.int32, device=dev)
+    ones = torch.ones(K, device=dev)
+    outs = []
+    for dense in (False, True):
+        low = torch.empty(M, K, dtype=torch.int8, device=dev)
+        scales = torch.empty(M, device=dev)
+        _native.check(lib.reax_quant_rows(xb.data_ptr(), None if dense else cols.data_ptr(), None,
+                                          None if dense else ones.data_ptr(), None, low.data_ptr(), None,
+                                          scales.data_ptr(), M, K, K, 0, 0, _native.stream_handle(dev)))
+        outs.append((low, scales))
+    torch.cuda.synchronize()
+    (lm, sm), (ld, sd) = outs
+    assert torch.equal(lm, ld)
+    assert torch.equal(sm.view(torch.int32), sd.view(torch.int32))
+
+
+def test_project_on_a_dense_bank_takes_the_dense_quantizer_with_the_same_bits():
+    """Native.project on a dense bank with prefill-sized rows (the dense quantizer behind reax_project_i8)
+    gives the bits of the mapped quantizer followed by the GEMM."""
+    from reax_engine_runtime_v3_b200.reaxv2 import gate_up as G
+    g = H.gen(8800)
+    M, K, Hh = 1200, 4096, 1792
+    x = H.activations(g, M, K).cuda()
+    bank = H.bank_to(H.int8_bank(g, K, Hh), "cuda")
+    assert G._dense_bank(bank)
+    out = G.Native(None).project(x, bank, "hybrid8_b128n256_s64n256")
+    low, high, sc = G.quantize_rows(x, bank)
+    two = G.gate_up_i8(low, bank.low_weight, high, bank.high_weight, sc, bank.scales, bank.bias)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), two.view(torch.int16))
