@@ -507,9 +507,13 @@ inline size_t quant_stream_smem(int K, int KL, int KH, int center, int nbuf) {
 // are plain 16-byte loads, V per thread in flight at once, and the many resident CTAs keep enough rows in
 // flight to stream HBM.  The host passes NULL maps for such a bank (reax_quant_rows).
 constexpr int kDenseThreads = 128;
+// CTAs per SM the compiler budgets registers for (more rows in flight per SM), as many as fit without
+// spilling the held runs: 16 for up to two runs per thread, 12 for up to four, 8 beyond
+template <int V>
+constexpr int dense_min_blocks() { return V <= 2 ? 16 : (V <= 4 ? 12 : 8); }
 
 template <int DIV, int V>
-__global__ void __launch_bounds__(kDenseThreads) quant_rows_dense_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(kDenseThreads, dense_min_blocks<V>()) quant_rows_dense_kernel(const __nv_bfloat16* __restrict__ x,
                                                                         int8_t* __restrict__ low,
                                                                         float* __restrict__ scales, int M, int K) {
     __shared__ float red[2][kDenseThreads / 32];
