@@ -76,9 +76,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--measure-int8-peak", action="store_true", help="print torch._int_mm int8 throughput and exit")
-    ap.add_argument("--lane-sms", choices=("whole", "half"), default="half",
-                    help="SMs each of the two lanes' GEMMs are planned for (reax_set_stream_sms): half each "
-                         "(the lanes' grids run side by side) or the whole GPU each")
+    ap.add_argument("--lane-sms", choices=("whole", "half", "weighted"), default="weighted",
+                    help="SMs each of the two lanes' GEMMs are planned for (reax_set_stream_sms): a larger share "
+                         "for the lane holding the largest bucket (weighted), half each, or the whole GPU each")
     ap.add_argument("--emulate-shard", type=int, default=1,
                     help="one GPU runs rank 0's H shard of an N-way job (a diagnostic of per-rank latency)")
     ap.add_argument("--no-side-records", action="store_true",
@@ -249,19 +249,28 @@ def lane_runner(lanes, dev, side=None):
     return run
 
 
-class LaneShares:
-    """With two lanes and ``--lane-sms half``: each lane's GEMMs are planned for half of the SMs
-    (reax_set_stream_sms), so the two lanes' persistent grids run side by side; used around the
-    capture of the step graphs, which keep the plans they were captured with."""
+# Share of the SMs for the first lane (the one holding the largest bucket, whose GEMM has the longest
+# epilogue) under --lane-sms weighted: 78 of 148.  Measured on cfg2 (one B200, 60 steps per point): step
+# 92.6-93.0 us at 74/74, 90.2 us at 77/71, 90.6-90.8 at 80/68, 90.4 at 83/65, 92.7 at 86/62.
+LANE0_SHARE = 0.527
 
-    def __init__(self, streams, dev, enabled):
+
+class LaneShares:
+    """With two lanes: each lane's GEMMs are planned for a share of the SMs (reax_set_stream_sms), so the
+    two lanes' persistent grids run side by side (``--lane-sms weighted``: LANE0_SHARE for the first lane,
+    ``half``: half each); used around the capture of the step graphs, which keep the plans they were
+    captured with."""
+
+    def __init__(self, streams, dev, enabled, weighted=False):
         self.streams = streams if enabled and len(streams) > 1 else []
         self.sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        first = round(self.sms * LANE0_SHARE) if weighted else self.sms // 2
+        self.split = [first, self.sms - first]
 
     def __enter__(self):
         from reax_engine_runtime_v3_b200 import _native
         for i, st in enumerate(self.streams):
-            _native.set_stream_sms(st, self.sms // 2 if i == 0 else self.sms - self.sms // 2)
+            _native.set_stream_sms(st, self.split[0] if i == 0 else self.split[1])
         return self
 
     def __exit__(self, *exc):
@@ -478,7 +487,7 @@ def run_down(args, world, rank, local):
     cap = torch.cuda.Stream(dev)
     cap.wait_stream(torch.cuda.current_stream(dev))
     # each lane's grouped GEMMs planned for half of the SMs, as in the gate/up step
-    shares = LaneShares([cap, side], dev, args.lane_sms == "half" and len(lanes) > 1)
+    shares = LaneShares([cap, side], dev, args.lane_sms != "whole" and len(lanes) > 1, args.lane_sms == "weighted")
 
     def graphs_of(fn):
         gs = []
@@ -597,7 +606,7 @@ def run_down(args, world, rank, local):
             "data": "synthetic (seeded N(0,1) activations, uniform int8 rotated weights)",
             "config": {"workload": down_desc(), "tokens_per_step": tokens, "parallelism": "1 GPU",
                        "lanes": [[buckets[j] for j in ln] for ln in lanes],
-                       "lane_sms": [shares.sms // 2, shares.sms - shares.sms // 2] if shares.streams else "whole GPU",
+                       "lane_sms": shares.split if shares.streams else "whole GPU",
                        "l2": f"{copies} rotating weight copies, a different copy on consecutive calls"},
             "roofline": roofline, "cpu_baseline": cpu,
             "e2e": {"value": tokens / (ems * 1e-3), "unit": "tokens/s",
@@ -811,7 +820,7 @@ def main():
     # inside a graph.
     cap = torch.cuda.Stream(dev)
     cap.wait_stream(torch.cuda.current_stream(dev))
-    shares = LaneShares([cap, side], dev, args.lane_sms == "half" and len(lanes) > 1)
+    shares = LaneShares([cap, side], dev, args.lane_sms != "whole" and len(lanes) > 1, args.lane_sms == "weighted")
     with torch.cuda.stream(cap), shares:
         for i in range(args.warmup):
             step(i)
@@ -1072,7 +1081,7 @@ def main():
                                f"rank 0 of an H-shard x{shard_world}, alone on one GPU (its tokens/s, not the job's)"
                                if shard_world > 1 else "1 GPU"),
                            "lanes": [[buckets[j] for j in ln] for ln in lanes],
-                           "lane_sms": [shares.sms // 2, shares.sms - shares.sms // 2] if shares.streams else "whole GPU",
+                           "lane_sms": shares.split if shares.streams else "whole GPU",
                            "l2": f"{copies} rotating weight copies ({copies * 2 * h * K * (1 if int8 else 2) / 1e6:.0f} MB > 126 MB L2), "
                                  "a different copy on consecutive calls"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
