@@ -622,8 +622,11 @@ def run_down(args, world, rank, local):
 # ------------------------------------------------------------------------------ side records of the cfg2 line
 def graph_time(fn, reps, n_rep, cap):
     """Seconds per call of fn(0), ..., fn(reps - 1) captured back to back in one CUDA graph on stream
-    `cap` and replayed n_rep times (CUDA events on `cap`).  Call with `cap` current."""
-    fn(0)
+    `cap` and replayed n_rep times (CUDA events on `cap`).  Call with `cap` current.  Every call runs
+    once eagerly first, so that anything a call prepares on first use (the dense-bank check of
+    gate_up.Native.project) is done outside the capture."""
+    for r in range(reps):
+        fn(r)
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=cap):
