@@ -383,13 +383,13 @@ void plan_schedule(reax::TcParams& p, int sms, bool allow_split, int* grid) {
 // 16 KiB of the pool behind it.
 // Whole INT8 weight-major tiles whose K-block slab (the gate then the up rows of a SwiGLU tile, or a grouped
 // projection tile's rows) has at most 128 rows stream kk > 1 K blocks per stage (TcParams::kk) and multiply
-// each slab with one M = 128 MMA: the largest kk in {4, 2} whose stage of kk x [slab | activation] rows
+// each slab with one M = 128 MMA: the largest kk in {8, 4, 2} whose stage of kk x [slab | activation] rows
 // leaves at least two stages in the pool; 1 otherwise.
 constexpr int kFusedMinRows = 24;
 int multi_kk(int slab_rows, int n_tok, int* stage_bytes, int* stages) {
     const int pool = kStages * reax::kStageBytes;
     if (slab_rows > reax::kBM) return 1;
-    for (int kk = 4; kk >= 2; kk /= 2) {
+    for (int kk = 8; kk >= 2; kk /= 2) {
         const int bytes = ((kk * (slab_rows + n_tok) * reax::kRowBytes) + 1023) & ~1023;
         // the M = 128 MMAs read 128 rows from each slab: past the last stage's last slab they read at most
         // 16 KiB beyond the pool, inside the output staging region that follows it
